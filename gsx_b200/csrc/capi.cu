@@ -1,0 +1,497 @@
+/*
+ * C ABI of gsx-b200 (include/gsx_b200.h): context and scratch management, and the orchestration
+ * of the render forward/backward pipeline on one stream.
+ *
+ * Forward: preprocess+scan (1 kernel) -> read the instance total (the only host synchronisation)
+ * -> emit keys -> radix sort (histogram + one onesweep kernel per 8-bit digit) -> tile ranges and
+ * bucket scan -> blend+compose.  Backward: blend backward -> preprocess backward.
+ * Scratch grows on demand with cudaMalloc (outside any stream capture) and is never shrunk.
+ */
+#include "../../include/gsx_b200.h"
+#include "gsx_b200_kernels.cuh"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &msg)
+{
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what)
+{
+    return fail(e == cudaErrorMemoryAllocation ? GSX_B200_OUT_OF_MEMORY : GSX_B200_UNKNOWN,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define GSX_CUDA_TRY(expr, what)                      \
+    do {                                              \
+        cudaError_t e__ = (expr);                     \
+        if(e__ != cudaSuccess) return cuda_fail(e__, what); \
+    } while(0)
+
+struct DevBuf {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+
+int ensure(DevBuf &b, size_t bytes, bool zero = false)
+{
+    if(b.bytes >= bytes && b.ptr != nullptr) return 0;
+    if(b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.bytes = 0;
+    size_t grow = bytes + bytes / 4 + 256;
+    cudaError_t e = cudaMalloc(&b.ptr, grow);
+    if(e != cudaSuccess) {
+        (void)cudaGetLastError();
+        b.ptr = nullptr;
+        return fail(GSX_B200_OUT_OF_MEMORY, std::string("cudaMalloc failed: ") + cudaGetErrorString(e));
+    }
+    b.bytes = grow;
+    if(zero) {
+        e = cudaMemset(b.ptr, 0, grow);
+        if(e != cudaSuccess) return cuda_fail(e, "cudaMemset");
+    }
+    return 0;
+}
+
+void release(DevBuf &b)
+{
+    if(b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.bytes = 0;
+}
+
+CameraParams make_camera(const gsx_b200_camera &c)
+{
+    /* gsx-cuda/render.c:870-921: normalised quaternion -> row-major R, camera centre -R^T t */
+    CameraParams p;
+    float qx = c.rot_xyzw[0], qy = c.rot_xyzw[1], qz = c.rot_xyzw[2], qw = c.rot_xyzw[3];
+    const float nsq = qx * qx + qy * qy + qz * qz + qw * qw;
+    if(nsq > 1.0e-20f) {
+        const float inv = 1.0f / sqrtf(nsq);
+        qx *= inv;
+        qy *= inv;
+        qz *= inv;
+        qw *= inv;
+    } else {
+        qx = qy = qz = 0.0f;
+        qw = 1.0f;
+    }
+    float r[9];
+    r[0] = 1.0f - 2.0f * (qy * qy + qz * qz);
+    r[1] = 2.0f * (qx * qy - qw * qz);
+    r[2] = 2.0f * (qx * qz + qw * qy);
+    r[3] = 2.0f * (qx * qy + qw * qz);
+    r[4] = 1.0f - 2.0f * (qx * qx + qz * qz);
+    r[5] = 2.0f * (qy * qz - qw * qx);
+    r[6] = 2.0f * (qx * qz - qw * qy);
+    r[7] = 2.0f * (qy * qz + qw * qx);
+    r[8] = 1.0f - 2.0f * (qx * qx + qy * qy);
+    const float *t = c.transl;
+    const float w[12] = { r[0], r[1], r[2], t[0], r[3], r[4], r[5], t[1], r[6], r[7], r[8], t[2] };
+    memcpy(p.w2c, w, sizeof(w));
+    p.cam_pos[0] = -(r[0] * t[0] + r[3] * t[1] + r[6] * t[2]);
+    p.cam_pos[1] = -(r[1] * t[0] + r[4] * t[1] + r[7] * t[2]);
+    p.cam_pos[2] = -(r[2] * t[0] + r[5] * t[1] + r[8] * t[2]);
+    p.fx = c.fx;
+    p.fy = c.fy;
+    p.cx = c.cx;
+    p.cy = c.cy;
+    p.width_f = (float)c.width;
+    p.height_f = (float)c.height;
+    p.near_plane = c.near_plane;
+    p.far_plane = c.far_plane;
+    p.width = c.width;
+    p.height = c.height;
+    p.grid_w = (c.width + GSX_TILE - 1) / GSX_TILE;
+    p.grid_h = (c.height + GSX_TILE - 1) / GSX_TILE;
+    return p;
+}
+
+} // namespace
+
+struct gsx_b200_context {
+    int device = 0;
+    /* per primitive */
+    DevBuf rec, offsets, lookback, grad_acc;
+    int64_t prim_cap = 0;
+    /* per instance */
+    DevBuf keys, vals, sort_scratch;
+    uint64_t inst_cap = 0;
+    /* per tile / pixel / bucket */
+    DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap;
+    /* small device words: [0] flags, [1] preprocess tile counter, [2..3] pad */
+    DevBuf words;
+    uint32_t *host_words = nullptr; /* pinned: [0] instance total, [1] flags */
+    /* retained forward state */
+    bool has_train = false;
+    gsx_b200_gaussians g{};
+    int sh_degree = 0;
+    CameraParams cam{};
+    uint64_t n_instances = 0;
+    uint64_t bucket_cap = 0;
+    int n_tiles = 0;
+    int keys_in_b = 0;
+};
+
+extern "C" {
+
+const char *gsx_b200_last_error(void) { return g_last_error.c_str(); }
+
+const char *gsx_b200_version(void) { return "gsx-b200 0.1 (sm_100a)"; }
+
+int gsx_b200_context_create(int device, gsx_b200_context **out_ctx)
+{
+    if(out_ctx == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "out_ctx must be non-null");
+    *out_ctx = nullptr;
+    int count = 0;
+    GSX_CUDA_TRY(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if(device < 0 || device >= count) return fail(GSX_B200_OUT_OF_RANGE, "device index out of range");
+    cudaDeviceProp prop;
+    GSX_CUDA_TRY(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if(prop.major < 10) return fail(GSX_B200_NOT_SUPPORTED, "gsx-b200 requires an sm_100 (Blackwell) device");
+    GSX_CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+    gsx_b200_context *ctx = new gsx_b200_context();
+    ctx->device = device;
+    if(int rc = ensure(ctx->words, 64, true)) {
+        delete ctx;
+        return rc;
+    }
+    if(cudaMallocHost(&ctx->host_words, 64) != cudaSuccess) {
+        release(ctx->words);
+        delete ctx;
+        return fail(GSX_B200_OUT_OF_MEMORY, "cudaMallocHost failed");
+    }
+    memset(ctx->host_words, 0, 64);
+    *out_ctx = ctx;
+    return 0;
+}
+
+int gsx_b200_context_destroy(gsx_b200_context *ctx)
+{
+    if(ctx == nullptr) return 0;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->lookback, &ctx->grad_acc, &ctx->keys, &ctx->vals,
+                      &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
+                      &ctx->bucket_tile, &ctx->snap, &ctx->words };
+    for(DevBuf *b : all) release(*b);
+    if(ctx->host_words) cudaFreeHost(ctx->host_words);
+    delete ctx;
+    return 0;
+}
+
+int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int sh_degree,
+                            const gsx_b200_camera *camera, const float background[3], int forward_type, float *out_rgb,
+                            void *stream_)
+{
+    if(ctx == nullptr || g == nullptr || camera == nullptr || out_rgb == nullptr)
+        return fail(GSX_B200_INVALID_ARGUMENT, "ctx, gaussians, camera and out_rgb must be non-null");
+    if(sh_degree < 0 || sh_degree > 3) return fail(GSX_B200_OUT_OF_RANGE, "sh_degree must be in [0, 3]");
+    if(forward_type != GSX_B200_FORWARD_INFERENCE && forward_type != GSX_B200_FORWARD_TRAIN)
+        return fail(GSX_B200_OUT_OF_RANGE, "forward_type must be INFERENCE or TRAIN");
+    if(camera->width <= 0 || camera->height <= 0) return fail(GSX_B200_INVALID_ARGUMENT, "camera size must be positive");
+    if(!(camera->near_plane > 0.0f) || !(camera->far_plane > camera->near_plane))
+        return fail(GSX_B200_INVALID_ARGUMENT, "near_plane must be positive and below far_plane");
+    if(g->count < 0 || g->count > (int64_t)INT32_MAX) return fail(GSX_B200_OUT_OF_RANGE, "gaussian count out of range");
+    if(g->count > 0 && (g->mean3d == nullptr || g->rotation == nullptr || g->logscale == nullptr ||
+                        g->opacity == nullptr || g->sh0 == nullptr))
+        return fail(GSX_B200_INVALID_ARGUMENT, "gaussian field pointers must be non-null");
+    if((sh_degree >= 1 && g->sh1 == nullptr) || (sh_degree >= 2 && g->sh2 == nullptr) || (sh_degree >= 3 && g->sh3 == nullptr))
+        return fail(GSX_B200_INVALID_ARGUMENT, "higher-order SH tensors required by sh_degree are missing");
+    if(((uintptr_t)g->rotation & 15u) != 0) return fail(GSX_B200_INVALID_ARGUMENT, "rotation must be 16-byte aligned");
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t stream = (cudaStream_t)stream_;
+    const CameraParams cam = make_camera(*camera);
+    const int n_tiles = cam.grid_w * cam.grid_h;
+    const int64_t n = g->count;
+    const size_t P = (size_t)camera->width * (size_t)camera->height;
+    const float bg[3] = { background ? background[0] : 0.0f, background ? background[1] : 0.0f,
+                          background ? background[2] : 0.0f };
+    ctx->has_train = false;
+
+    /* per-primitive scratch */
+    const int64_t pblocks = (n + 255) / 256;
+    if(n > ctx->prim_cap) {
+        if(int rc = ensure(ctx->rec, sizeof(PrimRec) * (size_t)n)) return rc;
+        if(int rc = ensure(ctx->grad_acc, sizeof(float4) * 3 * (size_t)n, true)) return rc;
+        ctx->prim_cap = (int64_t)(ctx->rec.bytes / sizeof(PrimRec));
+        if((int64_t)(ctx->grad_acc.bytes / (3 * sizeof(float4))) < ctx->prim_cap)
+            ctx->prim_cap = (int64_t)(ctx->grad_acc.bytes / (3 * sizeof(float4)));
+    }
+    if(int rc = ensure(ctx->offsets, sizeof(uint32_t) * (size_t)(n + 1))) return rc;
+    if(int rc = ensure(ctx->lookback, sizeof(unsigned long long) * (size_t)(pblocks + 1))) return rc;
+    if(int rc = ensure(ctx->ranges, sizeof(uint2) * (size_t)n_tiles)) return rc;
+    if(int rc = ensure(ctx->bucket_offsets, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
+    if(int rc = ensure(ctx->tile_max, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
+    if(int rc = ensure(ctx->pix, sizeof(float4) * P)) return rc;
+    uint32_t *words = (uint32_t *)ctx->words.ptr;
+    uint32_t *offsets = (uint32_t *)ctx->offsets.ptr;
+
+    uint64_t total = 0;
+    if(n > 0) {
+        GSX_CUDA_TRY(cudaMemsetAsync(ctx->lookback.ptr, 0, sizeof(unsigned long long) * (size_t)pblocks, stream), "memset");
+        GSX_CUDA_TRY(cudaMemsetAsync(words + 1, 0, sizeof(uint32_t), stream), "memset");
+        GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2, g->sh3,
+                                           sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, offsets,
+                                           (uint32_t *)ctx->lookback.ptr, words + 1, words, stream),
+                     "preprocess launch");
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, offsets + n, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "D2H");
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 1, words, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "D2H");
+        GSX_CUDA_TRY(cudaStreamSynchronize(stream), "preprocess");
+        if(ctx->host_words[1] & GSX_FLAG_LOOKBACK_TIMEOUT)
+            return fail(GSX_B200_UNKNOWN, "preprocess scan lookback timed out");
+        total = ctx->host_words[0];
+    } else {
+        GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
+    }
+    ctx->n_instances = total;
+    const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
+    if(int rc = ensure(ctx->keys, sizeof(unsigned long long) * 2 * (size_t)(total + 1))) return rc;
+    if(int rc = ensure(ctx->vals, sizeof(uint32_t) * 2 * (size_t)(total + 1))) return rc;
+    if(int rc = ensure(ctx->sort_scratch, gsx_sort_scratch_bytes(total + 1))) return rc;
+    if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
+    if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
+    const uint64_t kcap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
+    unsigned long long *keys_a = (unsigned long long *)ctx->keys.ptr;
+    unsigned long long *keys_b = keys_a + kcap;
+    uint32_t *vals_a = (uint32_t *)ctx->vals.ptr;
+    uint32_t *vals_b = vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t));
+    int in_b = 0;
+    if(total > 0) {
+        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, offsets, cam.grid_w, keys_a, vals_a, total, words,
+                                     stream),
+                     "emit launch");
+        int tile_bits = 0;
+        while((1 << tile_bits) < n_tiles) ++tile_bits;
+        GSX_CUDA_TRY(gsx_launch_sort_pairs(keys_a, vals_a, keys_b, vals_b, total, 0, 32 + tile_bits, ctx->sort_scratch.ptr,
+                                           ctx->sort_scratch.bytes, words, &in_b, stream),
+                     "sort launch");
+    }
+    const unsigned long long *keys = in_b ? keys_b : keys_a;
+    const uint32_t *vals = in_b ? vals_b : vals_a;
+    GSX_CUDA_TRY(gsx_launch_tile_ranges(keys, total, n_tiles, (uint2 *)ctx->ranges.ptr, (uint32_t *)ctx->bucket_offsets.ptr,
+                                        (uint32_t *)ctx->bucket_tile.ptr, bucket_cap, words, stream),
+                 "ranges launch");
+    GSX_CUDA_TRY(gsx_launch_blend_forward(camera->width, camera->height, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
+                                          (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
+                                          out_rgb, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
+                                          (float4 *)ctx->snap.ptr, stream),
+                 "blend launch");
+    ctx->keys_in_b = in_b;
+    ctx->bucket_cap = bucket_cap;
+    ctx->n_tiles = n_tiles;
+    ctx->cam = cam;
+    if(forward_type == GSX_B200_FORWARD_TRAIN) {
+        ctx->has_train = true;
+        ctx->g = *g;
+        ctx->sh_degree = sh_degree;
+    }
+    return 0;
+}
+
+int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const gsx_b200_gaussian_grads *gr,
+                             void *stream_)
+{
+    if(ctx == nullptr || grad_rgb == nullptr || gr == nullptr)
+        return fail(GSX_B200_INVALID_ARGUMENT, "ctx, grad_rgb and grads must be non-null");
+    if(!ctx->has_train) return fail(GSX_B200_INVALID_STATE, "backward requires a retained TRAIN forward on the same context");
+    const int64_t n = ctx->g.count;
+    if(n > 0 && (gr->mean3d == nullptr || gr->rotation == nullptr || gr->logscale == nullptr || gr->opacity == nullptr ||
+                 gr->sh0 == nullptr))
+        return fail(GSX_B200_INVALID_ARGUMENT, "gradient pointers must be non-null");
+    if((ctx->sh_degree >= 1 && gr->sh1 == nullptr) || (ctx->sh_degree >= 2 && gr->sh2 == nullptr) ||
+       (ctx->sh_degree >= 3 && gr->sh3 == nullptr))
+        return fail(GSX_B200_INVALID_ARGUMENT, "higher-order SH gradient tensors required by sh_degree are missing");
+    if(((uintptr_t)gr->rotation & 15u) != 0) return fail(GSX_B200_INVALID_ARGUMENT, "rotation gradient must be 16-byte aligned");
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t stream = (cudaStream_t)stream_;
+    if(n == 0) return 0;
+    const unsigned long long *keys_a = (const unsigned long long *)ctx->keys.ptr;
+    (void)keys_a;
+    const uint32_t *vals_a = (const uint32_t *)ctx->vals.ptr;
+    const uint32_t *vals = ctx->keys_in_b ? vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t)) : vals_a;
+    if(ctx->n_instances > 0) {
+        GSX_CUDA_TRY(gsx_launch_blend_backward(ctx->cam.width, ctx->cam.height, ctx->cam.grid_w, (const uint2 *)ctx->ranges.ptr,
+                                               (const uint32_t *)ctx->bucket_offsets.ptr,
+                                               (const uint32_t *)ctx->bucket_tile.ptr, ctx->bucket_cap, ctx->n_tiles, vals,
+                                               (const PrimRec *)ctx->rec.ptr, (const float4 *)ctx->pix.ptr,
+                                               (const uint32_t *)ctx->tile_max.ptr, (const float4 *)ctx->snap.ptr, grad_rgb,
+                                               (float4 *)ctx->grad_acc.ptr, n, stream),
+                     "blend backward launch");
+    }
+    GSX_CUDA_TRY(gsx_launch_preprocess_backward(ctx->g.mean3d, ctx->g.rotation, ctx->g.logscale, ctx->g.sh1, ctx->g.sh2,
+                                                ctx->g.sh3, ctx->sh_degree, n, ctx->cam, (const uint32_t *)ctx->offsets.ptr,
+                                                (float4 *)ctx->grad_acc.ptr, gr->mean3d, gr->rotation, gr->logscale,
+                                                gr->opacity, gr->sh0, gr->sh1, gr->sh2, gr->sh3, stream),
+                 "preprocess backward launch");
+    return 0;
+}
+
+int gsx_b200_render_stats(gsx_b200_context *ctx, uint64_t *n_visible, uint64_t *n_instances, uint64_t *n_buckets,
+                          void *stream_)
+{
+    if(ctx == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx must be non-null");
+    cudaStream_t stream = (cudaStream_t)stream_;
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    GSX_CUDA_TRY(cudaStreamSynchronize(stream), "sync");
+    if(n_instances) *n_instances = ctx->n_instances;
+    if(n_buckets) {
+        uint32_t b = 0;
+        if(ctx->n_tiles > 0)
+            GSX_CUDA_TRY(cudaMemcpy(&b, (uint32_t *)ctx->bucket_offsets.ptr + ctx->n_tiles - 1, 4, cudaMemcpyDeviceToHost), "D2H");
+        *n_buckets = b;
+    }
+    if(n_visible) {
+        /* visible = primitives with a non-zero tile count (host pass over offsets; debug use) */
+        *n_visible = 0;
+        const int64_t n = ctx->g.count;
+        if(n > 0 && ctx->has_train) {
+            uint32_t *h = new uint32_t[(size_t)n + 1];
+            cudaError_t e = cudaMemcpy(h, ctx->offsets.ptr, sizeof(uint32_t) * (size_t)(n + 1), cudaMemcpyDeviceToHost);
+            if(e != cudaSuccess) {
+                delete[] h;
+                return cuda_fail(e, "D2H");
+            }
+            uint64_t v = 0;
+            for(int64_t i = 0; i < n; ++i) v += h[i + 1] != h[i];
+            delete[] h;
+            *n_visible = v;
+        }
+    }
+    return 0;
+}
+
+int gsx_b200_render_get_view(gsx_b200_context *ctx, gsx_b200_render_view *v)
+{
+    if(ctx == nullptr || v == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx and out_view must be non-null");
+    const uint64_t kcap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
+    const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
+    v->keys = (const uint64_t *)ctx->keys.ptr + (ctx->keys_in_b ? kcap : 0);
+    v->values = (const uint32_t *)ctx->vals.ptr + (ctx->keys_in_b ? vcap : 0);
+    v->ranges = (const uint32_t *)ctx->ranges.ptr;
+    v->offsets = (const uint32_t *)ctx->offsets.ptr;
+    v->tile_max = (const uint32_t *)ctx->tile_max.ptr;
+    v->pixel_state = (const float *)ctx->pix.ptr;
+    v->n_instances = ctx->n_instances;
+    v->n_tiles = ctx->n_tiles;
+    v->grid_width = ctx->cam.grid_w;
+    return 0;
+}
+
+int gsx_b200_context_check(gsx_b200_context *ctx, void *stream_)
+{
+    if(ctx == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx must be non-null");
+    cudaStream_t stream = (cudaStream_t)stream_;
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    uint32_t flags = 0;
+    GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 1, ctx->words.ptr, 4, cudaMemcpyDeviceToHost, stream), "D2H");
+    GSX_CUDA_TRY(cudaStreamSynchronize(stream), "sync");
+    flags = ctx->host_words[1];
+    if(flags != 0) {
+        GSX_CUDA_TRY(cudaMemsetAsync(ctx->words.ptr, 0, 4, stream), "memset");
+        GSX_CUDA_TRY(cudaStreamSynchronize(stream), "sync");
+        std::string m = "device-side failure:";
+        if(flags & GSX_FLAG_LOOKBACK_TIMEOUT) m += " lookback wait timed out;";
+        if(flags & GSX_FLAG_INSTANCE_OVERFLOW) m += " instance capacity overflow;";
+        if(flags & GSX_FLAG_BUCKET_OVERFLOW) m += " bucket capacity overflow;";
+        return fail(GSX_B200_UNKNOWN, m);
+    }
+    return 0;
+}
+
+int gsx_b200_loss_l1_ssim(int mode, const float *prediction, const float *target, float *loss_map, float *grad,
+                          float *loss_sum, int64_t planes, int32_t height, int32_t width, float l1_scale, float ssim_scale,
+                          float l1_grad_scale, float ssim_grad_scale, void *stream)
+{
+    if(prediction == nullptr || target == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "prediction and target must be non-null");
+    if((mode & 1) && loss_map == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "loss_map required by mode");
+    if((mode & 2) && grad == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "grad required by mode");
+    if(mode != 1 && mode != 2 && mode != 3 && mode != 5 && mode != 7)
+        return fail(GSX_B200_OUT_OF_RANGE, "mode must be one of 1, 2, 3, 5, 7");
+    if(planes <= 0 || height <= 0 || width <= 0) return fail(GSX_B200_INVALID_ARGUMENT, "image shape must be positive");
+    if(planes > INT32_MAX) return fail(GSX_B200_OUT_OF_RANGE, "too many planes");
+    GSX_CUDA_TRY(gsx_launch_l1_ssim(mode, prediction, target, loss_map, grad, loss_sum, (int)planes, height, width, l1_scale,
+                                    ssim_scale, l1_grad_scale, ssim_grad_scale, (cudaStream_t)stream),
+                 "l1_ssim launch");
+    return 0;
+}
+
+int gsx_b200_loss_pointwise(int op, const float *prediction, const float *target, float *out, uint64_t n, float scale,
+                            void *stream)
+{
+    if(op < 0 || op > 3) return fail(GSX_B200_OUT_OF_RANGE, "op must be in [0, 3]");
+    if(n > 0 && (prediction == nullptr || target == nullptr || out == nullptr))
+        return fail(GSX_B200_INVALID_ARGUMENT, "pointers must be non-null");
+    GSX_CUDA_TRY(gsx_launch_pointwise_loss(op, prediction, target, out, (size_t)n, scale, (cudaStream_t)stream),
+                 "pointwise loss launch");
+    return 0;
+}
+
+int gsx_b200_adam_step(const gsx_b200_adam_group *groups, int32_t group_count, void *stream)
+{
+    if(group_count < 0 || group_count > 16) return fail(GSX_B200_OUT_OF_RANGE, "group_count must be in [0, 16]");
+    if(group_count > 0 && groups == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "groups must be non-null");
+    AdamTable t;
+    memset(&t, 0, sizeof(t));
+    t.count = group_count;
+    for(int i = 0; i < group_count; ++i) {
+        const gsx_b200_adam_group &g = groups[i];
+        if(g.count > 0 && (g.parameter == nullptr || g.gradient == nullptr || g.first_moment == nullptr || g.second_moment == nullptr))
+            return fail(GSX_B200_INVALID_ARGUMENT, "adam group pointers must be non-null");
+        t.g[i].param = g.parameter;
+        t.g[i].grad = g.gradient;
+        t.g[i].m1 = g.first_moment;
+        t.g[i].m2 = g.second_moment;
+        t.g[i].n = g.count;
+        t.g[i].lr = g.learning_rate;
+        t.g[i].beta1 = g.beta1;
+        t.g[i].beta2 = g.beta2;
+        t.g[i].eps = g.epsilon;
+        t.g[i].weight_decay = g.weight_decay;
+        t.g[i].max_grad = g.max_grad;
+        t.g[i].inv_c1 = g.inv_bias_correction1;
+        t.g[i].inv_c2 = g.inv_bias_correction2;
+    }
+    GSX_CUDA_TRY(gsx_launch_adam(t, (cudaStream_t)stream), "adam launch");
+    return 0;
+}
+
+int gsx_b200_sort_pairs(gsx_b200_context *ctx, uint64_t *keys, uint32_t *values, uint64_t count, int32_t begin_bit,
+                        int32_t end_bit, void *stream_)
+{
+    if(ctx == nullptr || (count > 0 && (keys == nullptr || values == nullptr)))
+        return fail(GSX_B200_INVALID_ARGUMENT, "ctx, keys and values must be non-null");
+    if(begin_bit < 0 || end_bit > 64 || begin_bit > end_bit) return fail(GSX_B200_OUT_OF_RANGE, "bit range must satisfy 0 <= begin <= end <= 64");
+    if(count >= (1ull << 30)) return fail(GSX_B200_OUT_OF_RANGE, "count must be below 2^30");
+    if(count == 0 || begin_bit == end_bit) return 0;
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t stream = (cudaStream_t)stream_;
+    /* alternate buffers come from the context's instance scratch (invalidates a retained forward) */
+    ctx->has_train = false;
+    if(int rc = ensure(ctx->keys, sizeof(unsigned long long) * (size_t)count)) return rc;
+    if(int rc = ensure(ctx->vals, sizeof(uint32_t) * (size_t)count)) return rc;
+    if(int rc = ensure(ctx->sort_scratch, gsx_sort_scratch_bytes(count))) return rc;
+    int in_b = 0;
+    GSX_CUDA_TRY(gsx_launch_sort_pairs((unsigned long long *)keys, values, (unsigned long long *)ctx->keys.ptr,
+                                       (uint32_t *)ctx->vals.ptr, count, begin_bit, end_bit, ctx->sort_scratch.ptr,
+                                       ctx->sort_scratch.bytes, (uint32_t *)ctx->words.ptr, &in_b, stream),
+                 "sort launch");
+    if(in_b) {
+        GSX_CUDA_TRY(cudaMemcpyAsync(keys, ctx->keys.ptr, sizeof(uint64_t) * count, cudaMemcpyDeviceToDevice, stream), "copy");
+        GSX_CUDA_TRY(cudaMemcpyAsync(values, ctx->vals.ptr, sizeof(uint32_t) * count, cudaMemcpyDeviceToDevice, stream), "copy");
+    }
+    return 0;
+}
+
+} /* extern "C" */

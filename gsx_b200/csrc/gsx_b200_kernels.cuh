@@ -1,0 +1,163 @@
+/*
+ * Shared device-side definitions for the gsx-b200 sm_100a kernels.
+ *
+ * HBM layout of the per-frame render state (all owned by a gsx_b200_context):
+ *   per primitive (capacity N):
+ *     rec      PrimRec[N]   48 B: {mean2d.xy, conic.xy} {conic.z, opacity, rgb.rg} {rgb.b, depth, bx, by}
+ *     offsets  u32[N+1]     exclusive prefix of the exact tile-overlap counts (0 = culled)
+ *     grad_acc float4[3N]   per-primitive 2-D gradient accumulators of the blend backward
+ *   per instance (capacity I): keys u64[2I], values u32[2I] (double-buffered radix sort)
+ *   per tile (T):   ranges uint2[T], bucket_offsets u32[T] (inclusive), tile_max u32[T]
+ *   per pixel (P):  pix float4[P] = {composed rgb, n_contrib bits}
+ *   per bucket (B <= I/32 + T): bucket_tile u32[B], snap float4[256 B] (colour and transmittance
+ *                   before each 32-instance bucket, per pixel of the tile)
+ */
+#ifndef GSX_B200_KERNELS_CUH
+#define GSX_B200_KERNELS_CUH
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gsx_detmath.h"
+
+#define GSX_TILE 16
+#define GSX_TILE_PIXELS 256
+#define GSX_SEQ_TILES 8
+#define GSX_SPIN_LIMIT (1u << 22)
+
+/* device-side error flags (bitwise-or into ctx->dev_flags[0]) */
+#define GSX_FLAG_LOOKBACK_TIMEOUT 1u
+#define GSX_FLAG_INSTANCE_OVERFLOW 2u
+#define GSX_FLAG_BUCKET_OVERFLOW 4u
+
+struct __align__(16) PrimRec {
+    float4 a; /* mean2d.x, mean2d.y, conic.x, conic.y */
+    float4 b; /* conic.z, opacity, rgb.r, rgb.g  (rgb unclamped) */
+    float4 c; /* rgb.b, depth, bounds x (x0 | x1 << 16), bounds y (y0 | y1 << 16) as bits */
+};
+
+struct CameraParams {
+    float w2c[12];
+    float cam_pos[3];
+    float fx, fy, cx, cy;
+    float width_f, height_f;
+    float near_plane, far_plane;
+    int width, height;
+    int grid_w, grid_h;
+};
+
+/* Decoupled-lookback status word: 2-bit flag in the top bits, 30-bit count below. */
+#define GSX_LB_EMPTY 0u
+#define GSX_LB_AGG 1u
+#define GSX_LB_INC 2u
+#define GSX_LB_SHIFT 30
+#define GSX_LB_MASK ((1u << GSX_LB_SHIFT) - 1u)
+
+__device__ __forceinline__ uint32_t gsx_ld_acquire(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void gsx_st_release(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t gsx_ld_acquire64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void gsx_st_release64(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+/* fastgs/kernels_forward.cuh:71-106 (will_primitive_contribute), identical arithmetic to the
+ * oracle's orc_tile_contributes.  `mx, my` is mean2d - 0.5. */
+__device__ __forceinline__ bool gsx_tile_contributes(float mx, float my, float cx, float cy, float cz, unsigned tx,
+                                                     unsigned ty, float power_threshold)
+{
+    const float rminx = (float)(tx * GSX_TILE), rminy = (float)(ty * GSX_TILE);
+    const float rmaxx = (float)((tx + 1) * GSX_TILE - 1), rmaxy = (float)((ty + 1) * GSX_TILE - 1);
+    const float x_min_diff = rminx - mx;
+    const float x_left = x_min_diff > 0.0f ? 1.0f : 0.0f;
+    const float not_in_x = x_left + (mx > rmaxx ? 1.0f : 0.0f);
+    const float y_min_diff = rminy - my;
+    const float y_above = y_min_diff > 0.0f ? 1.0f : 0.0f;
+    const float not_in_y = y_above + (my > rmaxy ? 1.0f : 0.0f);
+    if(not_in_y + not_in_x == 0.0f) return true;
+    const float ccx = x_left != 0.0f ? rminx : rmaxx;
+    const float ccy = y_above != 0.0f ? rminy : rmaxy;
+    const float diffx = mx - ccx, diffy = my - ccy;
+    const float dx = copysignf((float)(GSX_TILE - 1), x_min_diff);
+    const float dy = copysignf((float)(GSX_TILE - 1), y_min_diff);
+    const float tx_ = not_in_y * gsx_saturatef((dx * cx * diffx + dx * cy * diffy) / (dx * cx * dx));
+    const float ty_ = not_in_x * gsx_saturatef((dy * cy * diffx + dy * cz * diffy) / (dy * cz * dy));
+    const float px = ccx + tx_ * dx, py = ccy + ty_ * dy;
+    const float ddx = mx - px, ddy = my - py;
+    const float power = 0.5f * (cx * ddx * ddx + cz * ddy * ddy) + cy * ddx * ddy;
+    return power <= power_threshold;
+}
+
+/* ---- kernel launchers (each .cu file owns its kernels; these are host-side entry points) ---- */
+struct RenderScratch;
+
+cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
+                                  const float *opacity, const float *sh0, const float *sh1, const float *sh2,
+                                  const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
+                                  uint32_t *offsets, uint32_t *lookback, uint32_t *tile_counter, uint32_t *flags,
+                                  cudaStream_t stream);
+cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *offsets, int grid_w,
+                            unsigned long long *keys, uint32_t *vals, uint64_t capacity, uint32_t *flags,
+                            cudaStream_t stream);
+size_t gsx_sort_scratch_bytes(uint64_t capacity);
+cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
+                                  uint32_t *vals_b, uint64_t count, int begin_bit, int end_bit, void *scratch,
+                                  size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream);
+cudaError_t gsx_launch_tile_ranges(const unsigned long long *keys, uint64_t count, int n_tiles, uint2 *ranges,
+                                   uint32_t *bucket_offsets, uint32_t *bucket_tile, uint64_t bucket_capacity,
+                                   uint32_t *flags, cudaStream_t stream);
+cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
+                                     const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
+                                     const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max,
+                                     float4 *snap, cudaStream_t stream);
+cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const uint2 *ranges,
+                                      const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
+                                      int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,
+                                      const uint32_t *tile_max, const float4 *snap, const float *grad_rgb,
+                                      float4 *grad_acc, int64_t n, cudaStream_t stream);
+cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rotation, const float *logscale,
+                                           const float *sh1, const float *sh2, const float *sh3, int sh_degree,
+                                           int64_t n, const CameraParams &cam, const uint32_t *offsets,
+                                           float4 *grad_acc, float *g_mean3d, float *g_rotation, float *g_logscale,
+                                           float *g_opacity, float *g_sh0, float *g_sh1, float *g_sh2, float *g_sh3,
+                                           cudaStream_t stream);
+
+#define GSX_ADAM_MAX_GROUPS 16
+struct AdamGroupDev {
+    float *param;
+    const float *grad;
+    float *m1;
+    float *m2;
+    uint64_t n;
+    uint64_t first_block;
+    float lr, beta1, beta2, eps, weight_decay, max_grad;
+    double inv_c1, inv_c2;
+};
+struct AdamTable {
+    AdamGroupDev g[GSX_ADAM_MAX_GROUPS];
+    int count;
+};
+cudaError_t gsx_launch_adam(AdamTable &table, cudaStream_t stream);
+cudaError_t gsx_launch_l1_ssim(int mode, const float *pred, const float *target, float *loss_map, float *grad,
+                               float *loss_sum, int planes, int height, int width, float l1_scale, float ssim_scale,
+                               float l1_grad_scale, float ssim_grad_scale, cudaStream_t stream);
+cudaError_t gsx_launch_pointwise_loss(int op, const float *pred, const float *target, float *out, size_t n, float scale,
+                                      cudaStream_t stream);
+
+#endif /* GSX_B200_KERNELS_CUH */

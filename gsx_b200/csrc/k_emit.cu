@@ -1,0 +1,101 @@
+/*
+ * Emission of one 64-bit key (tile_id << 32 | depth bits) and one 32-bit primitive index per
+ * (visible Gaussian, touched tile), in primitive order and, per primitive, row-major tile order.
+ *
+ * Follows fastgs/kernels_forward.cuh:453-556 (create_instances_cu) for which tiles are emitted
+ * (the same exact overlap test as the preprocess count), but writes the combined tile|depth key
+ * so that one stable LSD radix sort yields the reference's (tile, then depth) order
+ * (forward.cu:155-161 depth sort followed by the stable 16-bit tile sort at :214-220).
+ * Compiled with -fmad=false (bit-identical overlap decisions with the preprocess and the oracle).
+ */
+#include "gsx_b200_kernels.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec *__restrict__ rec,
+                                                        const uint32_t *__restrict__ offsets, unsigned grid_w,
+                                                        unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
+                                                        uint64_t capacity, uint32_t *__restrict__ flags)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    uint32_t start = 0, cnt = 0;
+    if(i < n) {
+        start = offsets[i];
+        cnt = offsets[i + 1] - start;
+    }
+    if(__ballot_sync(0xffffffffu, cnt != 0) == 0) return;
+    float msx = 0.0f, msy = 0.0f, cx = 0.0f, cy = 0.0f, cz = 0.0f, pt = 0.0f;
+    unsigned bx0 = 0, bw = 0, by0 = 0, tmax = 0;
+    unsigned long long dbits = 0;
+    if(cnt != 0) {
+        const PrimRec r = rec[i];
+        msx = r.a.x - 0.5f;
+        msy = r.a.y - 0.5f;
+        cx = r.a.z;
+        cy = r.a.w;
+        cz = r.b.x;
+        pt = gsx_logf(r.b.y * 255.0f);
+        dbits = (unsigned long long)__float_as_uint(r.c.y);
+        const unsigned bx = __float_as_uint(r.c.z), by = __float_as_uint(r.c.w);
+        bx0 = bx & 0xffffu;
+        bw = (bx >> 16) - bx0;
+        by0 = by & 0xffffu;
+        tmax = bw * ((by >> 16) - by0);
+        if((uint64_t)start + cnt > capacity) {
+            atomicOr(flags, GSX_FLAG_INSTANCE_OVERFLOW);
+            cnt = 0;
+            tmax = 0;
+        }
+    }
+    uint32_t wpos = start;
+    const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
+    for(unsigned k = 0; k < nseq; ++k) {
+        const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
+        if(gsx_tile_contributes(msx, msy, cx, cy, cz, tx, ty, pt)) {
+            keys[wpos] = ((unsigned long long)(ty * grid_w + tx) << 32) | dbits;
+            vals[wpos] = (uint32_t)i;
+            ++wpos;
+        }
+    }
+    unsigned coop = __ballot_sync(0xffffffffu, tmax > GSX_SEQ_TILES);
+    const unsigned lt_mask = (1u << lane) - 1u;
+    while(coop) {
+        const int L = __ffs(coop) - 1;
+        coop &= coop - 1u;
+        const unsigned lbx0 = __shfl_sync(0xffffffffu, bx0, L), lbw = __shfl_sync(0xffffffffu, bw, L);
+        const unsigned lby0 = __shfl_sync(0xffffffffu, by0, L), ltmax = __shfl_sync(0xffffffffu, tmax, L);
+        const float lmx = __shfl_sync(0xffffffffu, msx, L), lmy = __shfl_sync(0xffffffffu, msy, L);
+        const float lcx = __shfl_sync(0xffffffffu, cx, L), lcy = __shfl_sync(0xffffffffu, cy, L);
+        const float lcz = __shfl_sync(0xffffffffu, cz, L), lpt = __shfl_sync(0xffffffffu, pt, L);
+        const unsigned long long ldb = __shfl_sync(0xffffffffu, dbits, L);
+        uint32_t lpos = __shfl_sync(0xffffffffu, wpos, L);
+        const uint32_t lidx = (uint32_t)__shfl_sync(0xffffffffu, (long long)i, L);
+        for(unsigned base = GSX_SEQ_TILES; base < ltmax; base += 32u) {
+            const unsigned k = base + (unsigned)lane;
+            const unsigned tx = lbx0 + k % lbw, ty = lby0 + k / lbw;
+            const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, tx, ty, lpt);
+            const unsigned ballot = __ballot_sync(0xffffffffu, c);
+            if(c) {
+                const uint32_t p = lpos + (uint32_t)__popc(ballot & lt_mask);
+                keys[p] = ((unsigned long long)(ty * grid_w + tx) << 32) | ldb;
+                vals[p] = lidx;
+            }
+            lpos += (uint32_t)__popc(ballot);
+        }
+    }
+}
+
+} // namespace
+
+cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *offsets, int grid_w,
+                            unsigned long long *keys, uint32_t *vals, uint64_t capacity, uint32_t *flags,
+                            cudaStream_t stream)
+{
+    if(n <= 0) return cudaSuccess;
+    const int64_t blocks = (n + kThreads - 1) / kThreads;
+    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, offsets, (unsigned)grid_w, keys, vals, capacity, flags);
+    return cudaGetLastError();
+}

@@ -1,0 +1,263 @@
+/*
+ * Image losses: separable-Gaussian SSIM fused with L1, forward and backward in ONE kernel.
+ *
+ * Semantics follow the reference's two-object training loss (gsx-runtime.c:1496-1510 issuing
+ * L1 then SSIM forward, then L1 then SSIM backward):
+ *   L1   gsx-cuda/loss-pointwise-kernels.cu:43-89  loss_map += s1*|p-t|, grad += sign(p-t)*g1
+ *   SSIM gsx-cuda/loss-ssim-kernels.cu:46-356       11x11 window sigma 1.5, zero padding, C1=1e-4,
+ *        C2=9e-4; inside a 5-pixel image border the loss map is SET to 0 (overwriting the L1 term)
+ *        and the SSIM partial derivatives are 0; grad += blur(-g2 * dm/dmu) + 2p blur(-g2 * dm/dsigma1^2)
+ *        + t blur(-g2 * dm/dsigma12).
+ * where g1, g2 are the caller's gradient scales (MEAN normalisation: scale / numel, applied by the
+ * host as gsx-tensor-helpers.h:236-244 does).
+ *
+ * B200 design: the reference runs two kernels and keeps 3 floats per element of partials in HBM
+ * between them.  Here one CTA owns a 32x32 output tile and recomputes the partials it needs on a
+ * 42x42 halo region from a 52x52 input tile in shared memory, so HBM sees only the inputs, the
+ * loss map and the gradient (no scratch at all).  The same kernel, with the loss or the gradient
+ * stage compiled out, serves the standalone SSIM forward and backward calls.
+ */
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kOut = 32;            /* output tile edge */
+constexpr int kR = 5;               /* window radius */
+constexpr int kMid = kOut + 2 * kR; /* 42: partials region */
+constexpr int kIn = kOut + 4 * kR;  /* 52: input region */
+
+__constant__ float c_gauss[11];
+
+struct LossSmem {
+    float in_p[kIn][kIn];
+    float in_t[kIn][kIn];
+    float h[5][kIn][kMid];   /* horizontal blur of p, p^2, t, t^2, pt */
+    float part[3][kMid][kMid];
+    float h2[3][kMid][kOut]; /* horizontal blur of partials */
+};
+
+template <bool DO_LOSS, bool DO_GRAD, bool WITH_L1>
+__global__ void __launch_bounds__(kThreads) l1_ssim_kernel(const float *__restrict__ pred, const float *__restrict__ target,
+                                                           float *__restrict__ loss_map, float *__restrict__ grad,
+                                                           float *__restrict__ loss_sum, int planes, int height, int width,
+                                                           float l1_scale, float ssim_scale, float l1_grad_scale,
+                                                           float ssim_grad_scale)
+{
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    LossSmem &S = *reinterpret_cast<LossSmem *>(smem_raw);
+    const int ox = blockIdx.x * kOut, oy = blockIdx.y * kOut;
+    const size_t plane_elems = (size_t)height * (size_t)width;
+    float local_sum = 0.0f;
+    for(int plane = blockIdx.z; plane < planes; plane += gridDim.z) {
+        const float *P = pred + (size_t)plane * plane_elems;
+        const float *Tg = target + (size_t)plane * plane_elems;
+        /* stage 0: input tile with zero padding */
+        for(int j = threadIdx.x; j < kIn * kIn; j += kThreads) {
+            const int y = j / kIn, x = j % kIn;
+            const int gy = oy - 2 * kR + y, gx = ox - 2 * kR + x;
+            float pv = 0.0f, tv = 0.0f;
+            if(gy >= 0 && gy < height && gx >= 0 && gx < width) {
+                const size_t idx = (size_t)gy * width + gx;
+                pv = P[idx];
+                tv = Tg[idx];
+            }
+            S.in_p[y][x] = pv;
+            S.in_t[y][x] = tv;
+        }
+        __syncthreads();
+        /* stage 1: horizontal blur of the five moments */
+        for(int j = threadIdx.x; j < kIn * kMid; j += kThreads) {
+            const int y = j / kMid, x = j % kMid;
+            float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, s4 = 0.0f;
+#pragma unroll
+            for(int k = 0; k < 11; ++k) {
+                const float w = c_gauss[k];
+                const float a = S.in_p[y][x + k], b = S.in_t[y][x + k];
+                s0 += w * a;
+                s1 += w * (a * a);
+                s2 += w * b;
+                s3 += w * (b * b);
+                s4 += w * (a * b);
+            }
+            S.h[0][y][x] = s0;
+            S.h[1][y][x] = s1;
+            S.h[2][y][x] = s2;
+            S.h[3][y][x] = s3;
+            S.h[4][y][x] = s4;
+        }
+        __syncthreads();
+        /* stage 2: vertical blur -> SSIM, loss and partials on the 42x42 halo region */
+        for(int j = threadIdx.x; j < kMid * kMid; j += kThreads) {
+            const int y = j / kMid, x = j % kMid;
+            const int gy = oy - kR + y, gx = ox - kR + x;
+            float mu1 = 0.0f, e11 = 0.0f, mu2 = 0.0f, e22 = 0.0f, e12 = 0.0f;
+#pragma unroll
+            for(int k = 0; k < 11; ++k) {
+                const float w = c_gauss[k];
+                mu1 += w * S.h[0][y + k][x];
+                e11 += w * S.h[1][y + k][x];
+                mu2 += w * S.h[2][y + k][x];
+                e22 += w * S.h[3][y + k][x];
+                e12 += w * S.h[4][y + k][x];
+            }
+            const bool in_image = gy >= 0 && gy < height && gx >= 0 && gx < width;
+            const bool border = gy < kR || gy >= height - kR || gx < kR || gx >= width - kR;
+            const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2;
+            const float s1sq = e11 - mu1_sq, s2sq = e22 - mu2_sq, s12 = e12 - mu1 * mu2;
+            const float A = mu1_sq + mu2_sq + 1e-4f, B = s1sq + s2sq + 9e-4f;
+            const float C = 2.0f * mu1 * mu2 + 1e-4f, D = 2.0f * s12 + 9e-4f;
+            const float den = A * B;
+            if(DO_LOSS && in_image && y >= kR && y < kR + kOut && x >= kR && x < kR + kOut) {
+                const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
+                const float ssim = den == 0.0f ? 1.0f : (C * D) / den;
+                float lm = loss_map[idx];
+                if(WITH_L1) lm += l1_scale * fabsf(S.in_p[y + kR][x + kR] - S.in_t[y + kR][x + kR]);
+                lm = border ? 0.0f : lm + ssim_scale * (1.0f - ssim);
+                loss_map[idx] = lm;
+                local_sum += lm;
+            }
+            if(DO_GRAD) {
+                float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f;
+                if(in_image && !border && den != 0.0f) {
+                    const float cd = C * D;
+                    d0 = (mu2 * 2.0f * D) / den - (mu2 * 2.0f * C) / den - (mu1 * 2.0f * cd) / (A * den) + (mu1 * 2.0f * cd) / (den * B);
+                    d1 = -cd / (den * B);
+                    d2 = (2.0f * C) / den;
+                }
+                S.part[0][y][x] = d0 * -ssim_grad_scale;
+                S.part[1][y][x] = d1 * -ssim_grad_scale;
+                S.part[2][y][x] = d2 * -ssim_grad_scale;
+            }
+        }
+        if(DO_GRAD) {
+            __syncthreads();
+            /* stage 3: horizontal blur of the partials */
+            for(int j = threadIdx.x; j < kMid * kOut; j += kThreads) {
+                const int y = j / kOut, x = j % kOut;
+                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+                for(int k = 0; k < 11; ++k) {
+                    const float w = c_gauss[k];
+                    s0 += w * S.part[0][y][x + k];
+                    s1 += w * S.part[1][y][x + k];
+                    s2 += w * S.part[2][y][x + k];
+                }
+                S.h2[0][y][x] = s0;
+                S.h2[1][y][x] = s1;
+                S.h2[2][y][x] = s2;
+            }
+            __syncthreads();
+            /* stage 4: vertical blur, chain rule, L1 gradient */
+            for(int j = threadIdx.x; j < kOut * kOut; j += kThreads) {
+                const int y = j / kOut, x = j % kOut;
+                const int gy = oy + y, gx = ox + x;
+                if(gy >= height || gx >= width) continue;
+                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+                for(int k = 0; k < 11; ++k) {
+                    const float w = c_gauss[k];
+                    s0 += w * S.h2[0][y + k][x];
+                    s1 += w * S.h2[1][y + k][x];
+                    s2 += w * S.h2[2][y + k][x];
+                }
+                const float p = S.in_p[y + 2 * kR][x + 2 * kR], t = S.in_t[y + 2 * kR][x + 2 * kR];
+                const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
+                float g = grad[idx];
+                if(WITH_L1) {
+                    const float d = p - t;
+                    g += (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * l1_grad_scale;
+                }
+                g += s0 + 2.0f * p * s1 + t * s2;
+                grad[idx] = g;
+            }
+        }
+        __syncthreads();
+    }
+    if(DO_LOSS && loss_sum != nullptr) {
+#pragma unroll
+        for(int d = 16; d > 0; d >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, d);
+        if((threadIdx.x & 31) == 0 && local_sum != 0.0f) atomicAdd(loss_sum, local_sum);
+    }
+}
+
+__global__ void pointwise_kernel(int op, const float *__restrict__ pred, const float *__restrict__ target,
+                                 float *__restrict__ out, size_t n, float scale)
+{
+    for(size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float d = pred[i] - target[i];
+        switch(op) {
+        case 0: out[i] += scale * fabsf(d); break;                                        /* L1 forward */
+        case 1: out[i] += (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * scale; break;   /* L1 backward */
+        case 2: out[i] += scale * d * d; break;                                           /* MSE forward */
+        default: out[i] += 2.0f * d * scale; break;                                       /* MSE backward */
+        }
+    }
+}
+
+bool g_gauss_ready[64];
+
+template <bool L, bool G, bool W>
+cudaError_t launch_l1_ssim(const float *pred, const float *target, float *loss_map, float *grad, float *loss_sum,
+                           int planes, int height, int width, float l1_scale, float ssim_scale, float l1_grad_scale,
+                           float ssim_grad_scale, cudaStream_t stream)
+{
+    const size_t smem = sizeof(LossSmem);
+    cudaError_t err = cudaFuncSetAttribute(l1_ssim_kernel<L, G, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if(err != cudaSuccess) return err;
+    dim3 grid((unsigned)((width + kOut - 1) / kOut), (unsigned)((height + kOut - 1) / kOut),
+              (unsigned)(planes < 65535 ? planes : 65535));
+    l1_ssim_kernel<L, G, W><<<grid, kThreads, smem, stream>>>(pred, target, loss_map, grad, loss_sum, planes, height,
+                                                              width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale);
+    return cudaGetLastError();
+}
+
+cudaError_t ensure_gauss()
+{
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if(err != cudaSuccess) return err;
+    if(dev < 64 && g_gauss_ready[dev]) return cudaSuccess;
+    double w[11], sum = 0.0;
+    for(int k = 0; k < 11; ++k) {
+        const double d = (double)(k - 5);
+        w[k] = __builtin_exp(-(d * d) / (2.0 * 1.5 * 1.5));
+        sum += w[k];
+    }
+    float wf[11];
+    for(int k = 0; k < 11; ++k) wf[k] = (float)(w[k] / sum);
+    err = cudaMemcpyToSymbol(c_gauss, wf, sizeof(wf));
+    if(err == cudaSuccess && dev < 64) g_gauss_ready[dev] = true;
+    return err;
+}
+
+} // namespace
+
+/* mode bit 0: loss map, bit 1: gradient, bit 2: include L1 */
+cudaError_t gsx_launch_l1_ssim(int mode, const float *pred, const float *target, float *loss_map, float *grad,
+                               float *loss_sum, int planes, int height, int width, float l1_scale, float ssim_scale,
+                               float l1_grad_scale, float ssim_grad_scale, cudaStream_t stream)
+{
+    cudaError_t err = ensure_gauss();
+    if(err != cudaSuccess) return err;
+    switch(mode) {
+    case 1: return launch_l1_ssim<true, false, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
+    case 2: return launch_l1_ssim<false, true, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
+    case 3: return launch_l1_ssim<true, true, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
+    case 5: return launch_l1_ssim<true, false, true>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
+    case 7: return launch_l1_ssim<true, true, true>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+/* op: 0 L1 fwd, 1 L1 bwd, 2 MSE fwd, 3 MSE bwd */
+cudaError_t gsx_launch_pointwise_loss(int op, const float *pred, const float *target, float *out, size_t n, float scale,
+                                      cudaStream_t stream)
+{
+    if(n == 0) return cudaSuccess;
+    size_t blocks = (n + 255) / 256;
+    if(blocks > 148 * 16) blocks = 148 * 16;
+    pointwise_kernel<<<(unsigned)blocks, 256, 0, stream>>>(op, pred, target, out, n, scale);
+    return cudaGetLastError();
+}

@@ -1,0 +1,299 @@
+/*
+ * Per-Gaussian preprocess fused with the single-pass prefix sum of the tile-overlap counts.
+ *
+ * Follows fastgs/kernels_forward.cuh:179-438 (preprocess_cu) for the projection, EWA covariance,
+ * opacity-aware screen bounds and SH colour, and :109-175 for the exact tile count.  Differences
+ * in structure (not in results):
+ *   - no atomic compaction of visible primitives: each primitive's count goes through a
+ *     decoupled-lookback exclusive scan inside this kernel (dynamic tile ids guarantee forward
+ *     progress), so `offsets` comes out in primitive order and emission is deterministic;
+ *   - everything the later stages need is packed into one 48-byte PrimRec per primitive.
+ * Compiled with -fmad=false: the arithmetic matches the oracle (oracle/gsx_oracle.c) bit for bit.
+ */
+#include "gsx_b200_kernels.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr unsigned long long kFlagAgg = 1ull << 62;
+constexpr unsigned long long kFlagInc = 2ull << 62;
+constexpr unsigned long long kValueMask = (1ull << 62) - 1ull;
+
+__device__ __forceinline__ int f2i_rd(float v)
+{
+    const float f = floorf(v);
+    if(!(f == f)) return 0;
+    if(f >= 2147483647.0f) return 2147483647;
+    if(f <= -2147483648.0f) return (int)(-2147483647 - 1);
+    return (int)f;
+}
+
+__device__ __forceinline__ int f2i_ru(float v)
+{
+    const float f = ceilf(v);
+    if(!(f == f)) return 0;
+    if(f >= 2147483647.0f) return 2147483647;
+    if(f <= -2147483648.0f) return (int)(-2147483647 - 1);
+    return (int)f;
+}
+
+__device__ __forceinline__ void sh_color(const float *__restrict__ sh0, const float *__restrict__ sh1,
+                                         const float *__restrict__ sh2, const float *__restrict__ sh3, const float m[3],
+                                         const float cam[3], int64_t i, int bases, float out[3])
+{
+#pragma unroll
+    for(int c = 0; c < 3; ++c) out[c] = 0.5f + 0.28209479177387814f * sh0[i * 3 + c];
+    if(bases > 1) {
+        const float dx = m[0] - cam[0], dy = m[1] - cam[1], dz = m[2] - cam[2];
+        const float inv = 1.0f / sqrtf(dx * dx + dy * dy + dz * dz);
+        const float x = dx * inv, y = dy * inv, z = dz * inv;
+        const float *c1 = sh1 + i * 9;
+        for(int c = 0; c < 3; ++c) {
+            out[c] = out[c] + (-0.48860251190291987f * y) * c1[0 * 3 + c] + (0.48860251190291987f * z) * c1[1 * 3 + c]
+                + (-0.48860251190291987f * x) * c1[2 * 3 + c];
+        }
+        if(bases > 4) {
+            const float xx = x * x, yy = y * y, zz = z * z, xy = x * y, xz = x * z, yz = y * z;
+            const float *c2 = sh2 + i * 15;
+            for(int c = 0; c < 3; ++c) {
+                out[c] = out[c] + (1.0925484305920792f * xy) * c2[0 * 3 + c] + (-1.0925484305920792f * yz) * c2[1 * 3 + c]
+                    + (0.94617469575755997f * zz - 0.31539156525251999f) * c2[2 * 3 + c]
+                    + (-1.0925484305920792f * xz) * c2[3 * 3 + c]
+                    + (0.54627421529603959f * xx - 0.54627421529603959f * yy) * c2[4 * 3 + c];
+            }
+            if(bases > 9) {
+                const float *c3 = sh3 + i * 21;
+                for(int c = 0; c < 3; ++c) {
+                    out[c] = out[c] + (0.59004358992664352f * y * (-3.0f * xx + yy)) * c3[0 * 3 + c]
+                        + (2.8906114426405538f * xy * z) * c3[1 * 3 + c]
+                        + (0.45704579946446572f * y * (1.0f - 5.0f * zz)) * c3[2 * 3 + c]
+                        + (0.3731763325901154f * z * (5.0f * zz - 3.0f)) * c3[3 * 3 + c]
+                        + (0.45704579946446572f * x * (1.0f - 5.0f * zz)) * c3[4 * 3 + c]
+                        + (1.4453057213202769f * z * (xx - yy)) * c3[5 * 3 + c]
+                        + (0.59004358992664352f * x * (-xx + 3.0f * yy)) * c3[6 * 3 + c];
+                }
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) preprocess_kernel(
+    const float *__restrict__ mean3d, const float *__restrict__ rotation, const float *__restrict__ logscale,
+    const float *__restrict__ opacity_raw, const float *__restrict__ sh0, const float *__restrict__ sh1,
+    const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n, CameraParams cam,
+    PrimRec *__restrict__ rec, uint32_t *__restrict__ offsets, unsigned long long *__restrict__ lookback,
+    uint32_t *__restrict__ tile_counter, uint32_t *__restrict__ flags)
+{
+    __shared__ uint32_t s_tile;
+    __shared__ uint32_t s_warp_sum[kThreads / 32];
+    __shared__ unsigned long long s_prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if(threadIdx.x == 0) s_tile = atomicAdd(tile_counter, 1u);
+    __syncthreads();
+    const uint32_t tile = s_tile;
+    const int64_t i = (int64_t)tile * kThreads + threadIdx.x;
+
+    bool active = i < n;
+    float m[3] = { 0.0f, 0.0f, 0.0f };
+    float depth = 0.0f, op = 0.0f, m2x = 0.0f, m2y = 0.0f, conx = 0.0f, cony = 0.0f, conz = 0.0f, pt = 0.0f;
+    unsigned bx0 = 0, bx1 = 0, by0 = 0, by1 = 0;
+    const float *w = cam.w2c;
+    if(active) {
+        m[0] = mean3d[i * 3 + 0];
+        m[1] = mean3d[i * 3 + 1];
+        m[2] = mean3d[i * 3 + 2];
+        depth = w[8] * m[0] + w[9] * m[1] + w[10] * m[2] + w[11];
+        if(depth < cam.near_plane || depth > cam.far_plane) active = false;
+    }
+    if(active) {
+        op = gsx_sigmoidf(opacity_raw[i]);
+        if(op < 1.0f / 255.0f) active = false;
+    }
+    if(active) {
+        float var[3];
+#pragma unroll
+        for(int k = 0; k < 3; ++k) {
+            const float s = gsx_expf(logscale[i * 3 + k]);
+            var[k] = s * s;
+        }
+        const float4 q = *reinterpret_cast<const float4 *>(rotation + i * 4);
+        const float qx = q.x, qy = q.y, qz = q.z, qr = q.w;
+        const float qrr = qr * qr, qxx_raw = qx * qx, qyy_raw = qy * qy, qzz_raw = qz * qz;
+        const float qn = qrr + qxx_raw + qyy_raw + qzz_raw;
+        if(qn < 1e-8f) {
+            active = false;
+        } else {
+            const float qxx = 2.0f * qxx_raw / qn, qyy = 2.0f * qyy_raw / qn, qzz = 2.0f * qzz_raw / qn;
+            const float qxy = 2.0f * qx * qy / qn, qxz = 2.0f * qx * qz / qn, qyz = 2.0f * qy * qz / qn;
+            const float qrx = 2.0f * qr * qx / qn, qry = 2.0f * qr * qy / qn, qrz = 2.0f * qr * qz / qn;
+            const float R[9] = { 1.0f - (qyy + qzz), qxy - qrz, qry + qxz,
+                                 qrz + qxy, 1.0f - (qxx + qzz), qyz - qrx,
+                                 qxz - qry, qrx + qyz, 1.0f - (qxx + qyy) };
+            const float RS[9] = { R[0] * var[0], R[1] * var[1], R[2] * var[2],
+                                  R[3] * var[0], R[4] * var[1], R[5] * var[2],
+                                  R[6] * var[0], R[7] * var[1], R[8] * var[2] };
+            const float c11 = RS[0] * R[0] + RS[1] * R[1] + RS[2] * R[2];
+            const float c12 = RS[0] * R[3] + RS[1] * R[4] + RS[2] * R[5];
+            const float c13 = RS[0] * R[6] + RS[1] * R[7] + RS[2] * R[8];
+            const float c22 = RS[3] * R[3] + RS[4] * R[4] + RS[5] * R[5];
+            const float c23 = RS[3] * R[6] + RS[4] * R[7] + RS[5] * R[8];
+            const float c33 = RS[6] * R[6] + RS[7] * R[7] + RS[8] * R[8];
+            const float x = (w[0] * m[0] + w[1] * m[1] + w[2] * m[2] + w[3]) / depth;
+            const float y = (w[4] * m[0] + w[5] * m[1] + w[6] * m[2] + w[7]) / depth;
+            const float clip_l = (-0.15f * cam.width_f - cam.cx) / cam.fx, clip_r = (1.15f * cam.width_f - cam.cx) / cam.fx;
+            const float clip_t = (-0.15f * cam.height_f - cam.cy) / cam.fy, clip_b = (1.15f * cam.height_f - cam.cy) / cam.fy;
+            const float tx = fmaxf(clip_l, fminf(x, clip_r));
+            const float ty = fmaxf(clip_t, fminf(y, clip_b));
+            const float j11 = cam.fx / depth, j13 = -j11 * tx, j22 = cam.fy / depth, j23 = -j22 * ty;
+            const float a1x = j11 * w[0] + j13 * w[8], a1y = j11 * w[1] + j13 * w[9], a1z = j11 * w[2] + j13 * w[10];
+            const float a2x = j22 * w[4] + j23 * w[8], a2y = j22 * w[5] + j23 * w[9], a2z = j22 * w[6] + j23 * w[10];
+            const float b1x = a1x * c11 + a1y * c12 + a1z * c13, b1y = a1x * c12 + a1y * c22 + a1z * c23,
+                        b1z = a1x * c13 + a1y * c23 + a1z * c33;
+            const float b2x = a2x * c11 + a2y * c12 + a2z * c13, b2y = a2x * c12 + a2y * c22 + a2z * c23,
+                        b2z = a2x * c13 + a2y * c23 + a2z * c33;
+            float cov_x = b1x * a1x + b1y * a1y + b1z * a1z;
+            const float cov_y = b1x * a2x + b1y * a2y + b1z * a2z;
+            float cov_z = b2x * a2x + b2y * a2y + b2z * a2z;
+            cov_x += 0.3f;
+            cov_z += 0.3f;
+            const float det = cov_x * cov_z - cov_y * cov_y;
+            if(det < 1e-8f) {
+                active = false;
+            } else {
+                conx = cov_z / det;
+                cony = -cov_y / det;
+                conz = cov_x / det;
+                m2x = x * cam.fx + cam.cx;
+                m2y = y * cam.fy + cam.cy;
+                pt = gsx_logf(op * 255.0f);
+                const float ptf = sqrtf(2.0f * pt);
+                const float ex = fmaxf(ptf * sqrtf(cov_x) - 0.5f, 0.0f);
+                const float ey = fmaxf(ptf * sqrtf(cov_z) - 0.5f, 0.0f);
+                const unsigned gw = (unsigned)cam.grid_w, gh = (unsigned)cam.grid_h;
+                int v;
+                v = f2i_rd((m2x - ex) / 16.0f); bx0 = (unsigned)(v > 0 ? v : 0); bx0 = bx0 > gw ? gw : bx0;
+                v = f2i_ru((m2x + ex) / 16.0f); bx1 = (unsigned)(v > 0 ? v : 0); bx1 = bx1 > gw ? gw : bx1;
+                v = f2i_rd((m2y - ey) / 16.0f); by0 = (unsigned)(v > 0 ? v : 0); by0 = by0 > gh ? gh : by0;
+                v = f2i_ru((m2y + ey) / 16.0f); by1 = (unsigned)(v > 0 ? v : 0); by1 = by1 > gh ? gh : by1;
+                if((bx1 - bx0) * (by1 - by0) == 0) active = false;
+            }
+        }
+    }
+
+    /* exact tile count: the first GSX_SEQ_TILES tiles of the rectangle per thread, the rest
+     * warp-cooperatively (all lanes converged here; no early return above). */
+    const unsigned bw = bx1 - bx0;
+    const unsigned tmax = active ? bw * (by1 - by0) : 0u;
+    const float msx = m2x - 0.5f, msy = m2y - 0.5f;
+    unsigned cnt = 0;
+    const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
+    for(unsigned k = 0; k < nseq; ++k) {
+        if(gsx_tile_contributes(msx, msy, conx, cony, conz, bx0 + k % bw, by0 + k / bw, pt)) ++cnt;
+    }
+    unsigned coop = __ballot_sync(0xffffffffu, tmax > GSX_SEQ_TILES);
+    while(coop) {
+        const int L = __ffs(coop) - 1;
+        coop &= coop - 1u;
+        const unsigned lbx0 = __shfl_sync(0xffffffffu, bx0, L), lbw = __shfl_sync(0xffffffffu, bw, L);
+        const unsigned lby0 = __shfl_sync(0xffffffffu, by0, L), ltmax = __shfl_sync(0xffffffffu, tmax, L);
+        const float lmx = __shfl_sync(0xffffffffu, msx, L), lmy = __shfl_sync(0xffffffffu, msy, L);
+        const float lcx = __shfl_sync(0xffffffffu, conx, L), lcy = __shfl_sync(0xffffffffu, cony, L);
+        const float lcz = __shfl_sync(0xffffffffu, conz, L), lpt = __shfl_sync(0xffffffffu, pt, L);
+        unsigned sum = 0;
+        for(unsigned base = GSX_SEQ_TILES; base < ltmax; base += 32u) {
+            const unsigned k = base + (unsigned)lane;
+            const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, lbx0 + k % lbw, lby0 + k / lbw, lpt);
+            sum += (unsigned)__popc(__ballot_sync(0xffffffffu, c));
+        }
+        if(lane == L) cnt += sum;
+    }
+    if(cnt == 0) active = false;
+
+    if(active) {
+        float col[3];
+        sh_color(sh0, sh1, sh2, sh3, m, cam.cam_pos, i, bases, col);
+        PrimRec r;
+        r.a = make_float4(m2x, m2y, conx, cony);
+        r.b = make_float4(conz, op, col[0], col[1]);
+        r.c = make_float4(col[2], depth, __uint_as_float(bx0 | (bx1 << 16)), __uint_as_float(by0 | (by1 << 16)));
+        rec[i] = r;
+    }
+
+    /* block-wide exclusive scan of cnt */
+    unsigned incl = cnt;
+#pragma unroll
+    for(int d = 1; d < 32; d <<= 1) {
+        const unsigned t = __shfl_up_sync(0xffffffffu, incl, d);
+        if(lane >= d) incl += t;
+    }
+    if(lane == 31) s_warp_sum[warp] = incl;
+    __syncthreads();
+    if(warp == 0) {
+        unsigned v = lane < kThreads / 32 ? s_warp_sum[lane] : 0u;
+        unsigned wi = v;
+#pragma unroll
+        for(int d = 1; d < 32; d <<= 1) {
+            const unsigned t = __shfl_up_sync(0xffffffffu, wi, d);
+            if(lane >= d) wi += t;
+        }
+        if(lane < kThreads / 32) s_warp_sum[lane] = wi - v; /* exclusive warp offsets */
+        const unsigned long long block_total = __shfl_sync(0xffffffffu, wi, kThreads / 32 - 1);
+        /* decoupled lookback over predecessor tiles, one warp, 32 tiles per round */
+        unsigned long long prefix = 0;
+        if(tile == 0) {
+            if(lane == 0) gsx_st_release64(&lookback[0], kFlagInc | block_total);
+        } else {
+            if(lane == 0) gsx_st_release64(&lookback[tile], kFlagAgg | block_total);
+            long long pos = (long long)tile - 1;
+            unsigned spins = 0;
+            bool timed_out = false;
+            while(true) {
+                const long long t = pos - lane;
+                unsigned long long st = t >= 0 ? gsx_ld_acquire64(&lookback[t]) : kFlagInc;
+                const unsigned flag = (unsigned)(st >> 62);
+                const unsigned inc_mask = __ballot_sync(0xffffffffu, flag == 2u);
+                const unsigned empty_mask = __ballot_sync(0xffffffffu, flag == 0u);
+                /* lanes up to and including the first INC must all be non-empty */
+                const unsigned upto = inc_mask ? ((inc_mask & (0u - inc_mask)) << 1) - 1u : 0xffffffffu;
+                if(empty_mask & upto) {
+                    if(++spins > GSX_SPIN_LIMIT) {
+                        timed_out = true;
+                        break;
+                    }
+                    continue;
+                }
+                unsigned long long val = (upto >> lane) & 1u ? (st & kValueMask) : 0ull;
+#pragma unroll
+                for(int d = 16; d > 0; d >>= 1) val += __shfl_xor_sync(0xffffffffu, val, d);
+                prefix += val;
+                if(inc_mask) break;
+                pos -= 32;
+            }
+            if(timed_out && lane == 0) atomicOr(flags, GSX_FLAG_LOOKBACK_TIMEOUT);
+            if(lane == 0) gsx_st_release64(&lookback[tile], kFlagInc | (prefix + block_total));
+        }
+        if(lane == 0) {
+            s_prefix = prefix;
+            const int64_t last = (int64_t)tile * kThreads + kThreads - 1;
+            if(last >= n - 1 && (int64_t)tile * kThreads <= n - 1) offsets[n] = (uint32_t)(prefix + block_total);
+        }
+    }
+    __syncthreads();
+    if(i < n) offsets[i] = (uint32_t)(s_prefix + s_warp_sum[warp] + (incl - cnt));
+}
+
+} // namespace
+
+cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
+                                  const float *opacity, const float *sh0, const float *sh1, const float *sh2,
+                                  const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
+                                  uint32_t *offsets, uint32_t *lookback, uint32_t *tile_counter, uint32_t *flags,
+                                  cudaStream_t stream)
+{
+    if(n <= 0) return cudaSuccess;
+    const int64_t blocks = (n + kThreads - 1) / kThreads;
+    preprocess_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(
+        mean3d, rotation, logscale, opacity, sh0, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, rec, offsets,
+        reinterpret_cast<unsigned long long *>(lookback), tile_counter, flags);
+    return cudaGetLastError();
+}

@@ -1,0 +1,195 @@
+/*
+ * gsx-b200: the C ABI of a B200-native (sm_100a) backend for the GSX Gaussian-splatting library.
+ *
+ * Plain C, plain pointers and sizes, no C++ or framework types.  All tensor arguments are DEVICE
+ * pointers on the context's GPU, laid out exactly as GSX's tensors (row-major "CHW" contract of
+ * gsx/include/gsx/gsx-core.h): Gaussian fields [N,3] / [N,4] / [N] / [N,k,3], images [3,H,W].
+ * `stream` is a cudaStream_t (NULL = legacy default stream); every call is asynchronous on it
+ * unless stated otherwise, and its outputs are ready on that stream when it returns, the same
+ * contract as GSX's major stream (gsx/include/gsx/gsx-base.h:94-109).
+ *
+ * Every function returns 0 on success or a gsx_error_code value (gsx-base.h:68-84); the message
+ * of the last failure on the calling thread is available from gsx_b200_last_error().  Nothing
+ * ever falls back to the CPU: without a usable sm_100 device, calls fail.
+ *
+ * Each entry point names the reference interface it replaces (paths are inside the reference
+ * project Adversarr/gsx).
+ */
+#ifndef GSX_B200_H
+#define GSX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GSX_B200_API __attribute__((visibility("default")))
+#else
+#define GSX_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    GSX_B200_SUCCESS = 0,
+    GSX_B200_OUT_OF_MEMORY = 1,
+    GSX_B200_INVALID_ARGUMENT = 2,
+    GSX_B200_OUT_OF_RANGE = 3,
+    GSX_B200_INVALID_STATE = 4,
+    GSX_B200_NOT_SUPPORTED = 5,
+    GSX_B200_UNKNOWN = 255
+};
+
+enum { GSX_B200_FORWARD_INFERENCE = 0, GSX_B200_FORWARD_TRAIN = 1 };
+
+/* Pinhole camera: world->camera rotation (quaternion x, y, z, w) and translation, as
+ * gsx_camera_pose (gsx-base.h:211-216) plus gsx_camera_intrinsics fx, fy, cx, cy, width, height. */
+typedef struct gsx_b200_camera {
+    int32_t width;
+    int32_t height;
+    float fx, fy, cx, cy;
+    float rot_xyzw[4];
+    float transl[3];
+    float near_plane;
+    float far_plane;
+} gsx_b200_camera;
+
+/* Gaussian parameters (the GS container fields of gsx-core.h:179-373).  sh1/sh2/sh3 may be NULL
+ * when sh_degree is below 1/2/3. */
+typedef struct gsx_b200_gaussians {
+    int64_t count;
+    const float *mean3d;   /* [N,3] */
+    const float *rotation; /* [N,4] xyzw, need not be normalised */
+    const float *logscale; /* [N,3] */
+    const float *opacity;  /* [N] pre-sigmoid */
+    const float *sh0;      /* [N,3] */
+    const float *sh1;      /* [N,3,3] */
+    const float *sh2;      /* [N,5,3] */
+    const float *sh3;      /* [N,7,3] */
+} gsx_b200_gaussians;
+
+/* Parameter-gradient outputs, same shapes as gsx_b200_gaussians.  Written, not accumulated. */
+typedef struct gsx_b200_gaussian_grads {
+    float *mean3d;
+    float *rotation;
+    float *logscale;
+    float *opacity;
+    float *sh0;
+    float *sh1;
+    float *sh2;
+    float *sh3;
+} gsx_b200_gaussian_grads;
+
+typedef struct gsx_b200_context gsx_b200_context;
+
+/* Message of the last failing call on this thread ("" if none).  Static storage per thread. */
+GSX_B200_API const char *gsx_b200_last_error(void);
+
+/* Library version string. */
+GSX_B200_API const char *gsx_b200_version(void);
+
+/* Context = one render context (replaces gsx_cuda_render_context, gsx-cuda/render.c:35-80, and its
+ * per-primitive/tile/instance/bucket scratch blobs, fastgs/buffer_utils.h:51-176).  It owns all
+ * scratch on `device`, grown on demand, never shrunk.  Not thread-safe; one caller thread. */
+GSX_B200_API int gsx_b200_context_create(int device, gsx_b200_context **out_ctx);
+GSX_B200_API int gsx_b200_context_destroy(gsx_b200_context *ctx);
+
+/*
+ * Forward render into out_rgb (device [3,H,W] f32), background composed.
+ * Replaces gsx_cuda_fastgs_forward_launch (gsx-cuda/render-kernels.cu:122-247) followed by
+ * gsx_cuda_render_compose_background_to_chw_f32_kernel_launch (render-kernels.cu:72-96), i.e. the
+ * body of gsx_cuda_renderer_render (gsx-cuda/render.c:1314-1423).
+ * TRAIN retains the intermediates for one gsx_b200_render_backward on the same context; the
+ * Gaussian buffers must stay unchanged until then.  One host synchronisation per call (to size
+ * the instance buffers).
+ */
+GSX_B200_API int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *gaussians, int sh_degree,
+                            const gsx_b200_camera *camera, const float background[3], int forward_type,
+                            float *out_rgb, void *stream);
+
+/*
+ * Backward of the last TRAIN forward on ctx: grad_rgb (device [3,H,W]) -> parameter gradients.
+ * Replaces gsx_cuda_fastgs_backward_launch (gsx-cuda/render-kernels.cu:249-343), i.e. the body of
+ * gsx_cuda_renderer_backward (gsx-cuda/render.c:1425-1571).  Gradients are written for every
+ * Gaussian (zero where culled); no prior zeroing needed.  Fails with GSX_B200_INVALID_STATE when
+ * no TRAIN forward is retained (render.c:1434-1436).
+ */
+GSX_B200_API int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const gsx_b200_gaussian_grads *grads,
+                             void *stream);
+
+/* Counts of the last forward (visible Gaussians, instances, buckets).  Synchronises the stream. */
+GSX_B200_API int gsx_b200_render_stats(gsx_b200_context *ctx, uint64_t *n_visible, uint64_t *n_instances, uint64_t *n_buckets,
+                          void *stream);
+
+/* Device pointers to the last forward's intermediates, for parity checks:
+ * keys (u64, sorted), values (u32, sorted), ranges (uint2 per tile), offsets (u32 [N+1], the
+ * exclusive prefix of the per-Gaussian tile counts), tile_max (u32 per tile), pixel state
+ * (float4 per pixel: composed rgb + n_contrib bits). */
+typedef struct gsx_b200_render_view {
+    const uint64_t *keys;
+    const uint32_t *values;
+    const uint32_t *ranges;
+    const uint32_t *offsets;
+    const uint32_t *tile_max;
+    const float *pixel_state;
+    uint64_t n_instances;
+    int32_t n_tiles;
+    int32_t grid_width;
+} gsx_b200_render_view;
+GSX_B200_API int gsx_b200_render_get_view(gsx_b200_context *ctx, gsx_b200_render_view *out_view);
+
+/* Synchronise the stream and report device-side failures of previous calls on ctx (bounded
+ * lookback waits that timed out, capacity overflows) as GSX_B200_UNKNOWN; clears them. */
+GSX_B200_API int gsx_b200_context_check(gsx_b200_context *ctx, void *stream);
+
+/*
+ * Fused image loss on [planes, H, W] f32 CHW planes (planes = outer * channels), one launch.
+ * mode bit 0: accumulate the loss map; bit 1: accumulate the gradient; bit 2: include L1.
+ * With bit 2: loss_map = (loss_map + l1_scale*|p-t|) then SSIM as below; grad += sign(p-t)*l1_grad_scale.
+ * SSIM: loss_map += ssim_scale*(1-ssim) (SET to 0 within 5 pixels of the border);
+ *       grad += SSIM gradient scaled by ssim_grad_scale.
+ * loss_sum (device f32, may be NULL) receives the sum of the loss-map values this call wrote.
+ * Replaces the L1 and SSIM launches of gsx-cuda/loss.c:414-685
+ * (gsx_cuda_loss_ssim_chw_f32_forward/backward_kernel_launch, loss-ssim-kernels.cu:360-480, and the
+ * L1 kernels of loss-pointwise-kernels.cu:43-89) with one kernel and no partial-derivative scratch.
+ */
+GSX_B200_API int gsx_b200_loss_l1_ssim(int mode, const float *prediction, const float *target, float *loss_map, float *grad,
+                          float *loss_sum, int64_t planes, int32_t height, int32_t width, float l1_scale,
+                          float ssim_scale, float l1_grad_scale, float ssim_grad_scale, void *stream);
+
+/* Pointwise losses on n elements: op 0 L1 forward (out += scale*|p-t|), 1 L1 backward
+ * (out += sign(p-t)*scale), 2 MSE forward (out += scale*(p-t)^2), 3 MSE backward (out += 2(p-t)*scale).
+ * Replaces gsx-cuda/loss-pointwise-kernels.cu:7-89. */
+GSX_B200_API int gsx_b200_loss_pointwise(int op, const float *prediction, const float *target, float *out, uint64_t n, float scale,
+                            void *stream);
+
+/* One Adam parameter group (gsx_optim_param_group_desc, gsx-optim.h:60-71, plus its moment state).
+ * inv_bias_correction1/2 = 1 / (1 - beta^t) computed by the caller in double (gsx-cuda/optim.c:776-778). */
+typedef struct gsx_b200_adam_group {
+    float *parameter;
+    const float *gradient;
+    float *first_moment;
+    float *second_moment;
+    uint64_t count;
+    float learning_rate, beta1, beta2, epsilon, weight_decay, max_grad;
+    double inv_bias_correction1, inv_bias_correction2;
+} gsx_b200_adam_group;
+
+/* All groups (up to 16) in ONE launch.  Replaces the per-group loop of gsx_cuda_optim_step_selected
+ * (gsx-cuda/optim.c:746-803) over gsx_cuda_adam_step_f32_kernel_launch (gsx-cuda-kernels.cu:595-640). */
+GSX_B200_API int gsx_b200_adam_step(const gsx_b200_adam_group *groups, int32_t group_count, void *stream);
+
+/*
+ * Stable sort of `count` (u64 key, u32 value) pairs by key bits [begin_bit, end_bit), onesweep LSD
+ * radix sort.  keys/values are sorted in place (the alternate buffers are context scratch).
+ * Replaces the two cub::DeviceRadixSort::SortPairs calls of fastgs/forward.cu:155-161,214-220.
+ */
+GSX_B200_API int gsx_b200_sort_pairs(gsx_b200_context *ctx, uint64_t *keys, uint32_t *values, uint64_t count, int32_t begin_bit,
+                        int32_t end_bit, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSX_B200_H */

@@ -1,0 +1,322 @@
+"""numpy front-end for the C oracle (oracle/gsx_oracle.c) and the reference-library driver.
+
+TEST INFRASTRUCTURE ONLY.  Importable from tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference legs as the checker; the product package never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_ROOT = os.path.dirname(_HERE)
+_LIB = os.path.join(_HERE, "_build", "libgsx_oracle.so")
+_REF_DIR = os.path.join(_HERE, "_ref")
+
+F32P = ctypes.POINTER(ctypes.c_float)
+U32P = ctypes.POINTER(ctypes.c_uint32)
+U64P = ctypes.POINTER(ctypes.c_uint64)
+
+
+def _p(a, t=F32P):
+    if a is None:
+        return None
+    return a.ctypes.data_as(t)
+
+
+class _Camera(ctypes.Structure):
+    _fields_ = [("w2c", ctypes.c_float * 12), ("cam_pos", ctypes.c_float * 3),
+                ("fx", ctypes.c_float), ("fy", ctypes.c_float), ("cx", ctypes.c_float), ("cy", ctypes.c_float),
+                ("width", ctypes.c_int), ("height", ctypes.c_int),
+                ("near_plane", ctypes.c_float), ("far_plane", ctypes.c_float)]
+
+
+_lib = None
+
+
+def build():
+    """Compile the oracle (gcc, -ffp-contract=off) into oracle/_build."""
+    subprocess.run(["make", "-s", "-f", "oracle/Makefile"], cwd=_ROOT, check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB):
+            build()
+        L = ctypes.CDLL(_LIB)
+        L.orc_preprocess.restype = ctypes.c_uint64
+        L.orc_ssim.restype = ctypes.c_int
+        L.orc_sort_pairs.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+@dataclass
+class Camera:
+    """Pinhole camera: world->camera pose (quaternion xyzw + translation) and intrinsics."""
+    width: int
+    height: int
+    fx: float
+    fy: float
+    cx: float
+    cy: float
+    q: tuple = (0.0, 0.0, 0.0, 1.0)
+    t: tuple = (0.0, 0.0, 0.0)
+    near: float = 0.01
+    far: float = 1000.0
+
+    def c_struct(self) -> _Camera:
+        c = _Camera()
+        q = np.asarray(self.q, np.float32)
+        t = np.asarray(self.t, np.float32)
+        w2c = np.zeros(12, np.float32)
+        pos = np.zeros(3, np.float32)
+        lib().orc_pose_to_camera(_p(q), _p(t), _p(w2c), _p(pos))
+        c.w2c[:] = w2c.tolist()
+        c.cam_pos[:] = pos.tolist()
+        c.fx, c.fy, c.cx, c.cy = self.fx, self.fy, self.cx, self.cy
+        c.width, c.height = self.width, self.height
+        c.near_plane, c.far_plane = self.near, self.far
+        return c
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def render_forward(g: dict, cam: Camera, sh_degree: int = 0, bg=(0.0, 0.0, 0.0)):
+    """Full forward restatement.  Returns a dict with every intermediate the GPU path exposes."""
+    L = lib()
+    n = int(g["mean3d"].shape[0])
+    mean3d, rot, logscale, op, sh0 = (_f32(g[k]) for k in ("mean3d", "rotation", "logscale", "opacity", "sh0"))
+    sh = [_f32(g[k]) if sh_degree >= i + 1 else None for i, k in enumerate(("sh1", "sh2", "sh3"))]
+    c = cam.c_struct()
+    n_touched = np.zeros(n, np.uint32)
+    bounds = np.zeros(n * 4, np.uint32)
+    mean2d = np.zeros(n * 2, np.float32)
+    conic_op = np.zeros(n * 4, np.float32)
+    color = np.zeros(n * 3, np.float32)
+    depth = np.zeros(n, np.float32)
+    total = L.orc_preprocess(ctypes.c_int64(n), _p(mean3d), _p(rot), _p(logscale), _p(op), _p(sh0),
+                             _p(sh[0]), _p(sh[1]), _p(sh[2]), ctypes.c_int(sh_degree), ctypes.byref(c),
+                             _p(n_touched, U32P), _p(bounds, U32P), _p(mean2d), _p(conic_op), _p(color), _p(depth))
+    keys = np.zeros(max(total, 1), np.uint64)
+    vals = np.zeros(max(total, 1), np.uint32)
+    L.orc_emit(ctypes.c_int64(n), _p(n_touched, U32P), _p(bounds, U32P), _p(mean2d), _p(conic_op), _p(depth),
+               ctypes.c_int(cam.width), _p(keys, U64P), _p(vals, U32P))
+    keys, vals = keys[:total], vals[:total]
+    unsorted_keys, unsorted_vals = keys.copy(), vals.copy()
+    L.orc_sort_pairs(ctypes.c_uint64(total), _p(keys, U64P), _p(vals, U32P))
+    gw = (cam.width + 15) // 16
+    gh = (cam.height + 15) // 16
+    n_tiles = gw * gh
+    ranges = np.zeros(n_tiles * 2, np.uint32)
+    L.orc_tile_ranges(ctypes.c_uint64(total), _p(keys, U64P), ctypes.c_int(n_tiles), _p(ranges, U32P))
+    P = cam.width * cam.height
+    out_rgb = np.zeros(3 * P, np.float32)
+    out_alpha = np.zeros(P, np.float32)
+    n_contrib = np.zeros(P, np.uint32)
+    tile_max = np.zeros(n_tiles, np.uint32)
+    bgv = np.asarray(bg, np.float32)
+    L.orc_blend_forward(ctypes.c_int(cam.width), ctypes.c_int(cam.height), _p(ranges, U32P), _p(vals, U32P),
+                        _p(mean2d), _p(conic_op), _p(color), _p(bgv), _p(out_rgb), _p(out_alpha),
+                        _p(n_contrib, U32P), _p(tile_max, U32P))
+    return dict(n_touched=n_touched, bounds=bounds.reshape(n, 4), mean2d=mean2d.reshape(n, 2),
+                conic_op=conic_op.reshape(n, 4), color=color.reshape(n, 3), depth=depth,
+                n_instances=int(total), unsorted_keys=unsorted_keys, unsorted_vals=unsorted_vals,
+                keys=keys, vals=vals, ranges=ranges.reshape(n_tiles, 2),
+                rgb=out_rgb.reshape(3, cam.height, cam.width), alpha=out_alpha.reshape(cam.height, cam.width),
+                n_contrib=n_contrib.reshape(cam.height, cam.width), tile_max=tile_max, _raw=dict(
+                    mean2d=mean2d, conic_op=conic_op, color=color, ranges=ranges, vals=vals, rgb=out_rgb,
+                    n_contrib=n_contrib, tile_max=tile_max, n_touched=n_touched))
+
+
+def render_backward(g: dict, cam: Camera, fwd: dict, grad_rgb, sh_degree: int = 0):
+    """Backward restatement; returns the parameter gradients (and the 2-D helper gradients)."""
+    L = lib()
+    n = int(g["mean3d"].shape[0])
+    r = fwd["_raw"]
+    grad_rgb = _f32(grad_rgb).reshape(-1)
+    d_mean2d = np.zeros(n * 2, np.float32)
+    d_conic = np.zeros(n * 3, np.float32)
+    d_op = np.zeros(n, np.float32)
+    d_color = np.zeros(n * 3, np.float32)
+    L.orc_blend_backward(ctypes.c_int(cam.width), ctypes.c_int(cam.height), _p(r["ranges"], U32P), _p(r["vals"], U32P),
+                         _p(r["mean2d"]), _p(r["conic_op"]), _p(r["color"]), _p(r["rgb"]), _p(r["n_contrib"], U32P),
+                         _p(r["tile_max"], U32P), _p(grad_rgb), _p(d_mean2d), _p(d_conic), _p(d_op), _p(d_color))
+    c = cam.c_struct()
+    mean3d, rot, logscale = (_f32(g[k]) for k in ("mean3d", "rotation", "logscale"))
+    sh = [_f32(g[k]) if sh_degree >= i + 1 else None for i, k in enumerate(("sh1", "sh2", "sh3"))]
+    out = dict(mean3d=np.zeros((n, 3), np.float32), rotation=np.zeros((n, 4), np.float32),
+               logscale=np.zeros((n, 3), np.float32), opacity=np.zeros(n, np.float32), sh0=np.zeros((n, 3), np.float32))
+    gsh = [np.zeros((n, k, 3), np.float32) if sh_degree >= i + 1 else None for i, k in enumerate((3, 5, 7))]
+    L.orc_preprocess_backward(ctypes.c_int64(n), _p(mean3d), _p(rot), _p(logscale), _p(sh[0]), _p(sh[1]), _p(sh[2]),
+                              ctypes.c_int(sh_degree), ctypes.byref(c), _p(r["n_touched"], U32P), _p(d_mean2d),
+                              _p(d_conic), _p(d_color), _p(d_op), _p(out["mean3d"]), _p(out["rotation"]),
+                              _p(out["logscale"]), _p(out["opacity"]), _p(out["sh0"]), _p(gsh[0]), _p(gsh[1]), _p(gsh[2]))
+    for i, k in enumerate(("sh1", "sh2", "sh3")):
+        if gsh[i] is not None:
+            out[k] = gsh[i]
+    out["_helpers"] = dict(mean2d=d_mean2d.reshape(n, 2), conic=d_conic.reshape(n, 3), opacity=d_op,
+                           color=d_color.reshape(n, 3))
+    return out
+
+
+def sort_pairs(keys, vals):
+    keys = np.ascontiguousarray(keys, np.uint64).copy()
+    vals = np.ascontiguousarray(vals, np.uint32).copy()
+    lib().orc_sort_pairs(ctypes.c_uint64(keys.size), _p(keys, U64P), _p(vals, U32P))
+    return keys, vals
+
+
+def l1_ssim_train(pred, target, l1_weight=0.8, ssim_weight=0.2, loss_map=None, grad=None, normalization="mean"):
+    """The training loss pair in the order the reference session issues it (gsx-runtime.c:1496-1510):
+    L1 forward, SSIM forward, L1 backward, SSIM backward, MEAN grad normalisation (scale / numel)."""
+    pred = _f32(pred)
+    target = _f32(target)
+    shp = pred.shape
+    outer = int(np.prod(shp[:-3])) if len(shp) > 3 else 1
+    C, H, W = shp[-3:]
+    n = pred.size
+    lm = np.zeros(n, np.float32) if loss_map is None else _f32(loss_map).reshape(-1).copy()
+    gr = np.zeros(n, np.float32) if grad is None else _f32(grad).reshape(-1).copy()
+    L = lib()
+    norm = (1.0 / n) if normalization == "mean" else 1.0
+    pf, tf = pred.reshape(-1), target.reshape(-1)
+    L.orc_l1_forward(ctypes.c_int64(n), _p(pf), _p(tf), _p(lm), ctypes.c_float(l1_weight))
+    L.orc_ssim(ctypes.c_int64(outer), C, H, W, _p(pf), _p(tf), _p(lm), ctypes.c_float(ssim_weight), None, ctypes.c_float(0))
+    L.orc_l1_backward(ctypes.c_int64(n), _p(pf), _p(tf), _p(gr), ctypes.c_float(np.float32(l1_weight) / np.float32(n) if normalization == "mean" else l1_weight))
+    L.orc_ssim(ctypes.c_int64(outer), C, H, W, _p(pf), _p(tf), None, ctypes.c_float(0),
+               _p(gr), ctypes.c_float(np.float32(ssim_weight) / np.float32(n) if normalization == "mean" else ssim_weight))
+    del norm
+    return lm.reshape(shp), gr.reshape(shp)
+
+
+def ssim(pred, target, loss_scale=1.0, grad_scale=None, loss_map=None, grad=None):
+    pred = _f32(pred)
+    target = _f32(target)
+    shp = pred.shape
+    outer = int(np.prod(shp[:-3])) if len(shp) > 3 else 1
+    C, H, W = shp[-3:]
+    lm = np.zeros(pred.size, np.float32) if loss_map is None else _f32(loss_map).reshape(-1).copy()
+    gr = None
+    if grad_scale is not None:
+        gr = np.zeros(pred.size, np.float32) if grad is None else _f32(grad).reshape(-1).copy()
+    lib().orc_ssim(ctypes.c_int64(outer), C, H, W, _p(pred.reshape(-1)), _p(target.reshape(-1)), _p(lm),
+                   ctypes.c_float(loss_scale), _p(gr), ctypes.c_float(grad_scale or 0.0))
+    return lm.reshape(shp), (gr.reshape(shp) if gr is not None else None)
+
+
+def adam(param, grad, m1, m2, step, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, max_grad=0.0):
+    """One Adam step in place (param, m1, m2 are float32 arrays); `step` is the 1-based step count."""
+    inv1 = 1.0 / (1.0 - float(np.float32(beta1)) ** step)
+    inv2 = 1.0 / (1.0 - float(np.float32(beta2)) ** step)
+    lib().orc_adam(ctypes.c_int64(param.size), _p(param), _p(_f32(grad)), _p(m1), _p(m2), ctypes.c_float(beta1),
+                   ctypes.c_float(beta2), ctypes.c_float(lr), ctypes.c_float(weight_decay), ctypes.c_float(eps),
+                   ctypes.c_float(max_grad), ctypes.c_double(inv1), ctypes.c_double(inv2))
+
+
+# ------------------------------------------------------------------ reference library driver
+_ref = {}
+
+
+def ref_available(kind: str = "cpu") -> bool:
+    return os.path.exists(os.path.join(_REF_DIR, f"libgsx_refdrv_{kind}.so"))
+
+
+def ref(kind: str = "cpu"):
+    """The reference GSX library built from its own sources (oracle/Makefile.ref), via oracle/ref_driver.c."""
+    if kind not in _ref:
+        L = ctypes.CDLL(os.path.join(_REF_DIR, f"libgsx_refdrv_{kind}.so"))
+        L.refdrv_message.restype = ctypes.c_char_p
+        rc = L.refdrv_init(0 if kind == "cpu" else 1)
+        if rc != 0:
+            raise RuntimeError(f"reference init failed: {L.refdrv_message().decode()}")
+        _ref[kind] = L
+    return _ref[kind]
+
+
+def _ref_check(L, rc):
+    if rc != 0:
+        raise RuntimeError(f"reference call failed ({rc}): {L.refdrv_message().decode()}")
+
+
+def ref_loss(kind, algorithm, pred, target, scale, normalization=0, loss_map=None, grad=None):
+    L = ref(kind)
+    pred = _f32(pred)
+    shp = pred.shape
+    if pred.ndim == 3:
+        outer, (C, H, W) = 1, shp
+    else:
+        outer, C, H, W = shp
+    lm = np.zeros(pred.size, np.float32) if loss_map is None else _f32(loss_map).reshape(-1).copy()
+    gr = np.zeros(pred.size, np.float32) if grad is None else _f32(grad).reshape(-1).copy()
+    _ref_check(L, L.refdrv_loss(algorithm, normalization, outer, C, H, W, _p(pred.reshape(-1)),
+                                _p(_f32(target).reshape(-1)), ctypes.c_float(scale), _p(lm), _p(gr)))
+    return lm.reshape(shp), gr.reshape(shp)
+
+
+def ref_adam(kind, param, grad, steps, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, max_grad=0.0):
+    L = ref(kind)
+    p = _f32(param).copy()
+    _ref_check(L, L.refdrv_adam(ctypes.c_int64(p.size), _p(p), _p(_f32(grad)), steps, ctypes.c_float(lr),
+                                ctypes.c_float(beta1), ctypes.c_float(beta2), ctypes.c_float(eps),
+                                ctypes.c_float(weight_decay), ctypes.c_float(max_grad)))
+    return p
+
+
+class RefSession:
+    """A reference-library training session (render + L1/SSIM + Adam) on the CPU or CUDA backend."""
+
+    FIELDS = ("mean3d", "logscale", "rotation", "opacity", "sh0", "sh1", "sh2", "sh3")
+
+    def __init__(self, kind, g, cam: Camera, target, sh_degree=0, bg=(0, 0, 0), lr=(1e-3, 1e-2, 1e-2, 1e-2, 1e-2, 1e-2, 1e-2, 1e-2)):
+        self.L = ref(kind)
+        self.g = {k: _f32(v) for k, v in g.items()}
+        self.cam = cam
+        self.sh_degree = sh_degree
+        self.n = int(g["mean3d"].shape[0])
+        self.h = ctypes.c_void_p()
+        sh = [self.g.get(k) if sh_degree >= i + 1 else None for i, k in enumerate(("sh1", "sh2", "sh3"))]
+        q = np.asarray(cam.q, np.float32)
+        t = np.asarray(cam.t, np.float32)
+        bgv = np.asarray(bg, np.float32)
+        lrv = np.asarray(lr, np.float32)
+        self._keep = (q, t, bgv, lrv, _f32(target))
+        _ref_check(self.L, self.L.refdrv_session_create(
+            ctypes.byref(self.h), ctypes.c_int64(self.n), _p(self.g["mean3d"]), _p(self.g["rotation"]),
+            _p(self.g["logscale"]), _p(self.g["opacity"]), _p(self.g["sh0"]), _p(sh[0]), _p(sh[1]), _p(sh[2]),
+            sh_degree, cam.width, cam.height, ctypes.c_float(cam.fx), ctypes.c_float(cam.fy), ctypes.c_float(cam.cx),
+            ctypes.c_float(cam.cy), _p(q), _p(t), ctypes.c_float(cam.near), ctypes.c_float(cam.far), _p(bgv),
+            _p(self._keep[4]), _p(lrv)))
+
+    def render(self):
+        out = np.zeros(3 * self.cam.width * self.cam.height, np.float32)
+        _ref_check(self.L, self.L.refdrv_session_render(self.h, _p(out)))
+        return out.reshape(3, self.cam.height, self.cam.width)
+
+    def render_backward(self, grad_rgb):
+        out = np.zeros(3 * self.cam.width * self.cam.height, np.float32)
+        cols = (3, 3, 4, 1, 3, 9, 15, 21)
+        nf = 5 + self.sh_degree
+        grads = [np.zeros(self.n * cols[f], np.float32) for f in range(nf)]
+        arr = (F32P * nf)(*[_p(x) for x in grads])
+        _ref_check(self.L, self.L.refdrv_session_render_backward(self.h, _p(_f32(grad_rgb).reshape(-1)), _p(out), arr))
+        res = {self.FIELDS[f]: grads[f] for f in range(nf)}
+        return out.reshape(3, self.cam.height, self.cam.width), res
+
+    def step(self, l1_weight=0.8, ssim_weight=0.2):
+        sec = ctypes.c_double()
+        _ref_check(self.L, self.L.refdrv_session_step(self.h, ctypes.c_float(l1_weight), ctypes.c_float(ssim_weight),
+                                                      ctypes.byref(sec)))
+        return sec.value
+
+    def download(self, which: int, size: int):
+        out = np.zeros(size, np.float32)
+        _ref_check(self.L, self.L.refdrv_session_download(self.h, which, _p(out)))
+        return out

@@ -1,0 +1,414 @@
+#define _POSIX_C_SOURCE 200809L
+/*
+ * Thin driver over the UNMODIFIED reference GSX library's public C API (test infrastructure only).
+ *
+ * Compiled against the reference's public headers and linked against the library that
+ * oracle/Makefile.ref builds from the reference sources (CPU: libgsx_ref_cpu.so; CUDA:
+ * libgsx_ref_cuda.so).  It exposes a few host-buffer entry points so that tests can compare the
+ * oracle with the reference itself, and so that bench.py's reference arm can time the reference
+ * CPU backend's training step through the reference's own public API (the calls mirror
+ * gsx-runtime.c:1491-1536: render TRAIN, L1 and SSIM forward/backward, render backward, Adam).
+ */
+#include <gsx/gsx.h>
+
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+
+#define REF_CHECK(expr)                                       \
+    do {                                                      \
+        gsx_error e__ = (expr);                               \
+        if(!gsx_error_is_success(e__)) {                      \
+            refdrv_last_message = e__.message ? e__.message : #expr; \
+            return (int)e__.code ? (int)e__.code : 255;       \
+        }                                                     \
+    } while(0)
+
+static const char *refdrv_last_message = "";
+static gsx_backend_t refdrv_backend = NULL;
+static gsx_backend_buffer_type_t refdrv_device_type = NULL;
+
+const char *refdrv_message(void) { return refdrv_last_message; }
+
+/* backend_type: 0 = CPU, 1 = CUDA */
+int refdrv_init(int backend_type)
+{
+    gsx_backend_device_t device = NULL;
+    gsx_backend_desc desc;
+    if(refdrv_backend != NULL) return 0;
+    REF_CHECK(gsx_backend_registry_init());
+    REF_CHECK(gsx_get_backend_device_by_type((gsx_backend_type)backend_type, 0, &device));
+    memset(&desc, 0, sizeof(desc));
+    desc.device = device;
+    REF_CHECK(gsx_backend_init(&refdrv_backend, &desc));
+    REF_CHECK(gsx_backend_find_buffer_type(refdrv_backend, GSX_BACKEND_BUFFER_TYPE_DEVICE, &refdrv_device_type));
+    return 0;
+}
+
+static int refdrv_tensor(gsx_arena_t arena, gsx_tensor_t *out, int rank, const int *shape, const float *host)
+{
+    gsx_tensor_desc d;
+    gsx_size_t bytes = sizeof(float);
+    memset(&d, 0, sizeof(d));
+    d.rank = rank;
+    for(int i = 0; i < rank; ++i) {
+        d.shape[i] = shape[i];
+        bytes *= (gsx_size_t)shape[i];
+    }
+    d.data_type = GSX_DATA_TYPE_F32;
+    d.storage_format = GSX_STORAGE_FORMAT_CHW;
+    d.arena = arena;
+    REF_CHECK(gsx_tensor_init(out, &d));
+    if(host != NULL) {
+        REF_CHECK(gsx_tensor_upload(*out, host, bytes));
+    } else {
+        REF_CHECK(gsx_tensor_set_zero(*out));
+    }
+    return 0;
+}
+
+static int refdrv_arena(gsx_arena_t *arena, gsx_size_t bytes)
+{
+    gsx_arena_desc ad;
+    memset(&ad, 0, sizeof(ad));
+    ad.initial_capacity_bytes = bytes;
+    REF_CHECK(gsx_arena_init(arena, refdrv_device_type, &ad));
+    return 0;
+}
+
+/* ---------------------------------------------------------------- a training session */
+typedef struct refdrv_session {
+    gsx_arena_t arena;
+    gsx_renderer_t renderer;
+    gsx_render_context_t rctx;
+    gsx_loss_t l1, ssim;
+    gsx_loss_context_t l1_ctx, ssim_ctx;
+    gsx_optim_t optim;
+    gsx_tensor_t params[8], grads[8];
+    gsx_tensor_t out_rgb, target, loss_map, grad_rgb;
+    gsx_camera_intrinsics intr;
+    gsx_camera_pose pose;
+    float near_plane, far_plane, bg[3];
+    int sh_degree, n_fields;
+    int64_t n;
+    int width, height;
+} refdrv_session;
+
+/*
+ * fields: mean3d[N,3], rotation[N,4], logscale[N,3], opacity[N], sh0[N,3] (+ sh1/2/3 when sh_degree > 0).
+ * lr[8] per role (mean3d, logscale, rotation, opacity, sh0, sh1, sh2, sh3).  target is CHW [3,H,W].
+ */
+int refdrv_session_create(refdrv_session **out, int64_t n, const float *mean3d, const float *rotation, const float *logscale,
+                          const float *opacity, const float *sh0, const float *sh1, const float *sh2, const float *sh3,
+                          int sh_degree, int width, int height, float fx, float fy, float cx, float cy, const float q[4],
+                          const float t[3], float near_plane, float far_plane, const float bg[3], const float *target,
+                          const float lr[8])
+{
+    refdrv_session *s = (refdrv_session *)calloc(1, sizeof(refdrv_session));
+    gsx_size_t per_g = (3 + 4 + 3 + 1 + 3 + 9 + 15 + 21) * 2 * 4 + 64;
+    gsx_size_t bytes = (gsx_size_t)n * per_g + (gsx_size_t)width * height * 4 * 16 + (1u << 20);
+    const float *pv[8] = { mean3d, logscale, rotation, opacity, sh0, sh1, sh2, sh3 };
+    const int cols[8] = { 3, 3, 4, 1, 3, 9, 15, 21 };
+    gsx_renderer_desc rd;
+    gsx_loss_desc ld;
+    gsx_optim_param_group_desc groups[8];
+    gsx_optim_desc od;
+    if(s == NULL) return 1;
+    *out = s;
+    s->n = n;
+    s->width = width;
+    s->height = height;
+    s->sh_degree = sh_degree;
+    s->n_fields = 5 + sh_degree;
+    s->near_plane = near_plane;
+    s->far_plane = far_plane;
+    memcpy(s->bg, bg, sizeof(s->bg));
+    if(refdrv_arena(&s->arena, bytes)) return 1;
+    for(int f = 0; f < s->n_fields; ++f) {
+        int shape[2] = { (int)n, cols[f] };
+        if(f == 3) {
+            if(refdrv_tensor(s->arena, &s->params[f], 1, shape, pv[f])) return 1;
+            if(refdrv_tensor(s->arena, &s->grads[f], 1, shape, NULL)) return 1;
+        } else {
+            if(f >= 5) shape[1] = cols[f] / 3;
+            int shape3[3] = { (int)n, cols[f] / 3, 3 };
+            if(f >= 5) {
+                if(refdrv_tensor(s->arena, &s->params[f], 3, shape3, pv[f])) return 1;
+                if(refdrv_tensor(s->arena, &s->grads[f], 3, shape3, NULL)) return 1;
+            } else {
+                if(refdrv_tensor(s->arena, &s->params[f], 2, shape, pv[f])) return 1;
+                if(refdrv_tensor(s->arena, &s->grads[f], 2, shape, NULL)) return 1;
+            }
+        }
+    }
+    {
+        int img[3] = { 3, height, width };
+        if(refdrv_tensor(s->arena, &s->out_rgb, 3, img, NULL)) return 1;
+        if(refdrv_tensor(s->arena, &s->target, 3, img, target)) return 1;
+        if(refdrv_tensor(s->arena, &s->loss_map, 3, img, NULL)) return 1;
+        if(refdrv_tensor(s->arena, &s->grad_rgb, 3, img, NULL)) return 1;
+    }
+    memset(&rd, 0, sizeof(rd));
+    rd.width = width;
+    rd.height = height;
+    rd.output_data_type = GSX_DATA_TYPE_F32;
+    REF_CHECK(gsx_renderer_init(&s->renderer, refdrv_backend, &rd));
+    REF_CHECK(gsx_render_context_init(&s->rctx, s->renderer));
+    memset(&ld, 0, sizeof(ld));
+    ld.algorithm = GSX_LOSS_ALGORITHM_L1;
+    ld.grad_normalization = GSX_LOSS_GRAD_NORMALIZATION_TYPE_MEAN;
+    REF_CHECK(gsx_loss_init(&s->l1, refdrv_backend, &ld));
+    ld.algorithm = GSX_LOSS_ALGORITHM_SSIM;
+    REF_CHECK(gsx_loss_init(&s->ssim, refdrv_backend, &ld));
+    REF_CHECK(gsx_loss_context_init(&s->l1_ctx, s->l1));
+    REF_CHECK(gsx_loss_context_init(&s->ssim_ctx, s->ssim));
+    memset(groups, 0, sizeof(groups));
+    for(int f = 0; f < s->n_fields; ++f) {
+        groups[f].role = (gsx_optim_param_role)f;
+        groups[f].parameter = s->params[f];
+        groups[f].gradient = s->grads[f];
+        groups[f].learning_rate = lr[f];
+        groups[f].beta1 = 0.9f;
+        groups[f].beta2 = 0.999f;
+        groups[f].epsilon = 1e-8f;
+    }
+    memset(&od, 0, sizeof(od));
+    od.algorithm = GSX_OPTIM_ALGORITHM_ADAM;
+    od.param_groups = groups;
+    od.param_group_count = s->n_fields;
+    REF_CHECK(gsx_optim_init(&s->optim, refdrv_backend, &od));
+    memset(&s->intr, 0, sizeof(s->intr));
+    s->intr.model = (gsx_camera_model)0;
+    s->intr.fx = fx;
+    s->intr.fy = fy;
+    s->intr.cx = cx;
+    s->intr.cy = cy;
+    s->intr.width = width;
+    s->intr.height = height;
+    memset(&s->pose, 0, sizeof(s->pose));
+    s->pose.rot.x = q[0];
+    s->pose.rot.y = q[1];
+    s->pose.rot.z = q[2];
+    s->pose.rot.w = q[3];
+    s->pose.transl.x = t[0];
+    s->pose.transl.y = t[1];
+    s->pose.transl.z = t[2];
+    return 0;
+}
+
+static void refdrv_fill_forward(refdrv_session *s, gsx_render_forward_request *rq, gsx_render_forward_type type)
+{
+    memset(rq, 0, sizeof(*rq));
+    rq->intrinsics = &s->intr;
+    rq->pose = &s->pose;
+    rq->near_plane = s->near_plane;
+    rq->far_plane = s->far_plane;
+    rq->background_color.x = s->bg[0];
+    rq->background_color.y = s->bg[1];
+    rq->background_color.z = s->bg[2];
+    rq->precision = GSX_RENDER_PRECISION_FLOAT32;
+    rq->sh_degree = s->sh_degree;
+    rq->forward_type = type;
+    rq->borrow_train_state = false;
+    rq->gs_mean3d = s->params[0];
+    rq->gs_logscale = s->params[1];
+    rq->gs_rotation = s->params[2];
+    rq->gs_opacity = s->params[3];
+    rq->gs_sh0 = s->params[4];
+    rq->gs_sh1 = s->sh_degree >= 1 ? s->params[5] : NULL;
+    rq->gs_sh2 = s->sh_degree >= 2 ? s->params[6] : NULL;
+    rq->gs_sh3 = s->sh_degree >= 3 ? s->params[7] : NULL;
+    rq->out_rgb = s->out_rgb;
+}
+
+/* Forward INFERENCE render into out_rgb (host CHW). */
+int refdrv_session_render(refdrv_session *s, float *out_rgb)
+{
+    gsx_render_forward_request rq;
+    refdrv_fill_forward(s, &rq, GSX_RENDER_FORWARD_TYPE_INFERENCE);
+    REF_CHECK(gsx_renderer_render(s->renderer, s->rctx, &rq));
+    REF_CHECK(gsx_tensor_download(s->out_rgb, out_rgb, (gsx_size_t)3 * s->width * s->height * 4));
+    return 0;
+}
+
+/* TRAIN forward + backward with a caller-supplied image gradient; downloads the parameter grads
+ * in field order (mean3d, logscale, rotation, opacity, sh0[, sh1..]). */
+int refdrv_session_render_backward(refdrv_session *s, const float *grad_rgb, float *out_rgb, float **grad_out)
+{
+    gsx_render_forward_request rq;
+    gsx_render_backward_request bq;
+    refdrv_fill_forward(s, &rq, GSX_RENDER_FORWARD_TYPE_TRAIN);
+    REF_CHECK(gsx_renderer_render(s->renderer, s->rctx, &rq));
+    REF_CHECK(gsx_tensor_upload(s->grad_rgb, grad_rgb, (gsx_size_t)3 * s->width * s->height * 4));
+    memset(&bq, 0, sizeof(bq));
+    bq.grad_rgb = s->grad_rgb;
+    bq.grad_gs_mean3d = s->grads[0];
+    bq.grad_gs_logscale = s->grads[1];
+    bq.grad_gs_rotation = s->grads[2];
+    bq.grad_gs_opacity = s->grads[3];
+    bq.grad_gs_sh0 = s->grads[4];
+    bq.grad_gs_sh1 = s->sh_degree >= 1 ? s->grads[5] : NULL;
+    bq.grad_gs_sh2 = s->sh_degree >= 2 ? s->grads[6] : NULL;
+    bq.grad_gs_sh3 = s->sh_degree >= 3 ? s->grads[7] : NULL;
+    REF_CHECK(gsx_renderer_backward(s->renderer, s->rctx, &bq));
+    REF_CHECK(gsx_tensor_download(s->out_rgb, out_rgb, (gsx_size_t)3 * s->width * s->height * 4));
+    for(int f = 0; f < s->n_fields; ++f) {
+        gsx_size_t bytes = 0;
+        REF_CHECK(gsx_tensor_get_size_bytes(s->grads[f], &bytes));
+        REF_CHECK(gsx_tensor_download(s->grads[f], grad_out[f], bytes));
+    }
+    return 0;
+}
+
+/* One training step exactly as gsx-runtime.c:1413-1536 orders it (without ADC):
+ * zero grads, render TRAIN, loss forward L1 (0.8) and SSIM (0.2), loss backward both,
+ * render backward, Adam over every group.  Returns 0 and the wall seconds in *seconds. */
+int refdrv_session_step(refdrv_session *s, float l1_weight, float ssim_weight, double *seconds)
+{
+    struct timespec t0, t1;
+    gsx_render_forward_request rq;
+    gsx_render_backward_request bq;
+    gsx_loss_forward_request lf;
+    gsx_loss_backward_request lb;
+    gsx_optim_step_request oq;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    for(int f = 0; f < s->n_fields; ++f) REF_CHECK(gsx_tensor_set_zero(s->grads[f]));
+    REF_CHECK(gsx_tensor_set_zero(s->loss_map));
+    REF_CHECK(gsx_tensor_set_zero(s->grad_rgb));
+    refdrv_fill_forward(s, &rq, GSX_RENDER_FORWARD_TYPE_TRAIN);
+    REF_CHECK(gsx_renderer_render(s->renderer, s->rctx, &rq));
+    memset(&lf, 0, sizeof(lf));
+    lf.prediction = s->out_rgb;
+    lf.target = s->target;
+    lf.loss_map_accumulator = s->loss_map;
+    lf.train = true;
+    lf.scale = l1_weight;
+    REF_CHECK(gsx_loss_forward(s->l1, s->l1_ctx, &lf));
+    lf.scale = ssim_weight;
+    REF_CHECK(gsx_loss_forward(s->ssim, s->ssim_ctx, &lf));
+    memset(&lb, 0, sizeof(lb));
+    lb.grad_prediction_accumulator = s->grad_rgb;
+    lb.scale = l1_weight;
+    REF_CHECK(gsx_loss_backward(s->l1, s->l1_ctx, &lb));
+    lb.scale = ssim_weight;
+    REF_CHECK(gsx_loss_backward(s->ssim, s->ssim_ctx, &lb));
+    memset(&bq, 0, sizeof(bq));
+    bq.grad_rgb = s->grad_rgb;
+    bq.grad_gs_mean3d = s->grads[0];
+    bq.grad_gs_logscale = s->grads[1];
+    bq.grad_gs_rotation = s->grads[2];
+    bq.grad_gs_opacity = s->grads[3];
+    bq.grad_gs_sh0 = s->grads[4];
+    bq.grad_gs_sh1 = s->sh_degree >= 1 ? s->grads[5] : NULL;
+    bq.grad_gs_sh2 = s->sh_degree >= 2 ? s->grads[6] : NULL;
+    bq.grad_gs_sh3 = s->sh_degree >= 3 ? s->grads[7] : NULL;
+    REF_CHECK(gsx_renderer_backward(s->renderer, s->rctx, &bq));
+    memset(&oq, 0, sizeof(oq));
+    oq.force_all = true;
+    REF_CHECK(gsx_optim_step(s->optim, &oq));
+    REF_CHECK(gsx_backend_major_stream_sync(refdrv_backend));
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    if(seconds) *seconds = (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
+    return 0;
+}
+
+/* Download the current parameter, loss map or rendered image. which: 0..7 params, 8 out_rgb, 9 loss_map, 10 grad_rgb */
+int refdrv_session_download(refdrv_session *s, int which, float *dst)
+{
+    gsx_tensor_t t = which < 8 ? s->params[which] : (which == 8 ? s->out_rgb : (which == 9 ? s->loss_map : s->grad_rgb));
+    gsx_size_t bytes = 0;
+    REF_CHECK(gsx_tensor_get_size_bytes(t, &bytes));
+    REF_CHECK(gsx_tensor_download(t, dst, bytes));
+    return 0;
+}
+
+/* ---------------------------------------------------------------- standalone loss and Adam */
+/* algorithm: 0 L1, 1 MSE, 2 SSIM; normalization 0 MEAN, 1 SUM; shape [outer, C, H, W] CHW.
+ * loss_map and grad are read, accumulated into by the reference, and written back. */
+int refdrv_loss(int algorithm, int normalization, int outer, int channels, int height, int width, const float *pred,
+                const float *target, float scale, float *loss_map, float *grad)
+{
+    gsx_arena_t arena = NULL;
+    gsx_loss_t loss = NULL;
+    gsx_loss_context_t ctx = NULL;
+    gsx_tensor_t tp = NULL, tt = NULL, tl = NULL, tg = NULL;
+    gsx_loss_desc ld;
+    gsx_loss_forward_request lf;
+    gsx_loss_backward_request lb;
+    const gsx_size_t n = (gsx_size_t)outer * channels * height * width;
+    int shape[4] = { outer, channels, height, width };
+    int rc = 0;
+    if(refdrv_arena(&arena, n * 4 * 4 + 4096)) return 1;
+    if((rc = refdrv_tensor(arena, &tp, 4, shape, pred)) != 0) return rc;
+    if((rc = refdrv_tensor(arena, &tt, 4, shape, target)) != 0) return rc;
+    if((rc = refdrv_tensor(arena, &tl, 4, shape, loss_map)) != 0) return rc;
+    if((rc = refdrv_tensor(arena, &tg, 4, shape, grad)) != 0) return rc;
+    memset(&ld, 0, sizeof(ld));
+    ld.algorithm = (gsx_loss_algorithm)algorithm;
+    ld.grad_normalization = (gsx_loss_grad_normalization_type)normalization;
+    REF_CHECK(gsx_loss_init(&loss, refdrv_backend, &ld));
+    REF_CHECK(gsx_loss_context_init(&ctx, loss));
+    memset(&lf, 0, sizeof(lf));
+    lf.prediction = tp;
+    lf.target = tt;
+    lf.loss_map_accumulator = tl;
+    lf.train = true;
+    lf.scale = scale;
+    REF_CHECK(gsx_loss_forward(loss, ctx, &lf));
+    memset(&lb, 0, sizeof(lb));
+    lb.grad_prediction_accumulator = tg;
+    lb.scale = scale;
+    REF_CHECK(gsx_loss_backward(loss, ctx, &lb));
+    REF_CHECK(gsx_tensor_download(tl, loss_map, n * 4));
+    REF_CHECK(gsx_tensor_download(tg, grad, n * 4));
+    gsx_tensor_free(tg);
+    gsx_tensor_free(tl);
+    gsx_tensor_free(tt);
+    gsx_tensor_free(tp);
+    gsx_loss_context_free(ctx);
+    gsx_loss_free(loss);
+    gsx_arena_free(arena);
+    return 0;
+}
+
+/* `steps` Adam steps on one [n] group with a fixed gradient; param/m state returned in place. */
+int refdrv_adam(int64_t n, float *param, const float *grad, int steps, float lr, float beta1, float beta2, float eps,
+                float weight_decay, float max_grad)
+{
+    gsx_arena_t arena = NULL;
+    gsx_tensor_t tp = NULL, tg = NULL;
+    gsx_optim_t optim = NULL;
+    gsx_optim_param_group_desc g;
+    gsx_optim_desc od;
+    gsx_optim_step_request oq;
+    int shape[1] = { (int)n };
+    int rc = 0;
+    if(refdrv_arena(&arena, (gsx_size_t)n * 8 + 4096)) return 1;
+    if((rc = refdrv_tensor(arena, &tp, 1, shape, param)) != 0) return rc;
+    if((rc = refdrv_tensor(arena, &tg, 1, shape, grad)) != 0) return rc;
+    memset(&g, 0, sizeof(g));
+    g.role = GSX_OPTIM_PARAM_ROLE_MEAN3D;
+    g.parameter = tp;
+    g.gradient = tg;
+    g.learning_rate = lr;
+    g.beta1 = beta1;
+    g.beta2 = beta2;
+    g.epsilon = eps;
+    g.weight_decay = weight_decay;
+    g.max_grad = max_grad;
+    memset(&od, 0, sizeof(od));
+    od.algorithm = GSX_OPTIM_ALGORITHM_ADAM;
+    od.param_groups = &g;
+    od.param_group_count = 1;
+    REF_CHECK(gsx_optim_init(&optim, refdrv_backend, &od));
+    memset(&oq, 0, sizeof(oq));
+    oq.force_all = true;
+    for(int s = 0; s < steps; ++s) REF_CHECK(gsx_optim_step(optim, &oq));
+    REF_CHECK(gsx_tensor_download(tp, param, (gsx_size_t)n * 4));
+    gsx_optim_free(optim);
+    gsx_tensor_free(tg);
+    gsx_tensor_free(tp);
+    gsx_arena_free(arena);
+    return 0;
+}
