@@ -1,0 +1,307 @@
+"""Benchmark of the GSX hot path on B200: the config-3 training step (3M Gaussians, 1245x825).
+
+One step = render TRAIN -> fused L1+SSIM -> render backward -> gradient all-reduce (N > 1) ->
+fused Adam, one view per GPU per step (data parallel over views, the Gaussian set replicated).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+For N > 1 it is launched with torch.distributed.run (one rank per GPU, NCCL).  Rank 0 prints ONE
+JSON line.  `value` = views/s of the whole job with every input resident in HBM (device-timed, max
+over ranks); `e2e` = the same through the public API with the step's target image copied from
+pinned host memory and the loss read back to the host inside the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd iters/s at 3M Gaussians 1245x825 (1/2/4/8 GPU); fwd Mpix/s"
+UNIT = "views/s"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region (200 ms period)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def reference_arm(args):
+    """The reference's own CPU implementation (built from its sources) on the box's host cores."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import ref_bench
+    cfg = {"workload": "config 3: 3M Gaussians (2M volume + 1M slab), 1245x825, 8 views, L1+SSIM, Adam",
+           "gaussians": 3_000_000, "width": 1245, "height": 825, "views_per_step": world}
+    if not ref_bench.available():
+        print(json.dumps({"impl": "reference", "metric": METRIC,
+                          "unavailable": "reference CPU library not built (oracle/_ref missing)"}))
+        return
+    r = ref_bench.run(args.steps, args.warmup)
+    sample = (f"each step trains the reference CPU backend on a seeded 1/16 sample ({r['n_sample']} of "
+              f"{r['n_full']}) of the config-3 Gaussians at the full 1245x825 view, one process per core "
+              f"({r['processes']} x {args.steps} steps, {r['seconds_per_step']:.2f} s/step); value scaled by "
+              f"the Gaussian fraction (the full set exceeds the reference CPU renderer's 2 GiB scratch limit)")
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / r["value"],
+                      "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                      "data": "synthetic (seeded config-3 generator)", "config": cfg,
+                      "cpu_baseline": {"value": r["value"], "unit": UNIT, "cores": r["processes"], "kind": "reference",
+                                       "sample": sample, "cpu": r["cpu"]},
+                      "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import gsx_b200 as gb
+    from gsx_b200 import scenes
+    from gsx_b200.train import GaussianModel, Trainer
+
+    world, rank, local = _dist_init()
+    dev = f"cuda:{local}"
+    group = dist.group.WORLD if world > 1 else None
+
+    scene = scenes.config3_scene(0)
+    cams = scenes.config3_cameras()
+    n = scene["mean3d"].shape[0]
+    # targets: renders of the seeded teacher model from the 8 views (computed once, not timed)
+    teacher = {k: torch.from_numpy(v).to(dev) for k, v in scenes.teacher(scene).items()}
+    tctx = gb.RenderContext(local)
+    targets = []
+    for c in cams:
+        t = torch.empty((3, c.height, c.width), device=dev)
+        gb.Renderer(c.width, c.height).render(tctx, teacher, c, t, forward_type=gb.FORWARD_INFERENCE)
+        targets.append(t)
+    tctx.close()
+    del teacher
+    model = GaussianModel(scene, dev)
+    W, H = cams[0].width, cams[0].height
+    trainer = Trainer(model, W, H, group=group, device=dev)
+
+    def view(step):
+        return (rank + step * world) % len(cams)
+
+    for s in range(args.warmup):
+        trainer.step(cams[view(s)], targets[view(s)])
+    trainer.ctx.check()
+    stats = trainer.ctx.stats()
+
+    # ---- device-timed region: inputs resident in HBM (params/grads/moments 3M x 56 B x 4 > L2) ----
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    le = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ae = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    trainer.ctx.set_profiling(True)
+    trainer.ctx.read_profile()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for s in range(args.steps):
+            c = cams[view(args.warmup + s)]
+            trainer.step(c, targets[view(args.warmup + s)], events=(le[s], ae[s]))
+        e1.record(stream)
+        torch.cuda.synchronize()
+    trainer.ctx.set_profiling(False)
+    prof = trainer.ctx.read_profile()
+    ms = e0.elapsed_time(e1)
+    loss_ms = sum(a.elapsed_time(b) for a, b in le) / args.steps
+    adam_ms = sum(a.elapsed_time(b) for a, b in ae) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms_max = float(t.item())
+    trainer.ctx.check()
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- end to end through the public API: H2D target + D2H loss every step ----
+    host_targets = [tt.cpu().pin_memory() for tt in targets]
+    dev_target = torch.empty_like(targets[0])
+    loss_host = torch.zeros(1, dtype=torch.float32).pin_memory()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for s in range(args.steps):
+        v = view(args.warmup + args.steps + s)
+        dev_target.copy_(host_targets[v], non_blocking=True)
+        loss = trainer.step(cams[v], dev_target)
+        loss_host.copy_(loss, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    t2 = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_value = world * args.steps / (float(t2.item()) / 1000.0)
+    h2d = dev_target.numel() * 4
+    trainer.ctx.check()
+
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        hbm = float(peaks["hbm_gbs"])
+        stage_avg = {k: (v[0] / v[1] if v[1] else 0.0) for k, v in prof.items()}
+        stage_avg["l1_ssim"] = loss_ms
+        stage_avg["adam"] = adam_ms
+        dom = max(stage_avg, key=stage_avg.get)
+        I = stats["n_instances"]
+        B = stats["n_buckets"]
+        P = W * H
+        V = stats["n_visible"]
+        algo_bytes = {
+            # per launch, see DESIGN.md "algorithmic bytes"
+            "preprocess": 56 * n + 52 * V + 4 * n,
+            "emit": 48 * V + 12 * I,
+            "sort": 24 * I * ((32 + (((W + 15) // 16) * ((H + 15) // 16) - 1).bit_length() + 7) // 8) + 8 * I,
+            "ranges": 8 * I + 16 * ((W + 15) // 16) * ((H + 15) // 16),
+            "blend_forward": 4 * I + 48 * I + 28 * P + 16 * 256 * B,
+            "blend_backward": 4 * I + 48 * I + 28 * P + 16 * 256 * B + 48 * I,
+            "preprocess_backward": 56 * n + 48 * V * 2 + 44 * n,
+            "l1_ssim": 16 * 3 * P,
+            "adam": 28 * 14 * n,
+        }
+        dom_ms = stage_avg[dom]
+        achieved = algo_bytes[dom] / (dom_ms / 1000.0) / 1e9
+        n_tiles = ((W + 15) // 16) * ((H + 15) // 16)
+        sort_passes = (32 + (n_tiles - 1).bit_length() + 7) // 8
+        # preprocess, emit, histogram + one onesweep per pass, ranges + bucket scan, blend fwd,
+        # fused loss, blend bwd, preprocess bwd, fused Adam
+        kernel_launches = 1 + 1 + (1 + sort_passes) + 2 + 1 + 1 + 1 + 1 + 1
+        cpu_baseline = None
+        if not args.no_cpu_baseline and world == 1:
+            from oracle import ref_bench
+            if ref_bench.available():
+                r = ref_bench.run(1, 0)
+                cpu_baseline = {"value": r["value"], "unit": UNIT, "cores": r["processes"], "kind": "reference",
+                                "sample": (f"1 reference-CPU training step per process on a seeded 1/16 sample "
+                                           f"({r['n_sample']} Gaussians) of the config-3 scene at 1245x825, "
+                                           f"{r['processes']} processes ({r['seconds_per_step']:.2f} s/step), "
+                                           f"scaled by the Gaussian fraction"), "cpu": r["cpu"]}
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config-3 generator, teacher-render targets)",
+            "config": {"workload": "config 3 training step: 3M Gaussians (2M volume + 1M z-slab), 1245x825, "
+                                   "one view per GPU per step, L1(0.8)+SSIM(0.2), per-role Adam",
+                       "gaussians": n, "width": W, "height": H, "views_per_step": world,
+                       "parallelism": f"dp{world} (views), NCCL all-reduce of 14 f32/Gaussian",
+                       "l2": "inputs larger than L2 (params+grads+moments = 672 MB)",
+                       "visible": V, "instances": I, "buckets": B},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+            "gpu_launches": kernel_launches * args.steps,
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None, "peak_source": peak_kind,
+                         "avg_ms": dom_ms, "algorithmic_bytes": algo_bytes[dom]},
+            "stages_ms": {k: round(v, 4) for k, v in stage_avg.items()},
+            "cpu_baseline": cpu_baseline,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(out))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

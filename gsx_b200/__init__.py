@@ -106,6 +106,18 @@ class RenderContext:
                                           _stream_handle(stream)))
         return dict(n_visible=v.value, n_instances=i.value, n_buckets=b.value)
 
+    def set_profiling(self, enable: bool = True):
+        """Record per-stage CUDA events on the launching stream (see read_profile)."""
+        check(lib().gsx_b200_context_set_profiling(self.handle, 1 if enable else 0))
+
+    def read_profile(self) -> dict:
+        """{stage: (total_ms, launches)} since the last read; synchronises."""
+        from ._capi import STAGES
+        ms = (ctypes.c_float * len(STAGES))()
+        cnt = (ctypes.c_int32 * len(STAGES))()
+        check(lib().gsx_b200_context_read_profile(self.handle, ms, cnt))
+        return {s: (float(ms[i]), int(cnt[i])) for i, s in enumerate(STAGES)}
+
     def view(self) -> RenderView:
         v = RenderView()
         check(lib().gsx_b200_render_get_view(self.handle, ctypes.byref(v)))
@@ -150,16 +162,16 @@ class Renderer:
 
 
 def l1_ssim(prediction, target, loss_map, grad, l1_weight=0.8, ssim_weight=0.2, normalization="mean",
-            loss_sum=None, stream=None):
+            loss_sum=None, overwrite=False, stream=None):
     """The fused training loss: L1 and SSIM forward and backward in one kernel.
 
     Same result as GSX's L1 loss then SSIM loss forward, then L1 then SSIM backward
-    (gsx-runtime.c:1496-1510): loss_map and grad are accumulated into.  MEAN normalisation divides
+    (gsx-runtime.c:1496-1510): loss_map and grad are accumulated into (written when overwrite=True).  MEAN normalisation divides
     the gradient scales by numel(prediction) (gsx-tensor-helpers.h:236-244)."""
     n = prediction.numel()
     gs = (1.0 / n) if normalization == "mean" else 1.0
     planes = n // (prediction.shape[-1] * prediction.shape[-2])
-    mode = 1 | (2 if grad is not None else 0) | 4
+    mode = 1 | (2 if grad is not None else 0) | 4 | (8 if overwrite else 0)
     l1g = float(_f32(l1_weight) / _f32(n)) if normalization == "mean" else l1_weight
     ssg = float(_f32(ssim_weight) / _f32(n)) if normalization == "mean" else ssim_weight
     del gs

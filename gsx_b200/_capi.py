@@ -11,6 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libgsx_b200.so")
 
+STAGES = ("preprocess", "emit", "sort", "ranges", "blend_forward", "blend_backward", "preprocess_backward")
 SUCCESS, OUT_OF_MEMORY, INVALID_ARGUMENT, OUT_OF_RANGE, INVALID_STATE, NOT_SUPPORTED, UNKNOWN = 0, 1, 2, 3, 4, 5, 255
 ERROR_NAMES = {0: "SUCCESS", 1: "OUT_OF_MEMORY", 2: "INVALID_ARGUMENT", 3: "OUT_OF_RANGE", 4: "INVALID_STATE",
                5: "NOT_SUPPORTED", 255: "UNKNOWN"}
@@ -70,6 +71,9 @@ SIGNATURES = {
                                              ctypes.c_void_p]),
     "gsx_b200_render_get_view": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(RenderView)]),
     "gsx_b200_context_check": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "gsx_b200_context_set_profiling": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "gsx_b200_context_read_profile": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_float),
+                                                     ctypes.POINTER(ctypes.c_int32)]),
     "gsx_b200_loss_l1_ssim": (ctypes.c_int, [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
                                              ctypes.c_int32, ctypes.c_float, ctypes.c_float, ctypes.c_float,

@@ -2,8 +2,8 @@
  * C ABI of gsx-b200 (include/gsx_b200.h): context and scratch management, and the orchestration
  * of the render forward/backward pipeline on one stream.
  *
- * Forward: preprocess+scan (1 kernel) -> read the instance total (the only host synchronisation)
- * -> emit keys -> radix sort (histogram + one onesweep kernel per 8-bit digit) -> tile ranges and
+ * Forward: preprocess (+ one-CTA scan of block totals) -> read the instance total (the only host
+ * synchronisation) -> emit keys (+ in-block scan into offsets) -> radix sort (histogram + one onesweep kernel per 8-bit digit) -> tile ranges and
  * bucket scan -> blend+compose.  Backward: blend backward -> preprocess backward.
  * Scratch grows on demand with cudaMalloc (outside any stream capture) and is never shrunk.
  */
@@ -18,6 +18,7 @@
 
 namespace {
 
+constexpr int kProfileSlots = 256;
 thread_local std::string g_last_error;
 
 int fail(int code, const std::string &msg)
@@ -123,7 +124,7 @@ CameraParams make_camera(const gsx_b200_camera &c)
 struct gsx_b200_context {
     int device = 0;
     /* per primitive */
-    DevBuf rec, offsets, lookback, grad_acc;
+    DevBuf rec, offsets, counts, block_sums, grad_acc;
     int64_t prim_cap = 0;
     /* per instance */
     DevBuf keys, vals, sort_scratch;
@@ -142,7 +143,34 @@ struct gsx_b200_context {
     uint64_t bucket_cap = 0;
     int n_tiles = 0;
     int keys_in_b = 0;
+    /* per-stage event timing (gsx_b200_context_set_profiling) */
+    bool profiling = false;
+    cudaEvent_t ev[GSX_B200_STAGE_COUNT][kProfileSlots][2];
+    int ev_count[GSX_B200_STAGE_COUNT] = {};
+    bool ev_created = false;
 };
+
+namespace {
+
+struct StageTimer {
+    gsx_b200_context *ctx;
+    int stage;
+    cudaStream_t stream;
+    int slot;
+    StageTimer(gsx_b200_context *c, int s, cudaStream_t st) : ctx(c), stage(s), stream(st), slot(-1)
+    {
+        if(ctx->profiling && ctx->ev_count[stage] < kProfileSlots) {
+            slot = ctx->ev_count[stage]++;
+            cudaEventRecord(ctx->ev[stage][slot][0], stream);
+        }
+    }
+    ~StageTimer()
+    {
+        if(slot >= 0) cudaEventRecord(ctx->ev[stage][slot][1], stream);
+    }
+};
+
+} // namespace
 
 extern "C" {
 
@@ -182,10 +210,16 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     if(ctx == nullptr) return 0;
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
-    DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->lookback, &ctx->grad_acc, &ctx->keys, &ctx->vals,
+    DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
                       &ctx->bucket_tile, &ctx->snap, &ctx->words };
     for(DevBuf *b : all) release(*b);
+    if(ctx->ev_created)
+        for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
+            for(int k = 0; k < kProfileSlots; ++k) {
+                cudaEventDestroy(ctx->ev[s][k][0]);
+                cudaEventDestroy(ctx->ev[s][k][1]);
+            }
     if(ctx->host_words) cudaFreeHost(ctx->host_words);
     delete ctx;
     return 0;
@@ -230,27 +264,29 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
             ctx->prim_cap = (int64_t)(ctx->grad_acc.bytes / (3 * sizeof(float4)));
     }
     if(int rc = ensure(ctx->offsets, sizeof(uint32_t) * (size_t)(n + 1))) return rc;
-    if(int rc = ensure(ctx->lookback, sizeof(unsigned long long) * (size_t)(pblocks + 1))) return rc;
+    if(int rc = ensure(ctx->counts, sizeof(uint32_t) * (size_t)(n + 1))) return rc;
+    if(int rc = ensure(ctx->block_sums, sizeof(uint32_t) * (size_t)(pblocks + 1))) return rc;
     if(int rc = ensure(ctx->ranges, sizeof(uint2) * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->bucket_offsets, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->tile_max, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->pix, sizeof(float4) * P)) return rc;
     uint32_t *words = (uint32_t *)ctx->words.ptr;
     uint32_t *offsets = (uint32_t *)ctx->offsets.ptr;
+    uint32_t *counts = (uint32_t *)ctx->counts.ptr;
+    uint32_t *block_sums = (uint32_t *)ctx->block_sums.ptr;
 
     uint64_t total = 0;
     if(n > 0) {
-        GSX_CUDA_TRY(cudaMemsetAsync(ctx->lookback.ptr, 0, sizeof(unsigned long long) * (size_t)pblocks, stream), "memset");
-        GSX_CUDA_TRY(cudaMemsetAsync(words + 1, 0, sizeof(uint32_t), stream), "memset");
-        GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2, g->sh3,
-                                           sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, offsets,
-                                           (uint32_t *)ctx->lookback.ptr, words + 1, words, stream),
-                     "preprocess launch");
-        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, offsets + n, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "D2H");
-        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 1, words, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream), "D2H");
+        {
+            StageTimer st0(ctx, 0, stream);
+            GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2,
+                                               g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, block_sums,
+                                               stream),
+                         "preprocess launch");
+        }
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
+                     "D2H");
         GSX_CUDA_TRY(cudaStreamSynchronize(stream), "preprocess");
-        if(ctx->host_words[1] & GSX_FLAG_LOOKBACK_TIMEOUT)
-            return fail(GSX_B200_UNKNOWN, "preprocess scan lookback timed out");
         total = ctx->host_words[0];
     } else {
         GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
@@ -268,26 +304,36 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     uint32_t *vals_a = (uint32_t *)ctx->vals.ptr;
     uint32_t *vals_b = vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t));
     int in_b = 0;
-    if(total > 0) {
-        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, offsets, cam.grid_w, keys_a, vals_a, total, words,
-                                     stream),
+    if(n > 0) {
+        StageTimer st(ctx, 1, stream);
+        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, block_sums, offsets, cam.grid_w, keys_a,
+                                     vals_a, total, words, stream),
                      "emit launch");
+    }
+    if(total > 0) {
         int tile_bits = 0;
         while((1 << tile_bits) < n_tiles) ++tile_bits;
+        StageTimer st(ctx, 2, stream);
         GSX_CUDA_TRY(gsx_launch_sort_pairs(keys_a, vals_a, keys_b, vals_b, total, 0, 32 + tile_bits, ctx->sort_scratch.ptr,
                                            ctx->sort_scratch.bytes, words, &in_b, stream),
                      "sort launch");
     }
     const unsigned long long *keys = in_b ? keys_b : keys_a;
     const uint32_t *vals = in_b ? vals_b : vals_a;
+    {
+    StageTimer st3(ctx, 3, stream);
     GSX_CUDA_TRY(gsx_launch_tile_ranges(keys, total, n_tiles, (uint2 *)ctx->ranges.ptr, (uint32_t *)ctx->bucket_offsets.ptr,
                                         (uint32_t *)ctx->bucket_tile.ptr, bucket_cap, words, stream),
                  "ranges launch");
+    }
+    {
+    StageTimer st4(ctx, 4, stream);
     GSX_CUDA_TRY(gsx_launch_blend_forward(camera->width, camera->height, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
                                           (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
                                           out_rgb, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
-                                          (float4 *)ctx->snap.ptr, stream),
+                                          (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr, stream),
                  "blend launch");
+    }
     ctx->keys_in_b = in_b;
     ctx->bucket_cap = bucket_cap;
     ctx->n_tiles = n_tiles;
@@ -322,6 +368,7 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
     const uint32_t *vals_a = (const uint32_t *)ctx->vals.ptr;
     const uint32_t *vals = ctx->keys_in_b ? vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t)) : vals_a;
     if(ctx->n_instances > 0) {
+        StageTimer st(ctx, 5, stream);
         GSX_CUDA_TRY(gsx_launch_blend_backward(ctx->cam.width, ctx->cam.height, ctx->cam.grid_w, (const uint2 *)ctx->ranges.ptr,
                                                (const uint32_t *)ctx->bucket_offsets.ptr,
                                                (const uint32_t *)ctx->bucket_tile.ptr, ctx->bucket_cap, ctx->n_tiles, vals,
@@ -330,8 +377,9 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
                                                (float4 *)ctx->grad_acc.ptr, n, stream),
                      "blend backward launch");
     }
+    StageTimer st6(ctx, 6, stream);
     GSX_CUDA_TRY(gsx_launch_preprocess_backward(ctx->g.mean3d, ctx->g.rotation, ctx->g.logscale, ctx->g.sh1, ctx->g.sh2,
-                                                ctx->g.sh3, ctx->sh_degree, n, ctx->cam, (const uint32_t *)ctx->offsets.ptr,
+                                                ctx->g.sh3, ctx->sh_degree, n, ctx->cam, (const uint32_t *)ctx->counts.ptr,
                                                 (float4 *)ctx->grad_acc.ptr, gr->mean3d, gr->rotation, gr->logscale,
                                                 gr->opacity, gr->sh0, gr->sh1, gr->sh2, gr->sh3, stream),
                  "preprocess backward launch");
@@ -410,6 +458,42 @@ int gsx_b200_context_check(gsx_b200_context *ctx, void *stream_)
     return 0;
 }
 
+int gsx_b200_context_set_profiling(gsx_b200_context *ctx, int enable)
+{
+    if(ctx == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx must be non-null");
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    if(enable && !ctx->ev_created) {
+        for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
+            for(int k = 0; k < kProfileSlots; ++k) {
+                GSX_CUDA_TRY(cudaEventCreate(&ctx->ev[s][k][0]), "cudaEventCreate");
+                GSX_CUDA_TRY(cudaEventCreate(&ctx->ev[s][k][1]), "cudaEventCreate");
+            }
+        ctx->ev_created = true;
+    }
+    ctx->profiling = enable != 0;
+    return 0;
+}
+
+int gsx_b200_context_read_profile(gsx_b200_context *ctx, float *total_ms, int32_t *launches)
+{
+    if(ctx == nullptr || total_ms == nullptr || launches == nullptr)
+        return fail(GSX_B200_INVALID_ARGUMENT, "ctx, total_ms and launches must be non-null");
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s) {
+        float sum = 0.0f;
+        for(int k = 0; k < ctx->ev_count[s]; ++k) {
+            GSX_CUDA_TRY(cudaEventSynchronize(ctx->ev[s][k][1]), "cudaEventSynchronize");
+            float ms = 0.0f;
+            GSX_CUDA_TRY(cudaEventElapsedTime(&ms, ctx->ev[s][k][0], ctx->ev[s][k][1]), "cudaEventElapsedTime");
+            sum += ms;
+        }
+        total_ms[s] = sum;
+        launches[s] = ctx->ev_count[s];
+        ctx->ev_count[s] = 0;
+    }
+    return 0;
+}
+
 int gsx_b200_loss_l1_ssim(int mode, const float *prediction, const float *target, float *loss_map, float *grad,
                           float *loss_sum, int64_t planes, int32_t height, int32_t width, float l1_scale, float ssim_scale,
                           float l1_grad_scale, float ssim_grad_scale, void *stream)
@@ -417,8 +501,9 @@ int gsx_b200_loss_l1_ssim(int mode, const float *prediction, const float *target
     if(prediction == nullptr || target == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "prediction and target must be non-null");
     if((mode & 1) && loss_map == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "loss_map required by mode");
     if((mode & 2) && grad == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "grad required by mode");
-    if(mode != 1 && mode != 2 && mode != 3 && mode != 5 && mode != 7)
-        return fail(GSX_B200_OUT_OF_RANGE, "mode must be one of 1, 2, 3, 5, 7");
+    const int base_mode = mode & 7;
+    if((mode & ~15) != 0 || (base_mode != 1 && base_mode != 2 && base_mode != 3 && base_mode != 5 && base_mode != 7))
+        return fail(GSX_B200_OUT_OF_RANGE, "mode must be 1, 2, 3, 5 or 7, optionally with the overwrite bit 8");
     if(planes <= 0 || height <= 0 || width <= 0) return fail(GSX_B200_INVALID_ARGUMENT, "image shape must be positive");
     if(planes > INT32_MAX) return fail(GSX_B200_OUT_OF_RANGE, "too many planes");
     GSX_CUDA_TRY(gsx_launch_l1_ssim(mode, prediction, target, loss_map, grad, loss_sum, (int)planes, height, width, l1_scale,

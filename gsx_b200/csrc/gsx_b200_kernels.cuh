@@ -4,7 +4,8 @@
  * HBM layout of the per-frame render state (all owned by a gsx_b200_context):
  *   per primitive (capacity N):
  *     rec      PrimRec[N]   48 B: {mean2d.xy, conic.xy} {conic.z, opacity, rgb.rg} {rgb.b, depth, bx, by}
- *     offsets  u32[N+1]     exclusive prefix of the exact tile-overlap counts (0 = culled)
+ *     counts   u32[N]       exact tile-overlap count (0 = culled); block_sums u32[N/256+1]
+ *     offsets  u32[N+1]     exclusive prefix of the counts (written by the emission kernel)
  *     grad_acc float4[3N]   per-primitive 2-D gradient accumulators of the blend backward
  *   per instance (capacity I): keys u64[2I], values u32[2I] (double-buffered radix sort)
  *   per tile (T):   ranges uint2[T], bucket_offsets u32[T] (inclusive), tile_max u32[T]
@@ -65,6 +66,20 @@ __device__ __forceinline__ void gsx_st_release(uint32_t *p, uint32_t v)
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+/* Relaxed (fence-free) device-scope accesses for decoupled-lookback status words whose value is
+ * self-contained (no other data is published through them). */
+__device__ __forceinline__ uint32_t gsx_ld_relaxed(const uint32_t *p)
+{
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void gsx_st_relaxed(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ uint64_t gsx_ld_acquire64(const unsigned long long *p)
 {
     unsigned long long v;
@@ -110,11 +125,10 @@ struct RenderScratch;
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
-                                  uint32_t *offsets, uint32_t *lookback, uint32_t *tile_counter, uint32_t *flags,
-                                  cudaStream_t stream);
-cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *offsets, int grid_w,
-                            unsigned long long *keys, uint32_t *vals, uint64_t capacity, uint32_t *flags,
-                            cudaStream_t stream);
+                                  uint32_t *counts, uint32_t *block_sums, cudaStream_t stream);
+cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *block_offsets,
+                            uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
+                            uint32_t *flags, cudaStream_t stream);
 size_t gsx_sort_scratch_bytes(uint64_t capacity);
 cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
                                   uint32_t *vals_b, uint64_t count, int begin_bit, int end_bit, void *scratch,
@@ -125,7 +139,7 @@ cudaError_t gsx_launch_tile_ranges(const unsigned long long *keys, uint64_t coun
 cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max,
-                                     float4 *snap, cudaStream_t stream);
+                                     float4 *snap, uint32_t *bucket_tile, cudaStream_t stream);
 cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const uint2 *ranges,
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
                                       int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,
@@ -133,7 +147,7 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const u
                                       float4 *grad_acc, int64_t n, cudaStream_t stream);
 cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rotation, const float *logscale,
                                            const float *sh1, const float *sh2, const float *sh3, int sh_degree,
-                                           int64_t n, const CameraParams &cam, const uint32_t *offsets,
+                                           int64_t n, const CameraParams &cam, const uint32_t *counts,
                                            float4 *grad_acc, float *g_mean3d, float *g_rotation, float *g_logscale,
                                            float *g_opacity, float *g_sh0, float *g_sh1, float *g_sh2, float *g_sh3,
                                            cudaStream_t stream);

@@ -1,18 +1,24 @@
 /*
- * Reverse-mode blend: one warp per 32-instance bucket, one instance per lane, walking the
- * tile's 256 pixels with per-pixel state handed lane to lane.
+ * Reverse-mode blend.  Gradient rules of fastgs/kernels_backward.cuh:484-730 (blend_backward_cu2,
+ * after Taming-3DGS): every pixel of the tile starts each 32-instance bucket from the forward
+ * snapshot (colour and transmittance before the bucket) and the composed image; fragments at or
+ * beyond the pixel's last contributor are skipped; sigma is clamped at 0 (no 1/255 skip in the
+ * backward), alpha at 0.999 with no opacity gradient when saturated, (1 - alpha) floored at 1e-4
+ * in the division; buckets at or beyond the tile's maximum contributor are skipped.
  *
- * Follows fastgs/kernels_backward.cuh:484-730 (blend_backward_cu2, after Taming-3DGS) for the
- * gradient rules: the state of each pixel starts from the forward snapshot taken before the
- * bucket (colour, transmittance) and from the composed image; fragments at or beyond the pixel's
- * last contributor are skipped; sigma is clamped at 0 (no 1/255 skip in the backward), alpha at
- * 0.999 with no opacity gradient when saturated, and (1 - alpha) is floored at 1e-4 in the
- * division.  Buckets at or beyond the tile's maximum contributor are skipped.
- *
- * B200 choices: the four 2-D gradient groups of an instance are accumulated in registers over all
- * 256 pixels and flushed with two 16-byte vector atomics (red.global.add.v4.f32) plus one scalar
- * atomic, instead of 9-11 scalar atomics; the grid is sized from the bucket capacity and buckets
- * past the device-side bucket count exit immediately (no host round trip for the count).
+ * B200 organisation (a different work decomposition from the reference's warp-per-bucket):
+ *   - a warp owns FOUR consecutive buckets (of the global bucket list, possibly from different
+ *     tiles); each bucket is an 8-lane segment and each lane owns 4 consecutive instances, so a
+ *     pixel's state walks 8 lanes instead of 32 (ramp of 7 steps instead of 31) and every state
+ *     hand-off (8 shuffles) is amortised over 4 fragment evaluations per lane;
+ *   - each segment prefetches its pixels' inputs (snapshot, composed colour, last contributor,
+ *     upstream gradient) 32 pixels ahead into shared memory with cp.async, and its first lane
+ *     feeds them into the chain, so segments from different tiles coexist in one warp;
+ *   - per pixel, (colour still to come) . (upstream gradient) is carried as one scalar (each
+ *     fragment lowers it by w * colour . gradient), so the hand-off is 6 values, not 8;
+ *   - the factors that are constant per instance (conic on the mean terms, colour clamp mask,
+ *     -1/2 on the conic terms, 1 - opacity) are applied once at the end, and each instance's
+ *     accumulators are flushed with two 16-byte vector atomics plus one scalar atomic.
  */
 #include "gsx_b200_kernels.cuh"
 
@@ -20,129 +26,210 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
+constexpr int kPerLane = 4;
 
-__global__ void __launch_bounds__(kThreads) blend_backward_kernel(
+struct Frag {
+    float mx, my, hcx, cy, hcz, op, r, g, b;
+};
+
+struct PixIn {
+    float4 snap; /* forward colour and transmittance before the bucket */
+    float4 img;  /* composed rgb, last-contributor bits */
+    float4 grad; /* upstream dL/drgb (x, y, z) */
+};
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+/* 2^x and 1/x on the special-function unit (approximate: the backward is compared with tolerance) */
+__device__ __forceinline__ float fast_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float fast_rcp(float x)
+{
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     int width, int height, int grid_w, int n_tiles, const uint2 *__restrict__ ranges,
     const uint32_t *__restrict__ bucket_offsets, const uint32_t *__restrict__ bucket_tile,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, const float4 *__restrict__ pix,
     const uint32_t *__restrict__ tile_max, const float4 *__restrict__ snap, const float *__restrict__ grad_rgb,
     float4 *__restrict__ grad_acc)
 {
-    __shared__ float4 s_up[kWarps][32]; /* grad r, g, b, last contributor bits */
-    __shared__ float4 s_lo[kWarps][32]; /* colour after (r, g, b), transmittance before bucket */
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    PixIn(*s_in)[4][2][32] = reinterpret_cast<PixIn(*)[4][2][32]>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint32_t bucket = blockIdx.x * kWarps + warp;
+    const int sub = lane & 7;
     const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
-    if(bucket >= n_buckets) return;
-    const uint32_t tile = bucket_tile[bucket];
-    const uint2 range = ranges[tile];
-    const int n_inst = (int)(range.y - range.x);
-    const uint32_t first = tile == 0 ? 0u : bucket_offsets[tile - 1];
-    const int tb = (int)(bucket - first);
-    if((uint32_t)tb * 32u >= tile_max[tile]) return;
-    const int tpi = tb * 32 + lane;
-    const bool valid_prim = tpi < n_inst;
-
-    uint32_t prim = 0;
-    float mx = 0.0f, my = 0.0f, cx = 0.0f, cy = 0.0f, cz = 0.0f, op = 0.0f;
-    float colr = 0.0f, colg = 0.0f, colb = 0.0f, fr = 0.0f, fg = 0.0f, fb = 0.0f;
-    if(valid_prim) {
-        prim = vals[range.x + tpi];
-        const PrimRec r = rec[prim];
-        mx = r.a.x - 0.5f;
-        my = r.a.y - 0.5f;
-        cx = r.a.z;
-        cy = r.a.w;
-        cz = r.b.x;
-        op = r.b.y;
-        colr = fmaxf(r.b.z, 0.0f);
-        colg = fmaxf(r.b.w, 0.0f);
-        colb = fmaxf(r.c.x, 0.0f);
-        fr = r.b.z >= 0.0f ? 1.0f : 0.0f;
-        fg = r.b.w >= 0.0f ? 1.0f : 0.0f;
-        fb = r.c.x >= 0.0f ? 1.0f : 0.0f;
+    const uint32_t bucket = ((uint32_t)blockIdx.x * kWarps + warp) * 4u + (uint32_t)(lane >> 3);
+    bool seg_active = bucket < n_buckets;
+    uint32_t tile = 0;
+    int n_inst = 0, tb = 0;
+    uint32_t inst0 = 0;
+    if(seg_active) {
+        tile = bucket_tile[bucket];
+        const uint2 range = ranges[tile];
+        inst0 = range.x;
+        n_inst = (int)(range.y - range.x);
+        tb = (int)(bucket - (tile == 0 ? 0u : bucket_offsets[tile - 1]));
+        seg_active = (uint32_t)tb * 32u < tile_max[tile];
     }
+    if(__ballot_sync(0xffffffffu, seg_active) == 0) return;
+
+    /* this lane's four instances */
+    Frag f[kPerLane];
+    uint32_t prim[kPerLane];
+    int tpi[kPerLane];
+#pragma unroll
+    for(int k = 0; k < kPerLane; ++k) {
+        tpi[k] = tb * 32 + sub * kPerLane + k;
+        prim[k] = 0xffffffffu;
+        f[k] = Frag{ 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f };
+        if(seg_active && tpi[k] < n_inst) {
+            prim[k] = vals[inst0 + tpi[k]];
+            const PrimRec r = rec[prim[k]];
+            f[k] = Frag{ r.a.x - 0.5f, r.a.y - 0.5f, 0.5f * r.a.z, r.a.w, 0.5f * r.b.x, r.b.y,
+                         fmaxf(r.b.z, 0.0f), fmaxf(r.b.w, 0.0f), fmaxf(r.c.x, 0.0f) };
+        } else {
+            tpi[k] = 0x7fffffff; /* never below a last-contributor count */
+        }
+    }
+    float a_mx[kPerLane], a_my[kPerLane], a_cx[kPerLane], a_cy[kPerLane], a_cz[kPerLane], a_op[kPerLane];
+    float a_r[kPerLane], a_g[kPerLane], a_b[kPerLane];
+#pragma unroll
+    for(int k = 0; k < kPerLane; ++k) {
+        a_mx[k] = a_my[k] = a_cx[k] = a_cy[k] = a_cz[k] = a_op[k] = a_r[k] = a_g[k] = a_b[k] = 0.0f;
+    }
+
     const int tx0 = (int)(tile % (uint32_t)grid_w) * GSX_TILE, ty0 = (int)(tile / (uint32_t)grid_w) * GSX_TILE;
     const size_t P = (size_t)width * (size_t)height;
     const float4 *bsnap = snap + (size_t)bucket * GSX_TILE_PIXELS;
+    const int seg = lane >> 3;
+    PixIn(*stage)[32] = s_in[warp][seg];
 
-    float g_mx = 0.0f, g_my = 0.0f, g_cx = 0.0f, g_cy = 0.0f, g_cz = 0.0f, g_op = 0.0f;
-    float g_r = 0.0f, g_g = 0.0f, g_b = 0.0f;
-    /* per-pixel state travelling along the lanes */
-    float pgr = 0.0f, pgg = 0.0f, pgb = 0.0f, par = 0.0f, pag = 0.0f, pab = 0.0f, pT = 0.0f;
-    uint32_t plast = 0;
-
-    for(int i = 0; i < GSX_TILE_PIXELS + 31; ++i) {
-        if((i & 31) == 0 && i < GSX_TILE_PIXELS) {
-            const int p = i + lane;
+    /* the 8 lanes of a segment prefetch 32 pixels' inputs (snapshot, composed colour + last
+     * contributor, upstream gradient) into shared memory, one batch ahead, with cp.async */
+    auto prefetch = [&](int batch) {
+        PixIn *dst = stage[batch & 1];
+#pragma unroll
+        for(int q = 0; q < 4; ++q) {
+            const int pl = sub + 8 * q, p = batch * 32 + pl;
             const int qx = tx0 + (p & (GSX_TILE - 1)), qy = ty0 + (p >> 4);
-            float4 up = make_float4(0.0f, 0.0f, 0.0f, 0.0f), lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if(qx < width && qy < height) {
+            if(seg_active && qx < width && qy < height) {
                 const size_t idx = (size_t)qy * (size_t)width + (size_t)qx;
-                const float4 s = bsnap[p];
-                const float4 img = pix[idx];
-                up = make_float4(grad_rgb[idx], grad_rgb[P + idx], grad_rgb[2 * P + idx], img.w);
-                lo = make_float4(img.x - s.x, img.y - s.y, img.z - s.z, s.w);
+                cp_async16(&dst[pl].snap, bsnap + p);
+                cp_async16(&dst[pl].img, pix + idx);
+                cp_async4(&dst[pl].grad.x, grad_rgb + idx);
+                cp_async4(&dst[pl].grad.y, grad_rgb + P + idx);
+                cp_async4(&dst[pl].grad.z, grad_rgb + 2 * P + idx);
             }
-            s_up[warp][lane] = up;
-            s_lo[warp][lane] = lo;
+        }
+        cp_async_commit();
+    };
+    prefetch(0);
+
+    /* per-pixel state travelling along the 8 lanes of a segment: upstream gradient, last
+     * contributor, transmittance, and adg = (colour still to come) . (upstream gradient), kept as one
+     * scalar because every fragment changes it by -w * (colour . gradient) */
+    float gr = 0.0f, gg = 0.0f, gb = 0.0f, adg = 0.0f, T = 0.0f;
+    int last = 0;
+    for(int i = 0; i < GSX_TILE_PIXELS + 7; ++i) {
+        if((i & 31) == 0 && i < GSX_TILE_PIXELS) {
+            __syncwarp();
+            if(i + 32 < GSX_TILE_PIXELS) {
+                prefetch((i >> 5) + 1);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
+            }
             __syncwarp();
         }
-        pgr = __shfl_up_sync(0xffffffffu, pgr, 1);
-        pgg = __shfl_up_sync(0xffffffffu, pgg, 1);
-        pgb = __shfl_up_sync(0xffffffffu, pgb, 1);
-        plast = __shfl_up_sync(0xffffffffu, plast, 1);
-        par = __shfl_up_sync(0xffffffffu, par, 1);
-        pag = __shfl_up_sync(0xffffffffu, pag, 1);
-        pab = __shfl_up_sync(0xffffffffu, pab, 1);
-        pT = __shfl_up_sync(0xffffffffu, pT, 1);
-        if(lane == 0 && i < GSX_TILE_PIXELS) {
-            const float4 up = s_up[warp][i & 31];
-            const float4 lo = s_lo[warp][i & 31];
-            pgr = up.x;
-            pgg = up.y;
-            pgb = up.z;
-            plast = __float_as_uint(up.w);
-            par = lo.x;
-            pag = lo.y;
-            pab = lo.z;
-            pT = lo.w;
+        gr = __shfl_up_sync(0xffffffffu, gr, 1);
+        gg = __shfl_up_sync(0xffffffffu, gg, 1);
+        gb = __shfl_up_sync(0xffffffffu, gb, 1);
+        adg = __shfl_up_sync(0xffffffffu, adg, 1);
+        T = __shfl_up_sync(0xffffffffu, T, 1);
+        last = __shfl_up_sync(0xffffffffu, last, 1);
+        const int p = i - sub;
+        const int qx = tx0 + (p & (GSX_TILE - 1)), qy = ty0 + (p >> 4);
+        const bool valid = seg_active && p >= 0 && p < GSX_TILE_PIXELS && qx < width && qy < height;
+        if(sub == 0) {
+            /* segment head: this bucket's inputs for pixel p (= i) */
+            last = 0;
+            if(valid) {
+                const PixIn &in = stage[(i >> 5) & 1][i & 31];
+                const float4 sn = in.snap, img = in.img;
+                gr = in.grad.x;
+                gg = in.grad.y;
+                gb = in.grad.z;
+                last = (int)__float_as_uint(img.w);
+                adg = (img.x - sn.x) * gr + (img.y - sn.y) * gg + (img.z - sn.z) * gb;
+                T = sn.w;
+            }
         }
-        const int idx = i - lane;
-        if(idx < 0 || idx >= GSX_TILE_PIXELS) continue;
-        const int qx = tx0 + (idx & (GSX_TILE - 1)), qy = ty0 + (idx >> 4);
-        if(!valid_prim || qx >= width || qy >= height || (uint32_t)tpi >= plast) continue;
-        const float dx = mx - (float)qx, dy = my - (float)qy;
-        const float dxx = dx * dx, dxy = dx * dy, dyy = dy * dy;
-        const float sig = fmaxf(0.5f * (cx * dxx + cz * dyy) + cy * dxy, 0.0f);
-        const float a_pre = op * __expf(-sig);
-        const float alpha = fminf(a_pre, 0.999f);
-        const bool sat = a_pre >= 0.999f;
-        const float wgt = pT * alpha;
-        g_r += wgt * (pgr * fr);
-        g_g += wgt * (pgg * fg);
-        g_b += wgt * (pgb * fb);
-        par -= wgt * colr;
-        pag -= wgt * colg;
-        pab -= wgt * colb;
-        const float cdg = colr * pgr + colg * pgg + colb * pgb;
-        const float adg = par * pgr + pag * pgg + pab * pgb;
-        const float oma = 1.0f - alpha;
-        const float dl_dalpha = pT * cdg - adg * (1.0f / fmaxf(oma, 1e-4f));
-        const float part = sat ? 0.0f : alpha * dl_dalpha;
-        g_cx += -0.5f * part * dxx;
-        g_cy += -part * dxy;
-        g_cz += -0.5f * part * dyy;
-        g_mx -= part * (cx * dx + cy * dy);
-        g_my -= part * (cy * dx + cz * dy);
-        g_op += part;
-        pT *= oma;
+        if(!valid) continue;
+        const float fx = (float)qx, fy = (float)qy;
+#pragma unroll
+        for(int k = 0; k < kPerLane; ++k) {
+            const float dx = f[k].mx - fx, dy = f[k].my - fy;
+            const float dxx = dx * dx, dxy = dx * dy, dyy = dy * dy;
+            const float sig = fmaxf(fmaf(f[k].hcx, dxx, fmaf(f[k].hcz, dyy, f[k].cy * dxy)), 0.0f);
+            const float a_pre = f[k].op * fast_exp2(sig * -1.4426950408889634f);
+            const float alpha = tpi[k] < last ? fminf(a_pre, 0.999f) : 0.0f;
+            const float w = T * alpha;
+            a_r[k] = fmaf(w, gr, a_r[k]);
+            a_g[k] = fmaf(w, gg, a_g[k]);
+            a_b[k] = fmaf(w, gb, a_b[k]);
+            const float cdg = fmaf(f[k].r, gr, fmaf(f[k].g, gg, f[k].b * gb));
+            adg = fmaf(-w, cdg, adg);
+            const float oma = 1.0f - alpha;
+            const float dl = fmaf(T, cdg, -adg * fast_rcp(fmaxf(oma, 1e-4f)));
+            const float part = a_pre >= 0.999f ? 0.0f : alpha * dl;
+            a_cx[k] = fmaf(part, dxx, a_cx[k]);
+            a_cy[k] = fmaf(part, dxy, a_cy[k]);
+            a_cz[k] = fmaf(part, dyy, a_cz[k]);
+            a_mx[k] = fmaf(part, dx, a_mx[k]);
+            a_my[k] = fmaf(part, dy, a_my[k]);
+            a_op[k] += part;
+            T *= oma;
+        }
     }
-    if(valid_prim) {
-        float4 *acc = grad_acc + (size_t)prim * 3;
-        atomicAdd(acc + 0, make_float4(g_mx, g_my, g_cx, g_cy));
-        atomicAdd(acc + 1, make_float4(g_cz, g_op * (1.0f - op), g_r, g_g));
-        atomicAdd(&acc[2].x, g_b);
+#pragma unroll
+    for(int k = 0; k < kPerLane; ++k) {
+        if(prim[k] == 0xffffffffu) continue;
+        const PrimRec r = rec[prim[k]];
+        const float fr = r.b.z >= 0.0f ? 1.0f : 0.0f, fg = r.b.w >= 0.0f ? 1.0f : 0.0f, fb = r.c.x >= 0.0f ? 1.0f : 0.0f;
+        float4 *acc = grad_acc + (size_t)prim[k] * 3;
+        /* sum(part * (conic . d)) = conic . sum(part * d): the mean gradient is finished here */
+        const float cx = r.a.z, cy = r.a.w, cz = r.b.x;
+        const float gmx = fmaf(cx, a_mx[k], cy * a_my[k]), gmy = fmaf(cy, a_mx[k], cz * a_my[k]);
+        atomicAdd(acc + 0, make_float4(-gmx, -gmy, -0.5f * a_cx[k], -a_cy[k]));
+        atomicAdd(acc + 1, make_float4(-0.5f * a_cz[k], a_op[k] * (1.0f - f[k].op), a_r[k] * fr, a_g[k] * fg));
+        atomicAdd(&acc[2].x, a_b[k] * fb);
     }
 }
 
@@ -156,8 +243,12 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const u
 {
     (void)n;
     if(bucket_capacity == 0 || n_tiles <= 0) return cudaSuccess;
-    const uint64_t blocks = (bucket_capacity + kWarps - 1) / kWarps;
-    blend_backward_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(width, height, grid_w, n_tiles, ranges,
+    const uint64_t per_block = (uint64_t)kWarps * 4;
+    const uint64_t blocks = (bucket_capacity + per_block - 1) / per_block;
+    const size_t smem = sizeof(PixIn) * kWarps * 4 * 2 * 32;
+    cudaError_t err = cudaFuncSetAttribute(blend_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if(err != cudaSuccess) return err;
+    blend_backward_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, grid_w, n_tiles, ranges,
                                                                       bucket_offsets, bucket_tile, vals, rec, pix,
                                                                       tile_max, snap, grad_rgb, grad_acc);
     return cudaGetLastError();

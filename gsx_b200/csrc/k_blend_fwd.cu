@@ -5,42 +5,75 @@
  * Follows fastgs/kernels_forward.cuh:595-736 (blend_cu<false>) and render-kernels.cu:13-36:
  * alpha = min(opacity * exp(-sigma), 0.999), fragments with sigma < 0 or alpha < 1/255 skipped,
  * the pixel stops after the fragment that takes transmittance below 1e-4, a (colour,
- * transmittance) snapshot per pixel before every 32-instance bucket for the backward pass, and
+ * transmittance) snapshot per pixel before every 32-instance bucket for the backward pass
+ * (written for every bucket of every batch the tile processes, as the reference does), and
  * out = colour + (1 - alpha) * background.
  *
- * B200 choices: batches of 256 instances are staged in shared memory as two float4 + one float
- * per instance (half-conic and clamped colour precomputed at staging, both exact transforms);
- * the whole-tile early exit is a __syncthreads_count vote; sigma > 5.6 is rejected before the
- * exponential (exp(-5.6) < 1/255, so such fragments can never pass the alpha test: the decision
- * is identical).  Compiled with -fmad=false; the fragment arithmetic uses explicit fmaf exactly
- * as the oracle's orc_blend_forward, so RGB is bit-identical to it.
+ * B200 organisation: each warp owns an 8x4 pixel block of the tile.  After a batch of 256
+ * instances is staged in shared memory, every warp builds the ordered list of staged instances
+ * whose opacity-aware footprint can reach its block: the exact minimum of the instance's
+ * quadratic form over the block's pixel-centre rectangle is compared with ln(255 * opacity) plus
+ * a safety margin (the conic is bounded by the +0.3 dilation, so the float rounding of a pixel's
+ * sigma is far below the margin).  Only listed instances are evaluated per pixel; an instance not
+ * listed can never pass the per-pixel alpha test, so the result is unchanged.  Compiled with
+ * -fmad=false; the per-pixel arithmetic uses explicit fmaf exactly as the oracle's
+ * orc_blend_forward, so RGB is bit-identical to it.
  */
 #include "gsx_b200_kernels.cuh"
 
 namespace {
 
 constexpr int kThreads = GSX_TILE_PIXELS;
+constexpr int kWarps = kThreads / 32;
+
+/* minimum of q(d) = hcx dx^2 + cy dx dy + hcz dy^2, d = m - p, over p in [x0,x1] x [y0,y1] */
+__device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, float cy, float hcz, float icx, float icz,
+                                                float x0, float x1, float y0, float y1)
+{
+    if(mx >= x0 && mx <= x1 && my >= y0 && my <= y1) return 0.0f;
+    const float dy_lo = my - y1, dy_hi = my - y0, dx_lo = mx - x1, dx_hi = mx - x0;
+    float best = 3.0e38f;
+#pragma unroll
+    for(int e = 0; e < 2; ++e) {
+        const float dx = e == 0 ? dx_hi : dx_lo; /* edges x = x0, x = x1 */
+        const float dy = fminf(fmaxf(-cy * dx * icz, dy_lo), dy_hi);
+        best = fminf(best, hcx * dx * dx + cy * dx * dy + hcz * dy * dy);
+    }
+#pragma unroll
+    for(int e = 0; e < 2; ++e) {
+        const float dy = e == 0 ? dy_hi : dy_lo; /* edges y = y0, y = y1 */
+        const float dx = fminf(fmaxf(-cy * dy * icx, dx_lo), dx_hi);
+        best = fminf(best, hcx * dx * dx + cy * dx * dy + hcz * dy * dy);
+    }
+    return best;
+}
 
 __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     int width, int height, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, float *__restrict__ out_rgb,
-    float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap)
+    float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile)
 {
-    __shared__ float4 s_a[kThreads];
-    __shared__ float4 s_b[kThreads];
-    __shared__ float s_c[kThreads];
-    __shared__ uint32_t s_max[kThreads / 32];
+    __shared__ float4 s_a[kThreads]; /* mean2d.x, mean2d.y, conic.x / 2, conic.y */
+    __shared__ float4 s_b[kThreads]; /* conic.z / 2, opacity, clamped r, g */
+    __shared__ float4 s_c[kThreads]; /* clamped b, cull threshold, 1/conic.x, 1/conic.z */
+    __shared__ uint8_t s_list[kWarps][kThreads];
+    __shared__ uint32_t s_max[kWarps];
     const int tile = blockIdx.x;
     const int tx = tile % grid_w, ty = tile / grid_w;
-    const int lx = threadIdx.x & (GSX_TILE - 1), ly = threadIdx.x >> 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lx = (warp & 1) * 8 + (lane & 7), ly = (warp >> 1) * 4 + (lane >> 3);
+    const int prank = ly * GSX_TILE + lx; /* pixel rank in the tile: snapshot slot */
     const int px = tx * GSX_TILE + lx, py = ty * GSX_TILE + ly;
     const bool inside = px < width && py < height;
     const float pxf = (float)px + 0.5f, pyf = (float)py + 0.5f;
+    const float rx0 = (float)(tx * GSX_TILE + (warp & 1) * 8) + 0.5f, rx1 = rx0 + 7.0f;
+    const float ry0 = (float)(ty * GSX_TILE + (warp >> 1) * 4) + 0.5f, ry1 = ry0 + 3.0f;
     const uint2 range = ranges[tile];
     uint32_t bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
+    for(uint32_t b = bucket + threadIdx.x; b < bucket_offsets[tile]; b += kThreads) bucket_tile[b] = (uint32_t)tile;
 
     float cr = 0.0f, cg = 0.0f, cb = 0.0f, T = 1.0f;
-    uint32_t npos = 0, ncon = 0;
+    uint32_t ncon = 0;
     bool done = !inside;
     const int total = (int)(range.y - range.x);
     for(int start = 0; start < total; start += kThreads) {
@@ -48,39 +81,57 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
         const int fetch = start + (int)threadIdx.x;
         if(fetch < total) {
             const PrimRec r = rec[vals[range.x + fetch]];
+            const float thr = __logf(r.b.y * 255.0f);
             s_a[threadIdx.x] = make_float4(r.a.x, r.a.y, 0.5f * r.a.z, r.a.w);
             s_b[threadIdx.x] = make_float4(0.5f * r.b.x, r.b.y, fmaxf(r.b.z, 0.0f), fmaxf(r.b.w, 0.0f));
-            s_c[threadIdx.x] = fmaxf(r.c.x, 0.0f);
+            s_c[threadIdx.x] = make_float4(fmaxf(r.c.x, 0.0f), thr + 0.05f + 1e-3f * fabsf(thr), 1.0f / r.a.z, 1.0f / r.b.x);
         }
         __syncthreads();
         const int batch = total - start < kThreads ? total - start : kThreads;
-        int j = 0;
-        for(; !done && j < batch; ++j) {
-            if((j & 31) == 0) {
-                snap[(size_t)bucket * kThreads + threadIdx.x] = make_float4(cr, cg, cb, T);
-                ++bucket;
+        /* ordered list of the staged instances that can reach this warp's 8x4 block */
+        int cnt = 0;
+        if(__any_sync(0xffffffffu, !done)) {
+#pragma unroll 1
+            for(int k = 0; k * 32 < batch; ++k) {
+                const int e = k * 32 + lane;
+                bool pass = false;
+                if(e < batch) {
+                    const float4 a = s_a[e], b = s_b[e], c = s_c[e];
+                    pass = rect_min_power(a.x, a.y, a.z, a.w, b.x, c.z, c.w, rx0, rx1, ry0, ry1) <= c.y;
+                }
+                const unsigned m = __ballot_sync(0xffffffffu, pass);
+                if(pass) s_list[warp][cnt + __popc(m & ((1u << lane) - 1u))] = (uint8_t)e;
+                cnt += __popc(m);
             }
-            ++npos;
-            const float4 a = s_a[j];
-            const float dx = a.x - pxf, dy = a.y - pyf;
-            const float4 b = s_b[j];
-            const float sigma = fmaf(dx, fmaf(a.z, dx, a.w * dy), (b.x * dy) * dy);
-            if(sigma < 0.0f || sigma > 5.6f) continue;
-            const float g = gsx_expf_inrange(-sigma);
-            const float alpha = fminf(b.y * g, 0.999f);
-            if(alpha < 1.0f / 255.0f) continue;
-            const float w = T * alpha;
-            cr = fmaf(w, b.z, cr);
-            cg = fmaf(w, b.w, cg);
-            cb = fmaf(w, s_c[j], cb);
-            T = T * (1.0f - alpha);
-            ncon = npos;
-            if(T < 1e-4f) done = true;
         }
-        for(j = (j + 31) & ~31; j < batch; j += 32) {
-            snap[(size_t)bucket * kThreads + threadIdx.x] = make_float4(cr, cg, cb, T);
+        __syncwarp();
+        int li = 0;
+        for(int kb = 0; kb * 32 < batch; ++kb) {
+            snap[(size_t)bucket * kThreads + prank] = make_float4(cr, cg, cb, T);
             ++bucket;
+            const int bend = (kb + 1) * 32;
+            for(; li < cnt; ++li) {
+                const int e = s_list[warp][li];
+                if(e >= bend) break;
+                if(done) continue;
+                const float4 a = s_a[e];
+                const float dx = a.x - pxf, dy = a.y - pyf;
+                const float4 b = s_b[e];
+                const float sigma = fmaf(dx, fmaf(a.z, dx, a.w * dy), (b.x * dy) * dy);
+                if(sigma < 0.0f || sigma > 5.6f) continue;
+                const float g = gsx_expf_inrange(-sigma);
+                const float alpha = fminf(b.y * g, 0.999f);
+                if(alpha < 1.0f / 255.0f) continue;
+                const float w = T * alpha;
+                cr = fmaf(w, b.z, cr);
+                cg = fmaf(w, b.w, cg);
+                cb = fmaf(w, s_c[e].x, cb);
+                T = T * (1.0f - alpha);
+                ncon = (uint32_t)(start + e + 1);
+                if(T < 1e-4f) done = true;
+            }
         }
+        __syncthreads();
     }
     if(inside) {
         const size_t P = (size_t)width * (size_t)height;
@@ -96,12 +147,12 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     uint32_t m = ncon;
 #pragma unroll
     for(int d = 16; d > 0; d >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, d));
-    if((threadIdx.x & 31) == 0) s_max[threadIdx.x >> 5] = m;
+    if(lane == 0) s_max[warp] = m;
     __syncthreads();
     if(threadIdx.x == 0) {
         uint32_t mm = 0;
 #pragma unroll
-        for(int w = 0; w < kThreads / 32; ++w) mm = max(mm, s_max[w]);
+        for(int w = 0; w < kWarps; ++w) mm = max(mm, s_max[w]);
         tile_max[tile] = mm;
     }
 }
@@ -111,11 +162,11 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
 cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max, float4 *snap,
-                                     cudaStream_t stream)
+                                     uint32_t *bucket_tile, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
     blend_forward_kernel<<<(unsigned)n_tiles, kThreads, 0, stream>>>(
         width, height, grid_w, ranges, bucket_offsets, vals, rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
-        tile_max, snap);
+        tile_max, snap, bucket_tile);
     return cudaGetLastError();
 }

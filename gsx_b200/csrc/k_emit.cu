@@ -15,17 +15,31 @@ namespace {
 constexpr int kThreads = 256;
 
 __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec *__restrict__ rec,
-                                                        const uint32_t *__restrict__ offsets, unsigned grid_w,
+                                                        const uint32_t *__restrict__ counts,
+                                                        const uint32_t *__restrict__ block_offsets,
+                                                        uint32_t *__restrict__ offsets, unsigned grid_w,
                                                         unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
                                                         uint64_t capacity, uint32_t *__restrict__ flags)
 {
-    const int lane = threadIdx.x & 31;
+    __shared__ uint32_t s_warp[kThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-    uint32_t start = 0, cnt = 0;
-    if(i < n) {
-        start = offsets[i];
-        cnt = offsets[i + 1] - start;
+    uint32_t cnt = i < n ? counts[i] : 0u;
+    /* exclusive position = block offset + in-block exclusive scan of the counts */
+    uint32_t incl = cnt;
+#pragma unroll
+    for(int d = 1; d < 32; d <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, d);
+        if(lane >= d) incl += t;
     }
+    if(lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    uint32_t woff = 0;
+#pragma unroll
+    for(int k = 0; k < kThreads / 32; ++k) woff += k < warp ? s_warp[k] : 0u;
+    const uint32_t start = block_offsets[blockIdx.x] + woff + incl - cnt;
+    if(i < n) offsets[i] = start;
+    if(i == n - 1) offsets[n] = start + cnt;
     if(__ballot_sync(0xffffffffu, cnt != 0) == 0) return;
     float msx = 0.0f, msy = 0.0f, cx = 0.0f, cy = 0.0f, cz = 0.0f, pt = 0.0f;
     unsigned bx0 = 0, bw = 0, by0 = 0, tmax = 0;
@@ -90,12 +104,13 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 
 } // namespace
 
-cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *offsets, int grid_w,
-                            unsigned long long *keys, uint32_t *vals, uint64_t capacity, uint32_t *flags,
-                            cudaStream_t stream)
+cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *block_offsets,
+                            uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
+                            uint32_t *flags, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
-    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, offsets, (unsigned)grid_w, keys, vals, capacity, flags);
+    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, block_offsets, offsets, (unsigned)grid_w, keys,
+                                                            vals, capacity, flags);
     return cudaGetLastError();
 }

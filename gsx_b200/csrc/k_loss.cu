@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(kThreads) l1_ssim_kernel(const float *__restri
                                                            float *__restrict__ loss_map, float *__restrict__ grad,
                                                            float *__restrict__ loss_sum, int planes, int height, int width,
                                                            float l1_scale, float ssim_scale, float l1_grad_scale,
-                                                           float ssim_grad_scale)
+                                                           float ssim_grad_scale, bool overwrite)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     LossSmem &S = *reinterpret_cast<LossSmem *>(smem_raw);
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kThreads) l1_ssim_kernel(const float *__restri
             if(DO_LOSS && in_image && y >= kR && y < kR + kOut && x >= kR && x < kR + kOut) {
                 const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
                 const float ssim = den == 0.0f ? 1.0f : (C * D) / den;
-                float lm = loss_map[idx];
+                float lm = overwrite ? 0.0f : loss_map[idx];
                 if(WITH_L1) lm += l1_scale * fabsf(S.in_p[y + kR][x + kR] - S.in_t[y + kR][x + kR]);
                 lm = border ? 0.0f : lm + ssim_scale * (1.0f - ssim);
                 loss_map[idx] = lm;
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) l1_ssim_kernel(const float *__restri
                 }
                 const float p = S.in_p[y + 2 * kR][x + 2 * kR], t = S.in_t[y + 2 * kR][x + 2 * kR];
                 const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
-                float g = grad[idx];
+                float g = overwrite ? 0.0f : grad[idx];
                 if(WITH_L1) {
                     const float d = p - t;
                     g += (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * l1_grad_scale;
@@ -201,7 +201,7 @@ bool g_gauss_ready[64];
 template <bool L, bool G, bool W>
 cudaError_t launch_l1_ssim(const float *pred, const float *target, float *loss_map, float *grad, float *loss_sum,
                            int planes, int height, int width, float l1_scale, float ssim_scale, float l1_grad_scale,
-                           float ssim_grad_scale, cudaStream_t stream)
+                           float ssim_grad_scale, bool overwrite, cudaStream_t stream)
 {
     const size_t smem = sizeof(LossSmem);
     cudaError_t err = cudaFuncSetAttribute(l1_ssim_kernel<L, G, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -209,7 +209,7 @@ cudaError_t launch_l1_ssim(const float *pred, const float *target, float *loss_m
     dim3 grid((unsigned)((width + kOut - 1) / kOut), (unsigned)((height + kOut - 1) / kOut),
               (unsigned)(planes < 65535 ? planes : 65535));
     l1_ssim_kernel<L, G, W><<<grid, kThreads, smem, stream>>>(pred, target, loss_map, grad, loss_sum, planes, height,
-                                                              width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale);
+                                                              width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, overwrite);
     return cudaGetLastError();
 }
 
@@ -241,12 +241,13 @@ cudaError_t gsx_launch_l1_ssim(int mode, const float *pred, const float *target,
 {
     cudaError_t err = ensure_gauss();
     if(err != cudaSuccess) return err;
-    switch(mode) {
-    case 1: return launch_l1_ssim<true, false, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
-    case 2: return launch_l1_ssim<false, true, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
-    case 3: return launch_l1_ssim<true, true, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
-    case 5: return launch_l1_ssim<true, false, true>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
-    case 7: return launch_l1_ssim<true, true, true>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, stream);
+    const bool ow = (mode & 8) != 0;
+    switch(mode & 7) {
+    case 1: return launch_l1_ssim<true, false, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, ow, stream);
+    case 2: return launch_l1_ssim<false, true, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, ow, stream);
+    case 3: return launch_l1_ssim<true, true, false>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, ow, stream);
+    case 5: return launch_l1_ssim<true, false, true>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, ow, stream);
+    case 7: return launch_l1_ssim<true, true, true>(pred, target, loss_map, grad, loss_sum, planes, height, width, l1_scale, ssim_scale, l1_grad_scale, ssim_grad_scale, ow, stream);
     default: return cudaErrorInvalidValue;
     }
 }

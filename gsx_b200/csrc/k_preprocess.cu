@@ -1,12 +1,14 @@
 /*
- * Per-Gaussian preprocess fused with the single-pass prefix sum of the tile-overlap counts.
+ * Per-Gaussian preprocess: projection, EWA covariance, screen bounds, exact tile count, SH colour.
  *
  * Follows fastgs/kernels_forward.cuh:179-438 (preprocess_cu) for the projection, EWA covariance,
  * opacity-aware screen bounds and SH colour, and :109-175 for the exact tile count.  Differences
  * in structure (not in results):
- *   - no atomic compaction of visible primitives: each primitive's count goes through a
- *     decoupled-lookback exclusive scan inside this kernel (dynamic tile ids guarantee forward
- *     progress), so `offsets` comes out in primitive order and emission is deterministic;
+ *   - no atomic compaction of visible primitives: each CTA writes its primitives' tile counts and
+ *     its block total; a one-CTA scan over block totals and the emission kernel's in-block scan
+ *     turn them into exclusive offsets in primitive order, so emission is deterministic;
+ *   - the [N,3] fields are staged through shared memory so every global load is a coalesced,
+ *     contiguous warp access;
  *   - everything the later stages need is packed into one 48-byte PrimRec per primitive.
  * Compiled with -fmad=false: the arithmetic matches the oracle (oracle/gsx_oracle.c) bit for bit.
  */
@@ -15,9 +17,6 @@
 namespace {
 
 constexpr int kThreads = 256;
-constexpr unsigned long long kFlagAgg = 1ull << 62;
-constexpr unsigned long long kFlagInc = 2ull << 62;
-constexpr unsigned long long kValueMask = (1ull << 62) - 1ull;
 
 __device__ __forceinline__ int f2i_rd(float v)
 {
@@ -81,17 +80,24 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     const float *__restrict__ mean3d, const float *__restrict__ rotation, const float *__restrict__ logscale,
     const float *__restrict__ opacity_raw, const float *__restrict__ sh0, const float *__restrict__ sh1,
     const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n, CameraParams cam,
-    PrimRec *__restrict__ rec, uint32_t *__restrict__ offsets, unsigned long long *__restrict__ lookback,
-    uint32_t *__restrict__ tile_counter, uint32_t *__restrict__ flags)
+    PrimRec *__restrict__ rec, uint32_t *__restrict__ counts, uint32_t *__restrict__ block_sums)
 {
-    __shared__ uint32_t s_tile;
+    __shared__ float s_m[kThreads * 3];
+    __shared__ float s_s[kThreads * 3];
     __shared__ uint32_t s_warp_sum[kThreads / 32];
-    __shared__ unsigned long long s_prefix;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if(threadIdx.x == 0) s_tile = atomicAdd(tile_counter, 1u);
-    __syncthreads();
-    const uint32_t tile = s_tile;
-    const int64_t i = (int64_t)tile * kThreads + threadIdx.x;
+    const int64_t base = (int64_t)blockIdx.x * kThreads;
+    const int64_t i = base + threadIdx.x;
+    {
+        /* coalesced staging of the block's [256,3] mean and log-scale rows */
+        const int64_t avail = (n - base) * 3;
+        for(int j = threadIdx.x; j < kThreads * 3; j += kThreads) {
+            const bool ok = j < avail;
+            s_m[j] = ok ? mean3d[base * 3 + j] : 0.0f;
+            s_s[j] = ok ? logscale[base * 3 + j] : 0.0f;
+        }
+        __syncthreads();
+    }
 
     bool active = i < n;
     float m[3] = { 0.0f, 0.0f, 0.0f };
@@ -99,9 +105,9 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     unsigned bx0 = 0, bx1 = 0, by0 = 0, by1 = 0;
     const float *w = cam.w2c;
     if(active) {
-        m[0] = mean3d[i * 3 + 0];
-        m[1] = mean3d[i * 3 + 1];
-        m[2] = mean3d[i * 3 + 2];
+        m[0] = s_m[threadIdx.x * 3 + 0];
+        m[1] = s_m[threadIdx.x * 3 + 1];
+        m[2] = s_m[threadIdx.x * 3 + 2];
         depth = w[8] * m[0] + w[9] * m[1] + w[10] * m[2] + w[11];
         if(depth < cam.near_plane || depth > cam.far_plane) active = false;
     }
@@ -113,7 +119,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
         float var[3];
 #pragma unroll
         for(int k = 0; k < 3; ++k) {
-            const float s = gsx_expf(logscale[i * 3 + k]);
+            const float s = gsx_expf(s_s[threadIdx.x * 3 + k]);
             var[k] = s * s;
         }
         const float4 q = *reinterpret_cast<const float4 *>(rotation + i * 4);
@@ -219,67 +225,49 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
         rec[i] = r;
     }
 
-    /* block-wide exclusive scan of cnt */
-    unsigned incl = cnt;
+    if(i < n) counts[i] = cnt;
+    unsigned sum = cnt;
+#pragma unroll
+    for(int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
+    if(lane == 0) s_warp_sum[warp] = sum;
+    __syncthreads();
+    if(threadIdx.x == 0) {
+        unsigned t = 0;
+#pragma unroll
+        for(int k = 0; k < kThreads / 32; ++k) t += s_warp_sum[k];
+        block_sums[blockIdx.x] = t;
+    }
+}
+
+/* exclusive scan of the per-CTA totals (one CTA); block_sums[nb] receives the grand total */
+__global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t *__restrict__ block_sums, int nb)
+{
+    __shared__ uint32_t s_w[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int per = (nb + 1023) / 1024;
+    const int b0 = threadIdx.x * per;
+    uint32_t local = 0;
+    for(int b = b0; b < b0 + per && b < nb; ++b) local += block_sums[b];
+    uint32_t incl = local;
 #pragma unroll
     for(int d = 1; d < 32; d <<= 1) {
-        const unsigned t = __shfl_up_sync(0xffffffffu, incl, d);
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, d);
         if(lane >= d) incl += t;
     }
-    if(lane == 31) s_warp_sum[warp] = incl;
+    if(lane == 31) s_w[warp] = incl;
     __syncthreads();
-    if(warp == 0) {
-        unsigned v = lane < kThreads / 32 ? s_warp_sum[lane] : 0u;
-        unsigned wi = v;
-#pragma unroll
-        for(int d = 1; d < 32; d <<= 1) {
-            const unsigned t = __shfl_up_sync(0xffffffffu, wi, d);
-            if(lane >= d) wi += t;
-        }
-        if(lane < kThreads / 32) s_warp_sum[lane] = wi - v; /* exclusive warp offsets */
-        const unsigned long long block_total = __shfl_sync(0xffffffffu, wi, kThreads / 32 - 1);
-        /* decoupled lookback over predecessor tiles, one warp, 32 tiles per round */
-        unsigned long long prefix = 0;
-        if(tile == 0) {
-            if(lane == 0) gsx_st_release64(&lookback[0], kFlagInc | block_total);
-        } else {
-            if(lane == 0) gsx_st_release64(&lookback[tile], kFlagAgg | block_total);
-            long long pos = (long long)tile - 1;
-            unsigned spins = 0;
-            bool timed_out = false;
-            while(true) {
-                const long long t = pos - lane;
-                unsigned long long st = t >= 0 ? gsx_ld_acquire64(&lookback[t]) : kFlagInc;
-                const unsigned flag = (unsigned)(st >> 62);
-                const unsigned inc_mask = __ballot_sync(0xffffffffu, flag == 2u);
-                const unsigned empty_mask = __ballot_sync(0xffffffffu, flag == 0u);
-                /* lanes up to and including the first INC must all be non-empty */
-                const unsigned upto = inc_mask ? ((inc_mask & (0u - inc_mask)) << 1) - 1u : 0xffffffffu;
-                if(empty_mask & upto) {
-                    if(++spins > GSX_SPIN_LIMIT) {
-                        timed_out = true;
-                        break;
-                    }
-                    continue;
-                }
-                unsigned long long val = (upto >> lane) & 1u ? (st & kValueMask) : 0ull;
-#pragma unroll
-                for(int d = 16; d > 0; d >>= 1) val += __shfl_xor_sync(0xffffffffu, val, d);
-                prefix += val;
-                if(inc_mask) break;
-                pos -= 32;
-            }
-            if(timed_out && lane == 0) atomicOr(flags, GSX_FLAG_LOOKBACK_TIMEOUT);
-            if(lane == 0) gsx_st_release64(&lookback[tile], kFlagInc | (prefix + block_total));
-        }
-        if(lane == 0) {
-            s_prefix = prefix;
-            const int64_t last = (int64_t)tile * kThreads + kThreads - 1;
-            if(last >= n - 1 && (int64_t)tile * kThreads <= n - 1) offsets[n] = (uint32_t)(prefix + block_total);
-        }
+    uint32_t woff = 0, tot = 0;
+    for(int k = 0; k < 32; ++k) {
+        woff += k < warp ? s_w[k] : 0u;
+        tot += s_w[k];
     }
-    __syncthreads();
-    if(i < n) offsets[i] = (uint32_t)(s_prefix + s_warp_sum[warp] + (incl - cnt));
+    uint32_t run = woff + incl - local;
+    for(int b = b0; b < b0 + per && b < nb; ++b) {
+        const uint32_t v = block_sums[b];
+        block_sums[b] = run;
+        run += v;
+    }
+    if(threadIdx.x == 0) block_sums[nb] = tot;
 }
 
 } // namespace
@@ -287,13 +275,13 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
-                                  uint32_t *offsets, uint32_t *lookback, uint32_t *tile_counter, uint32_t *flags,
-                                  cudaStream_t stream)
+                                  uint32_t *counts, uint32_t *block_sums, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
     preprocess_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(
-        mean3d, rotation, logscale, opacity, sh0, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, rec, offsets,
-        reinterpret_cast<unsigned long long *>(lookback), tile_counter, flags);
+        mean3d, rotation, logscale, opacity, sh0, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, rec, counts,
+        block_sums);
+    block_scan_kernel<<<1, 1024, 0, stream>>>(block_sums, (int)blocks);
     return cudaGetLastError();
 }

@@ -13,37 +13,52 @@
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 
 __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     const float *__restrict__ mean3d, const float *__restrict__ rotation, const float *__restrict__ logscale,
     const float *__restrict__ sh1, const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n,
-    CameraParams cam, const uint32_t *__restrict__ offsets, float4 *__restrict__ grad_acc, float *__restrict__ g_mean3d,
+    CameraParams cam, const uint32_t *__restrict__ counts, float4 *__restrict__ grad_acc, float *__restrict__ g_mean3d,
     float *__restrict__ g_rotation, float *__restrict__ g_logscale, float *__restrict__ g_opacity,
     float *__restrict__ g_sh0, float *__restrict__ g_sh1, float *__restrict__ g_sh2, float *__restrict__ g_sh3)
 {
-    const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-    if(i >= n) return;
-    const bool visible = offsets[i + 1] != offsets[i];
-    if(!visible) {
-        g_mean3d[i * 3 + 0] = 0.0f;
-        g_mean3d[i * 3 + 1] = 0.0f;
-        g_mean3d[i * 3 + 2] = 0.0f;
+    __shared__ float s_m[kThreads * 3];  /* staged mean3d rows, then gradient mean3d rows */
+    __shared__ float s_s[kThreads * 3];  /* staged logscale rows, then gradient logscale rows */
+    __shared__ float s_c[kThreads * 3];  /* gradient sh0 rows */
+    const int64_t base = (int64_t)blockIdx.x * kThreads;
+    const int64_t i = base + threadIdx.x;
+    const int64_t avail = (n - base) * 3;
+    /* every independent load of this thread is issued up front (the kernel is latency-bound) */
+    const bool in_range = i < n;
+    const uint32_t cnt = in_range ? counts[i] : 0u;
+    float4 A0 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), A1 = A0, A2 = A0, q = A0;
+    if(in_range) {
+        const float4 *acc_in = grad_acc + (size_t)i * 3;
+        A0 = acc_in[0];
+        A1 = acc_in[1];
+        A2 = acc_in[2];
+        q = *reinterpret_cast<const float4 *>(rotation + i * 4);
+    }
+    for(int j = threadIdx.x; j < kThreads * 3; j += kThreads) {
+        const bool ok = j < avail;
+        s_m[j] = ok ? mean3d[base * 3 + j] : 0.0f;
+        s_s[j] = ok ? logscale[base * 3 + j] : 0.0f;
+        s_c[j] = 0.0f;
+    }
+    __syncthreads();
+    const float m0 = s_m[threadIdx.x * 3 + 0], m1 = s_m[threadIdx.x * 3 + 1], m2 = s_m[threadIdx.x * 3 + 2];
+    const float ls0 = s_s[threadIdx.x * 3 + 0], ls1 = s_s[threadIdx.x * 3 + 1], ls2 = s_s[threadIdx.x * 3 + 2];
+    float gm[3] = { 0.0f, 0.0f, 0.0f }, gs[3] = { 0.0f, 0.0f, 0.0f };
+    const bool visible = in_range && cnt != 0;
+    if(i < n && !visible) {
         *reinterpret_cast<float4 *>(g_rotation + i * 4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        g_logscale[i * 3 + 0] = 0.0f;
-        g_logscale[i * 3 + 1] = 0.0f;
-        g_logscale[i * 3 + 2] = 0.0f;
         g_opacity[i] = 0.0f;
-        g_sh0[i * 3 + 0] = 0.0f;
-        g_sh0[i * 3 + 1] = 0.0f;
-        g_sh0[i * 3 + 2] = 0.0f;
         if(bases > 1) for(int k = 0; k < 9; ++k) g_sh1[i * 9 + k] = 0.0f;
         if(bases > 4) for(int k = 0; k < 15; ++k) g_sh2[i * 15 + k] = 0.0f;
         if(bases > 9) for(int k = 0; k < 21; ++k) g_sh3[i * 21 + k] = 0.0f;
-        return;
     }
+    if(visible) {
     float4 *acc = grad_acc + (size_t)i * 3;
-    const float4 A0 = acc[0], A1 = acc[1], A2 = acc[2];
     acc[0] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     acc[1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     acc[2] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -51,11 +66,10 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     const float gc[3] = { A1.z, A1.w, A2.x };
     g_opacity[i] = A1.y;
 
-    const float m0 = mean3d[i * 3 + 0], m1 = mean3d[i * 3 + 1], m2 = mean3d[i * 3 + 2];
     /* SH colour backward */
     float dmc0 = 0.0f, dmc1 = 0.0f, dmc2 = 0.0f;
 #pragma unroll
-    for(int c = 0; c < 3; ++c) g_sh0[i * 3 + c] = 0.28209479177387814f * gc[c];
+    for(int c = 0; c < 3; ++c) s_c[threadIdx.x * 3 + c] = 0.28209479177387814f * gc[c];
     if(bases > 1) {
         const float xr = m0 - cam.cam_pos[0], yr = m1 - cam.cam_pos[1], zr = m2 - cam.cam_pos[2];
         const float nsq = xr * xr + yr * yr + zr * zr;
@@ -129,10 +143,9 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     float s[3], var[3];
 #pragma unroll
     for(int k = 0; k < 3; ++k) {
-        s[k] = __expf(logscale[i * 3 + k]);
+        s[k] = __expf(k == 0 ? ls0 : (k == 1 ? ls1 : ls2));
         var[k] = s[k] * s[k];
     }
-    const float4 q = *reinterpret_cast<const float4 *>(rotation + i * 4);
     const float qx = q.x, qy = q.y, qz = q.z, qr = q.w;
     const float qn = qr * qr + qx * qx + qy * qy + qz * qz;
     const float iqn = 1.0f / qn;
@@ -190,9 +203,9 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     const float dcam0 = j11 * (dm2x - dj13c * idepth);
     const float dcam1 = j22 * (dm2y - dj23c * idepth);
     const float dcam2 = -j11 * (x * dm2x + h1 * idepth) - j22 * (y * dm2y + h2 * idepth);
-    g_mean3d[i * 3 + 0] = w[0] * dcam0 + w[4] * dcam1 + w[8] * dcam2 + dmc0;
-    g_mean3d[i * 3 + 1] = w[1] * dcam0 + w[5] * dcam1 + w[9] * dcam2 + dmc1;
-    g_mean3d[i * 3 + 2] = w[2] * dcam0 + w[6] * dcam1 + w[10] * dcam2 + dmc2;
+    gm[0] = w[0] * dcam0 + w[4] * dcam1 + w[8] * dcam2 + dmc0;
+    gm[1] = w[1] * dcam0 + w[5] * dcam1 + w[9] * dcam2 + dmc1;
+    gm[2] = w[2] * dcam0 + w[6] * dcam1 + w[10] * dcam2 + dmc2;
 
     float dRS[9];
 #pragma unroll
@@ -202,7 +215,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
             dRS[a * 3 + b] = 2.0f * (dcov3[a][0] * R[0 * 3 + b] * s[b] + dcov3[a][1] * R[1 * 3 + b] * s[b] + dcov3[a][2] * R[2 * 3 + b] * s[b]);
 #pragma unroll
     for(int b = 0; b < 3; ++b)
-        g_logscale[i * 3 + b] = (dRS[0 * 3 + b] * R[0 * 3 + b] + dRS[1 * 3 + b] * R[1 * 3 + b] + dRS[2 * 3 + b] * R[2 * 3 + b]) * s[b];
+        gs[b] = (dRS[0 * 3 + b] * R[0 * 3 + b] + dRS[1 * 3 + b] * R[1 * 3 + b] + dRS[2 * 3 + b] * R[2 * 3 + b]) * s[b];
     float dR[9];
 #pragma unroll
     for(int a = 0; a < 3; ++a)
@@ -220,20 +233,36 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     const float dotq = w_ * dw + x_ * dx_ + y_ * dy_ + z_ * dz_;
     *reinterpret_cast<float4 *>(g_rotation + i * 4) =
         make_float4((dx_ - x_ * dotq) * iq, (dy_ - y_ * dotq) * iq, (dz_ - z_ * dotq) * iq, (dw - w_ * dotq) * iq);
+    }
+    /* coalesced write-out of the [256,3] gradient rows through shared memory */
+    __syncthreads();
+#pragma unroll
+    for(int c = 0; c < 3; ++c) {
+        s_m[threadIdx.x * 3 + c] = gm[c];
+        s_s[threadIdx.x * 3 + c] = gs[c];
+    }
+    __syncthreads();
+    for(int j = threadIdx.x; j < kThreads * 3; j += kThreads) {
+        if(j < avail) {
+            g_mean3d[base * 3 + j] = s_m[j];
+            g_logscale[base * 3 + j] = s_s[j];
+            g_sh0[base * 3 + j] = s_c[j];
+        }
+    }
 }
 
 } // namespace
 
 cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rotation, const float *logscale,
                                            const float *sh1, const float *sh2, const float *sh3, int sh_degree,
-                                           int64_t n, const CameraParams &cam, const uint32_t *offsets,
+                                           int64_t n, const CameraParams &cam, const uint32_t *counts,
                                            float4 *grad_acc, float *g_mean3d, float *g_rotation, float *g_logscale,
                                            float *g_opacity, float *g_sh0, float *g_sh1, float *g_sh2, float *g_sh3,
                                            cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     preprocess_backward_kernel<<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, stream>>>(
-        mean3d, rotation, logscale, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, offsets, grad_acc,
+        mean3d, rotation, logscale, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, counts, grad_acc,
         g_mean3d, g_rotation, g_logscale, g_opacity, g_sh0, g_sh1, g_sh2, g_sh3);
     return cudaGetLastError();
 }

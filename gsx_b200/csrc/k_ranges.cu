@@ -3,8 +3,8 @@
  *
  * Follows fastgs/kernels_forward.cuh:558-577 (extract_instance_ranges_cu: [start, end) per tile,
  * empty tiles stay [0, 0)) and :579-593 + forward.cu:250-256 (32-instance buckets per tile and their
- * inclusive prefix).  The per-bucket tile index that the reference's blend kernel writes
- * (kernels_forward.cuh:637-644) is written here instead, by the single-block bucket scan.
+ * inclusive prefix).  The per-bucket tile index is written by the blend forward kernel, as in the
+ * reference (kernels_forward.cuh:637-644).
  */
 #include "gsx_b200_kernels.cuh"
 
@@ -50,15 +50,11 @@ __global__ void __launch_bounds__(kScanThreads) bucket_scan_kernel(const uint2 *
     uint32_t run = woff + incl - local;
     for(int t = t0; t < t0 + per && t < n_tiles; ++t) {
         const uint2 r = ranges[t];
-        const uint32_t nb = (r.y - r.x + 31u) / 32u;
-        if((uint64_t)run + nb > bucket_capacity) {
-            atomicOr(flags, GSX_FLAG_BUCKET_OVERFLOW);
-        } else {
-            for(uint32_t b = 0; b < nb; ++b) bucket_tile[run + b] = (uint32_t)t;
-        }
-        run += nb;
+        run += (r.y - r.x + 31u) / 32u;
         bucket_offsets[t] = run;
     }
+    if(threadIdx.x == kScanThreads - 1 && (uint64_t)run > bucket_capacity) atomicOr(flags, GSX_FLAG_BUCKET_OVERFLOW);
+    (void)bucket_tile;
 }
 
 } // namespace

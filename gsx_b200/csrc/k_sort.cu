@@ -156,13 +156,13 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(const unsigned long 
     uint32_t *my_status = lookback + (uint64_t)tile * kRadix + d;
     uint32_t prefix = 0;
     if(tile == 0) {
-        gsx_st_release(my_status, kInc | count);
+        gsx_st_relaxed(my_status, kInc | count);
     } else {
-        gsx_st_release(my_status, kAgg | count);
+        gsx_st_relaxed(my_status, kAgg | count);
         int64_t j = (int64_t)tile - 1;
         unsigned spins = 0;
         while(j >= 0) {
-            const uint32_t st = gsx_ld_acquire(lookback + (uint64_t)j * kRadix + d);
+            const uint32_t st = gsx_ld_relaxed(lookback + (uint64_t)j * kRadix + d);
             const uint32_t fl = st & ~kValMask;
             if(fl == 0u) {
                 if(++spins > GSX_SPIN_LIMIT) {
@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(const unsigned long 
             if(fl == kInc) break;
             --j;
         }
-        gsx_st_release(my_status, kInc | (prefix + count));
+        gsx_st_relaxed(my_status, kInc | (prefix + count));
     }
     s_digit_base[d] = hbase + prefix;
     __syncthreads();

@@ -1,0 +1,101 @@
+"""The training step: render TRAIN -> fused L1+SSIM -> render backward -> (all-reduce) -> Adam.
+
+Mirrors one iteration of GSX's session loop (gsx-runtime.c:1413-1536, without density control)
+on the B200 path.  Parameters and gradients each live in ONE flat fp32 allocation with the GS
+field order of gsx-core.h:287-302 (mean3d, logscale, rotation, opacity, sh0..sh3), every field
+16-byte aligned, so the data-parallel gradient exchange is a single NCCL all-reduce over one
+contiguous span (no per-field launches, no packing copies).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import FORWARD_TRAIN, Adam, Camera, ParamGroup, RenderContext, Renderer, l1_ssim
+
+FIELD_ORDER = ("mean3d", "logscale", "rotation", "opacity", "sh0", "sh1", "sh2", "sh3")
+FIELD_COLS = {"mean3d": (3,), "logscale": (3,), "rotation": (4,), "opacity": (), "sh0": (3,), "sh1": (3, 3),
+              "sh2": (5, 3), "sh3": (7, 3)}
+DEFAULT_LR = {"mean3d": 1e-3, "logscale": 1e-2, "rotation": 1e-2, "opacity": 1e-2, "sh0": 1e-2, "sh1": 1e-2,
+              "sh2": 1e-2, "sh3": 1e-2}
+
+
+class GaussianModel:
+    """Gaussian parameters and gradients as views into two flat, 16-byte-aligned allocations."""
+
+    def __init__(self, arrays: dict, device="cuda:0", sh_degree: int = 0):
+        self.n = int(arrays["mean3d"].shape[0])
+        self.sh_degree = sh_degree
+        self.fields = [f for f in FIELD_ORDER if f in ("mean3d", "logscale", "rotation", "opacity", "sh0")
+                       or int(f[2]) <= sh_degree]
+        offs, o = {}, 0
+        for f in self.fields:
+            cnt = self.n * int(np.prod(FIELD_COLS[f], dtype=np.int64))
+            offs[f] = (o, cnt)
+            o += (cnt + 3) // 4 * 4
+        self.numel = o
+        self.flat_param = torch.zeros(o, dtype=torch.float32, device=device)
+        self.flat_grad = torch.zeros(o, dtype=torch.float32, device=device)
+        self.params, self.grads = {}, {}
+        for f in self.fields:
+            a, c = offs[f]
+            shape = (self.n,) + FIELD_COLS[f]
+            self.params[f] = self.flat_param[a:a + c].view(shape)
+            self.grads[f] = self.flat_grad[a:a + c].view(shape)
+            src = np.ascontiguousarray(arrays[f], dtype=np.float32).reshape(shape)
+            self.params[f].copy_(torch.from_numpy(src))
+
+
+class Trainer:
+    """One view per call of step(); `group` is a torch.distributed process group (None = 1 GPU)."""
+
+    def __init__(self, model: GaussianModel, width: int, height: int, lr: dict | None = None, l1_weight=0.8,
+                 ssim_weight=0.2, background=(0.0, 0.0, 0.0), group=None, device="cuda:0"):
+        self.model = model
+        self.renderer = Renderer(width, height)
+        self.ctx = RenderContext(torch.device(device).index or 0)
+        self.out = torch.empty((3, height, width), dtype=torch.float32, device=device)
+        self.loss_map = torch.empty_like(self.out)
+        self.grad_rgb = torch.empty_like(self.out)
+        self.loss_sum = torch.zeros(1, dtype=torch.float32, device=device)
+        self.l1_weight, self.ssim_weight = l1_weight, ssim_weight
+        self.background = background
+        self.group = group
+        lr = dict(DEFAULT_LR, **(lr or {}))
+        self.optim = Adam([ParamGroup(f, model.params[f], model.grads[f], lr[f]) for f in model.fields])
+
+    def step(self, camera: Camera, target, events=None):
+        """One training iteration on `camera` against `target` ([3,H,W] on the device).
+        Returns the device scalar holding the summed loss map of this view.  `events`, if given, is
+        ((loss_start, loss_end), (adam_start, adam_end)) CUDA events recorded around those launches."""
+        m = self.model
+        self.renderer.render(self.ctx, m.params, camera, self.out, background=self.background,
+                             sh_degree=m.sh_degree, forward_type=FORWARD_TRAIN)
+        self.loss_sum.zero_()
+        if events:
+            events[0][0].record()
+        l1_ssim(self.out, target, self.loss_map, self.grad_rgb, self.l1_weight, self.ssim_weight,
+                loss_sum=self.loss_sum, overwrite=True)
+        if events:
+            events[0][1].record()
+        self.renderer.backward(self.ctx, self.grad_rgb, m.grads)
+        if self.group is not None:
+            allreduce_mean(m.flat_grad, self.group)
+        if events:
+            events[1][0].record()
+        self.optim.step(force_all=True)
+        if events:
+            events[1][1].record()
+        return self.loss_sum
+
+
+def allreduce_mean(flat, group):
+    """In-place mean of `flat` over the ranks of `group`: one collective over the whole span.
+    NCCL averages in the collective (ReduceOp.AVG); other backends (gloo, used by the CPU tests)
+    sum and scale."""
+    import torch.distributed as dist
+    if dist.get_backend(group) == "nccl":
+        dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=group)
+    else:
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        flat.div_(dist.get_world_size(group))

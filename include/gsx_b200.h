@@ -143,9 +143,21 @@ GSX_B200_API int gsx_b200_render_get_view(gsx_b200_context *ctx, gsx_b200_render
  * lookback waits that timed out, capacity overflows) as GSX_B200_UNKNOWN; clears them. */
 GSX_B200_API int gsx_b200_context_check(gsx_b200_context *ctx, void *stream);
 
+/* Per-stage device timing of the render pipeline with CUDA events on the launching stream (the
+ * reference's session timing syncs the stream at every stage instead, gsx-runtime.c:619-680).
+ * enable != 0 starts recording (up to 256 launches per stage), enable == 0 stops.  Stages:
+ * 0 preprocess+scan, 1 key emission, 2 radix sort, 3 tile ranges, 4 blend forward, 5 blend backward,
+ * 6 preprocess backward. */
+#define GSX_B200_STAGE_COUNT 7
+GSX_B200_API int gsx_b200_context_set_profiling(gsx_b200_context *ctx, int enable);
+/* Synchronises, writes per-stage total milliseconds and launch counts since the last read
+ * (arrays of GSX_B200_STAGE_COUNT), and resets them. */
+GSX_B200_API int gsx_b200_context_read_profile(gsx_b200_context *ctx, float *total_ms, int32_t *launches);
+
 /*
  * Fused image loss on [planes, H, W] f32 CHW planes (planes = outer * channels), one launch.
- * mode bit 0: accumulate the loss map; bit 1: accumulate the gradient; bit 2: include L1.
+ * mode bit 0: accumulate the loss map; bit 1: accumulate the gradient; bit 2: include L1;
+ * bit 3: overwrite instead of accumulate (loss_map and grad are written as if they held zeros).
  * With bit 2: loss_map = (loss_map + l1_scale*|p-t|) then SSIM as below; grad += sign(p-t)*l1_grad_scale.
  * SSIM: loss_map += ssim_scale*(1-ssim) (SET to 0 within 5 pixels of the border);
  *       grad += SSIM gradient scaled by ssim_grad_scale.

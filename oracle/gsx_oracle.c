@@ -389,6 +389,9 @@ void orc_blend_forward(int width, int height, const uint32_t *ranges, const uint
  * clamped at 0.999 with zero opacity gradient when saturated, (1-alpha) floored at 1e-4.
  * `image` is the composed output (colour + T*background), as the reference's retained image.
  * Outputs (accumulated with +=): d_mean2d[N*2], d_conic[N*3], d_opacity_raw[N], d_color[N*3]. */
+static int orc_backward_consistent = 0;
+void orc_set_backward_consistent(int v) { orc_backward_consistent = v; }
+
 void orc_blend_backward(int width, int height, const uint32_t *ranges, const uint32_t *vals, const float *mean2d,
                         const float *conic_op, const float *color, const float *image, const uint32_t *n_contrib,
                         const uint32_t *tile_max, const float *grad_rgb, float *d_mean2d, float *d_conic,
@@ -429,6 +432,12 @@ void orc_blend_backward(int width, int height, const uint32_t *ranges, const uin
                                 const float cx = conic_op[p * 4 + 0], cy = conic_op[p * 4 + 1], cz = conic_op[p * 4 + 2];
                                 const float op = conic_op[p * 4 + 3];
                                 float sig = 0.5f * (cx * dx * dx + cz * dy * dy) + cy * dx * dy;
+                                if(orc_backward_consistent) {
+                                    const float fdx = mean2d[p * 2 + 0] - pxf, fdy = mean2d[p * 2 + 1] - pyf;
+                                    const float fs = fmaf(fdx, fmaf(0.5f * cx, fdx, cy * fdy), (0.5f * cz * fdy) * fdy);
+                                    if(fs < 0.0f) continue;
+                                    if(fminf(op * gsx_expf(-fs), 0.999f) < 1.0f / 255.0f) continue;
+                                }
                                 if(sig < 0.0f) sig = 0.0f;
                                 const float gauss = expf(-sig);
                                 const float a_pre = op * gauss;
