@@ -83,7 +83,10 @@ SIGNATURES = {
     "gsx_b200_adam_step": (ctypes.c_int, [ctypes.POINTER(AdamGroup), ctypes.c_int32, ctypes.c_void_p]),
     "gsx_b200_sort_pairs": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
+    "gsx_b200_sort_pairs_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32,
+                                                   ctypes.c_int32, ctypes.c_void_p]),
 }
+NOALLOC_SORT_MAX_PAIRS = 1 << 20
 
 _lib = None
 

@@ -172,6 +172,10 @@ struct StageTimer {
 
 } // namespace
 
+/* Records `msg` as this thread's last error and returns `code` (for entry points defined in other
+ * translation units of the library). */
+int gsx_internal_fail(int code, const char *msg) { return fail(code, msg); }
+
 extern "C" {
 
 const char *gsx_b200_last_error(void) { return g_last_error.c_str(); }

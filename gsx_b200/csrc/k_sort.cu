@@ -256,3 +256,82 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
     *out_result_in_b = passes & 1;
     return cudaGetLastError();
 }
+
+/* ------------------------------------------------------------------------------------------------
+ * Allocation-free variant (gsx_b200_sort_pairs_noalloc, include/gsx_b200.h).
+ *
+ * Some callers must not allocate device memory on their own: a host that hands every buffer out of
+ * its own arenas and accounts for all device memory (GSX's backend model), or code that runs while
+ * a CUDA graph is being captured.  For them the sort's scratch (the alternate key/value buffers,
+ * the digit histograms and the lookback table) lives in one file-scope device array sized for
+ * GSX_B200_NOALLOC_SORT_MAX_PAIRS pairs.  Every GPU that loads this library holds the array until
+ * the process exits.  All calls share it: calls that overlap on the GPU (different streams, or
+ * different host threads on the same device) race and must be serialised by the caller.
+ */
+#include "../../include/gsx_b200.h"
+
+#include <mutex>
+
+int gsx_internal_fail(int code, const char *msg);
+
+namespace {
+
+constexpr uint64_t kNoAllocPairs = GSX_B200_NOALLOC_SORT_MAX_PAIRS;
+constexpr size_t kNoAllocKeysBytes = (size_t)kNoAllocPairs * sizeof(unsigned long long);
+constexpr size_t kNoAllocValsBytes = (size_t)kNoAllocPairs * sizeof(uint32_t);
+constexpr size_t kNoAllocSortBytes = (size_t)(8 * kRadix + 64 + 8 * ((kNoAllocPairs + kTile - 1) / kTile) * kRadix) * 4;
+constexpr size_t kNoAllocFlagBytes = 256;
+constexpr size_t kNoAllocBytes = kNoAllocKeysBytes + kNoAllocValsBytes + kNoAllocSortBytes + kNoAllocFlagBytes;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mutex;
+unsigned char *g_noalloc_ptr[256];
+
+} // namespace
+
+extern "C" int gsx_b200_sort_pairs_noalloc(uint64_t *keys, uint32_t *values, uint64_t count, int32_t begin_bit,
+                                           int32_t end_bit, void *stream_)
+{
+    if(count > 0 && (keys == nullptr || values == nullptr))
+        return gsx_internal_fail(GSX_B200_INVALID_ARGUMENT, "keys and values must be non-null");
+    if(begin_bit < 0 || end_bit > 64 || begin_bit > end_bit)
+        return gsx_internal_fail(GSX_B200_OUT_OF_RANGE, "bit range must satisfy 0 <= begin <= end <= 64");
+    if(count > kNoAllocPairs)
+        return gsx_internal_fail(GSX_B200_OUT_OF_RANGE,
+                                 "gsx_b200_sort_pairs_noalloc: count exceeds GSX_B200_NOALLOC_SORT_MAX_PAIRS (1048576)");
+    if(count == 0 || begin_bit == end_bit) return GSX_B200_SUCCESS;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if(err != cudaSuccess) return gsx_internal_fail(GSX_B200_UNKNOWN, cudaGetErrorString(err));
+    if(dev < 0 || dev >= 256) return gsx_internal_fail(GSX_B200_OUT_OF_RANGE, "device ordinal out of range");
+    unsigned char *base = nullptr;
+    {
+        /* once per device, with that device current: the array's device address (the host-side
+         * name of the array is not a device address) */
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        if(g_noalloc_ptr[dev] == nullptr) {
+            void *p = nullptr;
+            err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if(err != cudaSuccess) return gsx_internal_fail(GSX_B200_UNKNOWN, cudaGetErrorString(err));
+            g_noalloc_ptr[dev] = static_cast<unsigned char *>(p);
+        }
+        base = g_noalloc_ptr[dev];
+    }
+    cudaStream_t stream = (cudaStream_t)stream_;
+    unsigned long long *keys_b = reinterpret_cast<unsigned long long *>(base);
+    uint32_t *vals_b = reinterpret_cast<uint32_t *>(base + kNoAllocKeysBytes);
+    void *scratch = base + kNoAllocKeysBytes + kNoAllocValsBytes;
+    uint32_t *flags = reinterpret_cast<uint32_t *>(base + kNoAllocKeysBytes + kNoAllocValsBytes + kNoAllocSortBytes);
+    int in_b = 0;
+    /* the launcher clears the histograms, tile counters and lookback table before use */
+    err = gsx_launch_sort_pairs(reinterpret_cast<unsigned long long *>(keys), values, keys_b, vals_b, count, begin_bit,
+                                end_bit, scratch, kNoAllocSortBytes, flags, &in_b, stream);
+    if(err == cudaSuccess && in_b) {
+        err = cudaMemcpyAsync(keys, keys_b, sizeof(uint64_t) * count, cudaMemcpyDeviceToDevice, stream);
+        if(err == cudaSuccess)
+            err = cudaMemcpyAsync(values, vals_b, sizeof(uint32_t) * count, cudaMemcpyDeviceToDevice, stream);
+    }
+    if(err != cudaSuccess) return gsx_internal_fail(GSX_B200_UNKNOWN, cudaGetErrorString(err));
+    return GSX_B200_SUCCESS;
+}
