@@ -126,14 +126,16 @@ struct gsx_b200_context {
     /* per primitive */
     DevBuf rec, offsets, counts, block_sums, grad_acc;
     int64_t prim_cap = 0;
-    /* per instance */
-    DevBuf keys, vals, sort_scratch;
+    /* per instance; hist = per-digit-position key histograms written by the emission kernel */
+    DevBuf keys, vals, sort_scratch, hist;
     uint64_t inst_cap = 0;
+    uint32_t *host_hist = nullptr; /* pinned copy of hist */
     /* per tile / pixel / bucket */
     DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap;
     /* small device words: [0] flags, [1] preprocess tile counter, [2..3] pad */
     DevBuf words;
     uint32_t *host_words = nullptr; /* pinned: [0] instance total, [1] flags */
+    int sort_passes = 0;            /* digit passes the last forward's sort ran */
     /* retained forward state */
     bool has_train = false;
     gsx_b200_gaussians g{};
@@ -205,6 +207,12 @@ int gsx_b200_context_create(int device, gsx_b200_context **out_ctx)
         return fail(GSX_B200_OUT_OF_MEMORY, "cudaMallocHost failed");
     }
     memset(ctx->host_words, 0, 64);
+    if(cudaMallocHost(&ctx->host_hist, 8 * 256 * sizeof(uint32_t)) != cudaSuccess) {
+        cudaFreeHost(ctx->host_words);
+        release(ctx->words);
+        delete ctx;
+        return fail(GSX_B200_OUT_OF_MEMORY, "cudaMallocHost failed");
+    }
     *out_ctx = ctx;
     return 0;
 }
@@ -216,7 +224,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     cudaDeviceSynchronize();
     DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
-                      &ctx->bucket_tile, &ctx->snap, &ctx->words };
+                      &ctx->bucket_tile, &ctx->snap, &ctx->words, &ctx->hist };
     for(DevBuf *b : all) release(*b);
     if(ctx->ev_created)
         for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
@@ -225,6 +233,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
                 cudaEventDestroy(ctx->ev[s][k][1]);
             }
     if(ctx->host_words) cudaFreeHost(ctx->host_words);
+    if(ctx->host_hist) cudaFreeHost(ctx->host_hist);
     delete ctx;
     return 0;
 }
@@ -279,7 +288,34 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     uint32_t *counts = (uint32_t *)ctx->counts.ptr;
     uint32_t *block_sums = (uint32_t *)ctx->block_sums.ptr;
 
+    /* preprocess -> block-total scan -> emission into the current instance capacity (with the key
+     * histograms) -> ONE host synchronisation (instance total, histograms); if the capacity was too
+     * small the emission is repeated into grown buffers (rare: capacity keeps 25% headroom). */
+    int tile_bits = 0;
+    while((1 << tile_bits) < n_tiles) ++tile_bits;
+    const int end_bit = 32 + tile_bits;
+    const int n_digits = (end_bit + 7) / 8;
+    if(int rc = ensure(ctx->hist, sizeof(uint32_t) * 8 * 256)) return rc;
+    uint32_t *hist = (uint32_t *)ctx->hist.ptr;
     uint64_t total = 0;
+    auto emit_into_capacity = [&](uint64_t cap) -> int {
+        /* capacity in pairs; ensure() only reallocates when the request exceeds what is held, and
+         * inst_cap is the exact floor of what is held, so a steady workload never reallocates */
+        if(cap == 0) cap = 1;
+        if(int rc = ensure(ctx->keys, sizeof(unsigned long long) * 2 * (size_t)cap)) return rc;
+        if(int rc = ensure(ctx->vals, sizeof(uint32_t) * 2 * (size_t)cap)) return rc;
+        ctx->inst_cap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
+        const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
+        if(vcap < ctx->inst_cap) ctx->inst_cap = vcap;
+        GSX_CUDA_TRY(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 8 * 256, stream), "memset");
+        GSX_CUDA_TRY(cudaMemsetAsync(words, 0, sizeof(uint32_t), stream), "memset");
+        StageTimer st(ctx, 1, stream);
+        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, block_sums, offsets, cam.grid_w,
+                                     (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr, ctx->inst_cap, words,
+                                     hist, n_digits, stream),
+                     "emit launch");
+        return 0;
+    };
     if(n > 0) {
         {
             StageTimer st0(ctx, 0, stream);
@@ -288,17 +324,24 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
                                                stream),
                          "preprocess launch");
         }
+        if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
         GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
                      "D2H");
-        GSX_CUDA_TRY(cudaStreamSynchronize(stream), "preprocess");
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_hist, hist, sizeof(uint32_t) * 8 * 256, cudaMemcpyDeviceToHost, stream), "D2H");
+        GSX_CUDA_TRY(cudaStreamSynchronize(stream), "forward");
         total = ctx->host_words[0];
+        if(total > ctx->inst_cap) {
+            if(int rc = emit_into_capacity(total + total / 4 + 1024)) return rc;
+            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_hist, hist, sizeof(uint32_t) * 8 * 256, cudaMemcpyDeviceToHost, stream),
+                         "D2H");
+            GSX_CUDA_TRY(cudaStreamSynchronize(stream), "forward");
+        }
     } else {
         GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
+        if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
     }
     ctx->n_instances = total;
     const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
-    if(int rc = ensure(ctx->keys, sizeof(unsigned long long) * 2 * (size_t)(total + 1))) return rc;
-    if(int rc = ensure(ctx->vals, sizeof(uint32_t) * 2 * (size_t)(total + 1))) return rc;
     if(int rc = ensure(ctx->sort_scratch, gsx_sort_scratch_bytes(total + 1))) return rc;
     if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
     if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
@@ -308,18 +351,23 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     uint32_t *vals_a = (uint32_t *)ctx->vals.ptr;
     uint32_t *vals_b = vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t));
     int in_b = 0;
-    if(n > 0) {
-        StageTimer st(ctx, 1, stream);
-        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, block_sums, offsets, cam.grid_w, keys_a,
-                                     vals_a, total, words, stream),
-                     "emit launch");
-    }
+    ctx->sort_passes = 0;
     if(total > 0) {
-        int tile_bits = 0;
-        while((1 << tile_bits) < n_tiles) ++tile_bits;
+        /* plan: one onesweep pass per 8-bit digit position whose digit is not the same for all keys */
+        int positions[8], shifts[8], widths[8], np = 0;
+        for(int p = 0; p < n_digits; ++p) {
+            bool trivial = false;
+            for(int b = 0; b < 256; ++b) trivial |= ctx->host_hist[p * 256 + b] == total;
+            if(trivial) continue;
+            positions[np] = p;
+            shifts[np] = 8 * p;
+            widths[np] = end_bit - 8 * p < 8 ? end_bit - 8 * p : 8;
+            ++np;
+        }
+        ctx->sort_passes = np;
         StageTimer st(ctx, 2, stream);
-        GSX_CUDA_TRY(gsx_launch_sort_pairs(keys_a, vals_a, keys_b, vals_b, total, 0, 32 + tile_bits, ctx->sort_scratch.ptr,
-                                           ctx->sort_scratch.bytes, words, &in_b, stream),
+        GSX_CUDA_TRY(gsx_launch_sort_passes(keys_a, vals_a, keys_b, vals_b, total, positions, shifts, widths, np, hist,
+                                            ctx->sort_scratch.ptr, ctx->sort_scratch.bytes, words, &in_b, stream),
                      "sort launch");
     }
     const unsigned long long *keys = in_b ? keys_b : keys_a;

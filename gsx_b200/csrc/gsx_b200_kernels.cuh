@@ -128,7 +128,11 @@ cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, co
                                   uint32_t *counts, uint32_t *block_sums, cudaStream_t stream);
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
-                            uint32_t *flags, cudaStream_t stream);
+                            uint32_t *flags, uint32_t *hist, int n_digits, cudaStream_t stream);
+cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
+                                   uint32_t *vals_b, uint64_t count, const int *positions, const int *shifts,
+                                   const int *widths, int npasses, const uint32_t *hist, void *scratch,
+                                   size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream);
 size_t gsx_sort_scratch_bytes(uint64_t capacity);
 cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
                                   uint32_t *vals_b, uint64_t count, int begin_bit, int end_bit, void *scratch,

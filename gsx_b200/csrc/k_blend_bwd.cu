@@ -246,8 +246,15 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const u
     const uint64_t per_block = (uint64_t)kWarps * 4;
     const uint64_t blocks = (bucket_capacity + per_block - 1) / per_block;
     const size_t smem = sizeof(PixIn) * kWarps * 4 * 2 * 32;
-    cudaError_t err = cudaFuncSetAttribute(blend_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static bool attr_done[256];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
+    if(dev < 0 || dev >= 256 || !attr_done[dev]) {
+        err = cudaFuncSetAttribute(blend_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if(err != cudaSuccess) return err;
+        if(dev >= 0 && dev < 256) attr_done[dev] = true;
+    }
     blend_backward_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, grid_w, n_tiles, ranges,
                                                                       bucket_offsets, bucket_tile, vals, rec, pix,
                                                                       tile_max, snap, grad_rgb, grad_acc);

@@ -6,6 +6,8 @@
  * (the same exact overlap test as the preprocess count), but writes the combined tile|depth key
  * so that one stable LSD radix sort yields the reference's (tile, then depth) order
  * (forward.cu:155-161 depth sort followed by the stable 16-bit tile sort at :214-220).
+ * It also counts, per 8-bit digit position of the emitted keys, a 256-bin histogram, from which the
+ * host plans the radix-sort passes (passes whose digit is the same for every key are skipped).
  * Compiled with -fmad=false (bit-identical overlap decisions with the preprocess and the oracle).
  */
 #include "gsx_b200_kernels.cuh"
@@ -19,9 +21,12 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                                                         const uint32_t *__restrict__ block_offsets,
                                                         uint32_t *__restrict__ offsets, unsigned grid_w,
                                                         unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
-                                                        uint64_t capacity, uint32_t *__restrict__ flags)
+                                                        uint64_t capacity, uint32_t *__restrict__ flags,
+                                                        uint32_t *__restrict__ hist, int n_digits)
 {
     __shared__ uint32_t s_warp[kThreads / 32];
+    __shared__ uint32_t s_hist[8][256];
+    for(int j = threadIdx.x; j < 8 * 256; j += kThreads) (&s_hist[0][0])[j] = 0u;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
     uint32_t cnt = i < n ? counts[i] : 0u;
@@ -40,7 +45,8 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
     const uint32_t start = block_offsets[blockIdx.x] + woff + incl - cnt;
     if(i < n) offsets[i] = start;
     if(i == n - 1) offsets[n] = start + cnt;
-    if(__ballot_sync(0xffffffffu, cnt != 0) == 0) return;
+    const bool warp_busy = __ballot_sync(0xffffffffu, cnt != 0) != 0;
+    if(warp_busy) {
     float msx = 0.0f, msy = 0.0f, cx = 0.0f, cy = 0.0f, cz = 0.0f, pt = 0.0f;
     unsigned bx0 = 0, bw = 0, by0 = 0, tmax = 0;
     unsigned long long dbits = 0;
@@ -69,9 +75,11 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
     for(unsigned k = 0; k < nseq; ++k) {
         const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
         if(gsx_tile_contributes(msx, msy, cx, cy, cz, tx, ty, pt)) {
-            keys[wpos] = ((unsigned long long)(ty * grid_w + tx) << 32) | dbits;
+            const unsigned long long key = ((unsigned long long)(ty * grid_w + tx) << 32) | dbits;
+            keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
             ++wpos;
+            for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
     }
     unsigned coop = __ballot_sync(0xffffffffu, tmax > GSX_SEQ_TILES);
@@ -94,11 +102,20 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned ballot = __ballot_sync(0xffffffffu, c);
             if(c) {
                 const uint32_t p = lpos + (uint32_t)__popc(ballot & lt_mask);
-                keys[p] = ((unsigned long long)(ty * grid_w + tx) << 32) | ldb;
+                const unsigned long long key = ((unsigned long long)(ty * grid_w + tx) << 32) | ldb;
+                keys[p] = key;
                 vals[p] = lidx;
+                for(int q = 0; q < n_digits; ++q) atomicAdd(&s_hist[q][(uint32_t)(key >> (8 * q)) & 0xffu], 1u);
             }
             lpos += (uint32_t)__popc(ballot);
         }
+    }
+    }
+    /* per-digit-position histograms of the emitted keys, for the radix sort's pass planning */
+    __syncthreads();
+    for(int j = threadIdx.x; j < n_digits * 256; j += kThreads) {
+        const uint32_t v = (&s_hist[0][0])[j];
+        if(v) atomicAdd(&hist[j], v);
     }
 }
 
@@ -106,11 +123,11 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
-                            uint32_t *flags, cudaStream_t stream)
+                            uint32_t *flags, uint32_t *hist, int n_digits, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
     emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, block_offsets, offsets, (unsigned)grid_w, keys,
-                                                            vals, capacity, flags);
+                                                            vals, capacity, flags, hist, n_digits);
     return cudaGetLastError();
 }

@@ -14,7 +14,8 @@
  * B200 design: the reference runs two kernels and keeps 3 floats per element of partials in HBM
  * between them.  Here one CTA owns a 32x32 output tile and recomputes the partials it needs on a
  * 42x42 halo region from a 52x52 input tile in shared memory, so HBM sees only the inputs, the
- * loss map and the gradient (no scratch at all).  The same kernel, with the loss or the gradient
+ * loss map and the gradient (no scratch at all); each separable pass keeps its 11-tap window in
+ * registers over a run of 6-8 outputs per thread.  The same kernel, with the loss or the gradient
  * stage compiled out, serves the standalone SSIM forward and backward calls.
  */
 #include <cuda_runtime.h>
@@ -31,29 +32,39 @@ constexpr int kIn = kOut + 4 * kR;  /* 52: input region */
 __constant__ float c_gauss[11];
 
 struct LossSmem {
-    float in_p[kIn][kIn];
-    float in_t[kIn][kIn];
-    float h[5][kIn][kMid];   /* horizontal blur of p, p^2, t, t^2, pt */
+    float in_p[kIn][kIn + 1];
+    float in_t[kIn][kIn + 1];
+    union {
+        float h[5][kIn][kMid];   /* horizontal blur of p, p^2, t, t^2, pt */
+        float h2[3][kMid][kOut]; /* horizontal blur of the partials (h is dead by then) */
+    };
     float part[3][kMid][kMid];
-    float h2[3][kMid][kOut]; /* horizontal blur of partials */
 };
 
+/*
+ * Work items: every separable pass gives each thread a short run of adjacent outputs and keeps the
+ * 11-tap window in registers, so each shared-memory value is loaded once per run instead of once
+ * per tap.
+ */
 template <bool DO_LOSS, bool DO_GRAD, bool WITH_L1>
-__global__ void __launch_bounds__(kThreads) l1_ssim_kernel(const float *__restrict__ pred, const float *__restrict__ target,
-                                                           float *__restrict__ loss_map, float *__restrict__ grad,
-                                                           float *__restrict__ loss_sum, int planes, int height, int width,
-                                                           float l1_scale, float ssim_scale, float l1_grad_scale,
-                                                           float ssim_grad_scale, bool overwrite)
+__global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__restrict__ pred, const float *__restrict__ target,
+                                                              float *__restrict__ loss_map, float *__restrict__ grad,
+                                                              float *__restrict__ loss_sum, int planes, int height, int width,
+                                                              float l1_scale, float ssim_scale, float l1_grad_scale,
+                                                              float ssim_grad_scale, bool overwrite)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     LossSmem &S = *reinterpret_cast<LossSmem *>(smem_raw);
+    float wgt[11];
+#pragma unroll
+    for(int k = 0; k < 11; ++k) wgt[k] = c_gauss[k];
     const int ox = blockIdx.x * kOut, oy = blockIdx.y * kOut;
     const size_t plane_elems = (size_t)height * (size_t)width;
     float local_sum = 0.0f;
     for(int plane = blockIdx.z; plane < planes; plane += gridDim.z) {
         const float *P = pred + (size_t)plane * plane_elems;
         const float *Tg = target + (size_t)plane * plane_elems;
-        /* stage 0: input tile with zero padding */
+        /* stage 0: 52x52 input tile with zero padding */
         for(int j = threadIdx.x; j < kIn * kIn; j += kThreads) {
             const int y = j / kIn, x = j % kIn;
             const int gy = oy - 2 * kR + y, gx = ox - 2 * kR + x;
@@ -67,110 +78,142 @@ __global__ void __launch_bounds__(kThreads) l1_ssim_kernel(const float *__restri
             S.in_t[y][x] = tv;
         }
         __syncthreads();
-        /* stage 1: horizontal blur of the five moments */
-        for(int j = threadIdx.x; j < kIn * kMid; j += kThreads) {
-            const int y = j / kMid, x = j % kMid;
-            float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, s4 = 0.0f;
+        /* stage 1: horizontal blur of the five moments; item = (row, run of 6 columns) */
+        for(int j = threadIdx.x; j < kIn * 7; j += kThreads) {
+            const int y = j / 7, x0 = (j % 7) * 6;
+            float vp[16], vt[16];
 #pragma unroll
-            for(int k = 0; k < 11; ++k) {
-                const float w = c_gauss[k];
-                const float a = S.in_p[y][x + k], b = S.in_t[y][x + k];
-                s0 += w * a;
-                s1 += w * (a * a);
-                s2 += w * b;
-                s3 += w * (b * b);
-                s4 += w * (a * b);
+            for(int k = 0; k < 16; ++k) {
+                vp[k] = S.in_p[y][x0 + k];
+                vt[k] = S.in_t[y][x0 + k];
             }
-            S.h[0][y][x] = s0;
-            S.h[1][y][x] = s1;
-            S.h[2][y][x] = s2;
-            S.h[3][y][x] = s3;
-            S.h[4][y][x] = s4;
+#pragma unroll
+            for(int o = 0; o < 6; ++o) {
+                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, s4 = 0.0f;
+#pragma unroll
+                for(int k = 0; k < 11; ++k) {
+                    const float a = vp[o + k], b = vt[o + k], w = wgt[k];
+                    s0 = fmaf(w, a, s0);
+                    s1 = fmaf(w, a * a, s1);
+                    s2 = fmaf(w, b, s2);
+                    s3 = fmaf(w, b * b, s3);
+                    s4 = fmaf(w, a * b, s4);
+                }
+                S.h[0][y][x0 + o] = s0;
+                S.h[1][y][x0 + o] = s1;
+                S.h[2][y][x0 + o] = s2;
+                S.h[3][y][x0 + o] = s3;
+                S.h[4][y][x0 + o] = s4;
+            }
         }
         __syncthreads();
-        /* stage 2: vertical blur -> SSIM, loss and partials on the 42x42 halo region */
-        for(int j = threadIdx.x; j < kMid * kMid; j += kThreads) {
-            const int y = j / kMid, x = j % kMid;
-            const int gy = oy - kR + y, gx = ox - kR + x;
-            float mu1 = 0.0f, e11 = 0.0f, mu2 = 0.0f, e22 = 0.0f, e12 = 0.0f;
+        /* stage 2: vertical blur -> SSIM, loss and partials on the 42x42 halo region;
+         * item = (column, run of 6 rows) */
+        for(int j = threadIdx.x; j < kMid * 7; j += kThreads) {
+            const int x = j % kMid, y0 = (j / kMid) * 6;
+            float mom[5][6];
 #pragma unroll
-            for(int k = 0; k < 11; ++k) {
-                const float w = c_gauss[k];
-                mu1 += w * S.h[0][y + k][x];
-                e11 += w * S.h[1][y + k][x];
-                mu2 += w * S.h[2][y + k][x];
-                e22 += w * S.h[3][y + k][x];
-                e12 += w * S.h[4][y + k][x];
-            }
-            const bool in_image = gy >= 0 && gy < height && gx >= 0 && gx < width;
-            const bool border = gy < kR || gy >= height - kR || gx < kR || gx >= width - kR;
-            const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2;
-            const float s1sq = e11 - mu1_sq, s2sq = e22 - mu2_sq, s12 = e12 - mu1 * mu2;
-            const float A = mu1_sq + mu2_sq + 1e-4f, B = s1sq + s2sq + 9e-4f;
-            const float C = 2.0f * mu1 * mu2 + 1e-4f, D = 2.0f * s12 + 9e-4f;
-            const float den = A * B;
-            if(DO_LOSS && in_image && y >= kR && y < kR + kOut && x >= kR && x < kR + kOut) {
-                const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
-                const float ssim = den == 0.0f ? 1.0f : (C * D) / den;
-                float lm = overwrite ? 0.0f : loss_map[idx];
-                if(WITH_L1) lm += l1_scale * fabsf(S.in_p[y + kR][x + kR] - S.in_t[y + kR][x + kR]);
-                lm = border ? 0.0f : lm + ssim_scale * (1.0f - ssim);
-                loss_map[idx] = lm;
-                local_sum += lm;
-            }
-            if(DO_GRAD) {
-                float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f;
-                if(in_image && !border && den != 0.0f) {
-                    const float cd = C * D;
-                    d0 = (mu2 * 2.0f * D) / den - (mu2 * 2.0f * C) / den - (mu1 * 2.0f * cd) / (A * den) + (mu1 * 2.0f * cd) / (den * B);
-                    d1 = -cd / (den * B);
-                    d2 = (2.0f * C) / den;
+            for(int q = 0; q < 5; ++q) {
+                float v[16];
+#pragma unroll
+                for(int k = 0; k < 16; ++k) v[k] = S.h[q][y0 + k][x];
+#pragma unroll
+                for(int o = 0; o < 6; ++o) {
+                    float acc = 0.0f;
+#pragma unroll
+                    for(int k = 0; k < 11; ++k) acc = fmaf(wgt[k], v[o + k], acc);
+                    mom[q][o] = acc;
                 }
-                S.part[0][y][x] = d0 * -ssim_grad_scale;
-                S.part[1][y][x] = d1 * -ssim_grad_scale;
-                S.part[2][y][x] = d2 * -ssim_grad_scale;
+            }
+#pragma unroll
+            for(int o = 0; o < 6; ++o) {
+                const int y = y0 + o;
+                const int gy = oy - kR + y, gx = ox - kR + x;
+                const float mu1 = mom[0][o], e11 = mom[1][o], mu2 = mom[2][o], e22 = mom[3][o], e12 = mom[4][o];
+                const bool in_image = gy >= 0 && gy < height && gx >= 0 && gx < width;
+                const bool border = gy < kR || gy >= height - kR || gx < kR || gx >= width - kR;
+                const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2;
+                const float s1sq = e11 - mu1_sq, s2sq = e22 - mu2_sq, s12 = e12 - mu1 * mu2;
+                const float A = mu1_sq + mu2_sq + 1e-4f, B = s1sq + s2sq + 9e-4f;
+                const float C = 2.0f * mu1 * mu2 + 1e-4f, D = 2.0f * s12 + 9e-4f;
+                const float den = A * B;
+                if(DO_LOSS && in_image && y >= kR && y < kR + kOut && x >= kR && x < kR + kOut) {
+                    const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
+                    const float ssim = den == 0.0f ? 1.0f : (C * D) / den;
+                    float lm = overwrite ? 0.0f : loss_map[idx];
+                    if(WITH_L1) lm += l1_scale * fabsf(S.in_p[y + kR][x + kR] - S.in_t[y + kR][x + kR]);
+                    lm = border ? 0.0f : lm + ssim_scale * (1.0f - ssim);
+                    loss_map[idx] = lm;
+                    local_sum += lm;
+                }
+                if(DO_GRAD) {
+                    float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f;
+                    if(in_image && !border && den != 0.0f) {
+                        const float cd = C * D;
+                        const float iden = 1.0f / den;
+                        d0 = (mu2 * 2.0f * D) * iden - (mu2 * 2.0f * C) * iden - (mu1 * 2.0f * cd) * iden / A
+                            + (mu1 * 2.0f * cd) * iden / B;
+                        d1 = -cd * iden / B;
+                        d2 = (2.0f * C) * iden;
+                    }
+                    S.part[0][y][x] = d0 * -ssim_grad_scale;
+                    S.part[1][y][x] = d1 * -ssim_grad_scale;
+                    S.part[2][y][x] = d2 * -ssim_grad_scale;
+                }
             }
         }
         if(DO_GRAD) {
             __syncthreads();
-            /* stage 3: horizontal blur of the partials */
-            for(int j = threadIdx.x; j < kMid * kOut; j += kThreads) {
-                const int y = j / kOut, x = j % kOut;
-                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+            /* stage 3: horizontal blur of the partials; item = (row, run of 8 columns) */
+            for(int j = threadIdx.x; j < kMid * 4; j += kThreads) {
+                const int y = j / 4, x0 = (j % 4) * 8;
 #pragma unroll
-                for(int k = 0; k < 11; ++k) {
-                    const float w = c_gauss[k];
-                    s0 += w * S.part[0][y][x + k];
-                    s1 += w * S.part[1][y][x + k];
-                    s2 += w * S.part[2][y][x + k];
+                for(int q = 0; q < 3; ++q) {
+                    float v[18];
+#pragma unroll
+                    for(int k = 0; k < 18; ++k) v[k] = S.part[q][y][x0 + k];
+#pragma unroll
+                    for(int o = 0; o < 8; ++o) {
+                        float acc = 0.0f;
+#pragma unroll
+                        for(int k = 0; k < 11; ++k) acc = fmaf(wgt[k], v[o + k], acc);
+                        S.h2[q][y][x0 + o] = acc;
+                    }
                 }
-                S.h2[0][y][x] = s0;
-                S.h2[1][y][x] = s1;
-                S.h2[2][y][x] = s2;
             }
             __syncthreads();
-            /* stage 4: vertical blur, chain rule, L1 gradient */
-            for(int j = threadIdx.x; j < kOut * kOut; j += kThreads) {
-                const int y = j / kOut, x = j % kOut;
-                const int gy = oy + y, gx = ox + x;
-                if(gy >= height || gx >= width) continue;
-                float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f;
+            /* stage 4: vertical blur, chain rule, L1 gradient; item = (column, run of 8 rows) */
+            for(int j = threadIdx.x; j < kOut * 4; j += kThreads) {
+                const int x = j % kOut, y0 = (j / kOut) * 8;
+                float b[3][8];
 #pragma unroll
-                for(int k = 0; k < 11; ++k) {
-                    const float w = c_gauss[k];
-                    s0 += w * S.h2[0][y + k][x];
-                    s1 += w * S.h2[1][y + k][x];
-                    s2 += w * S.h2[2][y + k][x];
+                for(int q = 0; q < 3; ++q) {
+                    float v[18];
+#pragma unroll
+                    for(int k = 0; k < 18; ++k) v[k] = S.h2[q][y0 + k][x];
+#pragma unroll
+                    for(int o = 0; o < 8; ++o) {
+                        float acc = 0.0f;
+#pragma unroll
+                        for(int k = 0; k < 11; ++k) acc = fmaf(wgt[k], v[o + k], acc);
+                        b[q][o] = acc;
+                    }
                 }
-                const float p = S.in_p[y + 2 * kR][x + 2 * kR], t = S.in_t[y + 2 * kR][x + 2 * kR];
-                const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
-                float g = overwrite ? 0.0f : grad[idx];
-                if(WITH_L1) {
-                    const float d = p - t;
-                    g += (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * l1_grad_scale;
+#pragma unroll
+                for(int o = 0; o < 8; ++o) {
+                    const int y = y0 + o;
+                    const int gy = oy + y, gx = ox + x;
+                    if(gy >= height || gx >= width) continue;
+                    const float p = S.in_p[y + 2 * kR][x + 2 * kR], t = S.in_t[y + 2 * kR][x + 2 * kR];
+                    const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
+                    float g = overwrite ? 0.0f : grad[idx];
+                    if(WITH_L1) {
+                        const float d = p - t;
+                        g += (d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f)) * l1_grad_scale;
+                    }
+                    g += b[0][o] + 2.0f * p * b[1][o] + t * b[2][o];
+                    grad[idx] = g;
                 }
-                g += s0 + 2.0f * p * s1 + t * s2;
-                grad[idx] = g;
             }
         }
         __syncthreads();
@@ -204,8 +247,15 @@ cudaError_t launch_l1_ssim(const float *pred, const float *target, float *loss_m
                            float ssim_grad_scale, bool overwrite, cudaStream_t stream)
 {
     const size_t smem = sizeof(LossSmem);
-    cudaError_t err = cudaFuncSetAttribute(l1_ssim_kernel<L, G, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static bool attr_done[256];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
+    if(dev < 0 || dev >= 256 || !attr_done[dev]) {
+        err = cudaFuncSetAttribute(l1_ssim_kernel<L, G, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if(err != cudaSuccess) return err;
+        if(dev >= 0 && dev < 256) attr_done[dev] = true;
+    }
     dim3 grid((unsigned)((width + kOut - 1) / kOut), (unsigned)((height + kOut - 1) / kOut),
               (unsigned)(planes < 65535 ? planes : 65535));
     l1_ssim_kernel<L, G, W><<<grid, kThreads, smem, stream>>>(pred, target, loss_map, grad, loss_sum, planes, height,

@@ -9,7 +9,7 @@
  * combined tile|depth key gives the same (tile, depth) order.  Only bits [begin_bit, end_bit) are
  * sorted (for the render keys: 32 depth bits plus ceil(log2(tiles)) tile bits).
  *
- * Per pass, each block takes a dynamically numbered tile of 4096 pairs (16 per thread in a
+ * Per pass, each block takes a dynamically numbered tile of 4096 pairs (8 per thread of 512, in a
  * warp-striped arrangement), ranks them with warp-level multisplit (__match_any_sync), publishes
  * per-digit counts to the lookback table, resolves its global digit offsets by looking back at
  * predecessor tiles (bounded spin: on timeout it sets GSX_FLAG_LOOKBACK_TIMEOUT and carries on
@@ -19,9 +19,9 @@
 
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kItems = 16;
+constexpr int kItems = 8;
 constexpr int kTile = kThreads * kItems; /* 4096 */
 constexpr int kRadix = 256;
 constexpr int kHistBlocks = 148 * 4;
@@ -50,9 +50,9 @@ __global__ void __launch_bounds__(kThreads) histogram_kernel(const unsigned long
         }
     }
     __syncthreads();
-    for(int p = 0; p < passes; ++p) {
-        const uint32_t v = s_hist[p][threadIdx.x];
-        if(v) atomicAdd(&hist[p * kRadix + threadIdx.x], v);
+    for(int j = threadIdx.x; j < passes * kRadix; j += kThreads) {
+        const uint32_t v = (&s_hist[0][0])[j];
+        if(v) atomicAdd(&hist[j], v);
     }
 }
 
@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(const unsigned long 
     uint32_t *s_whist = reinterpret_cast<uint32_t *>(smem + kTile * 12);                     /* kWarps * 256 */
     uint32_t *s_digit_base = s_whist + kWarps * kRadix;                                      /* 256: global base */
     uint32_t *s_block_excl = s_digit_base + kRadix;                                          /* 256 */
-    uint32_t *s_misc = s_block_excl + kRadix;                                                /* 16 */
+    uint32_t *s_misc = s_block_excl + kRadix;                                                /* 32 */
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
     if(threadIdx.x == 0) s_misc[kWarps] = atomicAdd(tile_counter, 1u);
@@ -138,24 +138,28 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(const unsigned long 
     }
     __syncthreads();
 
-    /* per digit (thread d): block count, exclusive over warps */
+    /* per digit (threads 0..255, thread d = digit d): block count, exclusive over warps */
     const int d = threadIdx.x;
+    const bool is_digit = d < kRadix;
     uint32_t count = 0;
+    if(is_digit) {
 #pragma unroll
-    for(int w = 0; w < kWarps; ++w) {
-        const uint32_t c = s_whist[w * kRadix + d];
-        s_whist[w * kRadix + d] = count;
-        count += c;
+        for(int w = 0; w < kWarps; ++w) {
+            const uint32_t c = s_whist[w * kRadix + d];
+            s_whist[w * kRadix + d] = count;
+            count += c;
+        }
     }
     /* global base of digit d = exclusive scan of the pass histogram */
-    const uint32_t hbase = block_exclusive_scan(hist[d], s_misc, nullptr);
+    const uint32_t hbase = block_exclusive_scan(is_digit ? hist[d] : 0u, s_misc, nullptr);
     const uint32_t bexcl = block_exclusive_scan(count, s_misc, nullptr);
-    s_block_excl[d] = bexcl;
+    if(is_digit) s_block_excl[d] = bexcl;
 
     /* decoupled lookback for digit d */
     uint32_t *my_status = lookback + (uint64_t)tile * kRadix + d;
     uint32_t prefix = 0;
-    if(tile == 0) {
+    if(!is_digit) {
+    } else if(tile == 0) {
         gsx_st_relaxed(my_status, kInc | count);
     } else {
         gsx_st_relaxed(my_status, kAgg | count);
@@ -177,7 +181,7 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(const unsigned long 
         }
         gsx_st_relaxed(my_status, kInc | (prefix + count));
     }
-    s_digit_base[d] = hbase + prefix;
+    if(is_digit) s_digit_base[d] = hbase + prefix;
     __syncthreads();
 
     /* stage into shared memory in block-sorted order */
@@ -201,7 +205,20 @@ __global__ void __launch_bounds__(kThreads) onesweep_kernel(const unsigned long 
     }
 }
 
-constexpr size_t kSmemBytes = (size_t)kTile * 12 + (size_t)kWarps * kRadix * 4 + 2 * kRadix * 4 + 16 * 4;
+constexpr size_t kSmemBytes = (size_t)kTile * 12 + (size_t)kWarps * kRadix * 4 + 2 * kRadix * 4 + 32 * 4;
+
+bool g_attr_set[256];
+
+cudaError_t ensure_onesweep_attr()
+{
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if(err != cudaSuccess) return err;
+    if(dev >= 0 && dev < 256 && g_attr_set[dev]) return cudaSuccess;
+    err = cudaFuncSetAttribute(onesweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if(err == cudaSuccess && dev >= 0 && dev < 256) g_attr_set[dev] = true;
+    return err;
+}
 
 } // namespace
 
@@ -229,12 +246,8 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
     uint32_t *lookback = counters + 64;
     cudaError_t err = cudaMemsetAsync(scratch, 0, need, stream);
     if(err != cudaSuccess) return err;
-    static bool attr_set = false;
-    if(!attr_set) {
-        err = cudaFuncSetAttribute(onesweep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-        if(err != cudaSuccess) return err;
-        attr_set = true;
-    }
+    err = ensure_onesweep_attr();
+    if(err != cudaSuccess) return err;
     uint64_t hblocks = (count + kThreads - 1) / kThreads;
     if(hblocks > kHistBlocks) hblocks = kHistBlocks;
     histogram_kernel<<<(unsigned)hblocks, kThreads, 0, stream>>>(keys_a, count, begin_bit, end_bit, passes, hist);
@@ -254,6 +267,44 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
         vout = tv;
     }
     *out_result_in_b = passes & 1;
+    return cudaGetLastError();
+}
+
+/* Digit passes chosen by the caller (the render pipeline skips passes whose digit is the same for
+ * every key; its emission kernel produced the per-position histograms).  hist holds 256 counters
+ * per digit position; pass i sorts the digit at bit `shifts[i]`, `widths[i]` bits wide, using
+ * hist + positions[i] * 256.  scratch holds the tile counters and lookback tables. */
+cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
+                                   uint32_t *vals_b, uint64_t count, const int *positions, const int *shifts,
+                                   const int *widths, int npasses, const uint32_t *hist, void *scratch,
+                                   size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream)
+{
+    *out_result_in_b = 0;
+    if(count == 0 || npasses == 0) return cudaSuccess;
+    if(count >= (1ull << 30) || npasses > 8) return cudaErrorInvalidValue;
+    const uint64_t tiles = (count + kTile - 1) / kTile;
+    const size_t need = (size_t)(64 + (uint64_t)npasses * tiles * kRadix) * 4;
+    if(scratch_bytes < need) return cudaErrorInvalidValue;
+    uint32_t *counters = reinterpret_cast<uint32_t *>(scratch);
+    uint32_t *lookback = counters + 64;
+    cudaError_t err = cudaMemsetAsync(scratch, 0, need, stream);
+    if(err != cudaSuccess) return err;
+    err = ensure_onesweep_attr();
+    if(err != cudaSuccess) return err;
+    unsigned long long *kin = keys_a, *kout = keys_b;
+    uint32_t *vin = vals_a, *vout = vals_b;
+    for(int p = 0; p < npasses; ++p) {
+        onesweep_kernel<<<(unsigned)tiles, kThreads, kSmemBytes, stream>>>(
+            kin, vin, kout, vout, count, shifts[p], (1u << widths[p]) - 1u, hist + positions[p] * kRadix,
+            lookback + (uint64_t)p * tiles * kRadix, counters + p, flags);
+        unsigned long long *tk = kin;
+        kin = kout;
+        kout = tk;
+        uint32_t *tv = vin;
+        vin = vout;
+        vout = tv;
+    }
+    *out_result_in_b = npasses & 1;
     return cudaGetLastError();
 }
 
