@@ -38,6 +38,11 @@ struct PixIn {
     float4 grad; /* upstream dL/drgb (x, y, z) */
 };
 
+struct SegStage {
+    PixIn buf[2][32];
+    float4 pad;
+};
+
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem)
 {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -81,7 +86,9 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     float4 *__restrict__ grad_acc)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    PixIn(*s_in)[4][2][32] = reinterpret_cast<PixIn(*)[4][2][32]>(smem_raw);
+    /* per warp, per segment: 2 x 32 PixIn + one float4 of padding, so the four segment heads read
+     * different banks */
+    SegStage *s_in = reinterpret_cast<SegStage *>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sub = lane & 7;
     const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
@@ -129,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     const size_t P = (size_t)width * (size_t)height;
     const float4 *bsnap = snap + (size_t)bucket * GSX_TILE_PIXELS;
     const int seg = lane >> 3;
-    PixIn(*stage)[32] = s_in[warp][seg];
+    PixIn(*stage)[32] = s_in[warp * 4 + seg].buf;
 
     /* the 8 lanes of a segment prefetch 32 pixels' inputs (snapshot, composed colour + last
      * contributor, upstream gradient) into shared memory, one batch ahead, with cp.async */
@@ -245,7 +252,7 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const u
     if(bucket_capacity == 0 || n_tiles <= 0) return cudaSuccess;
     const uint64_t per_block = (uint64_t)kWarps * 4;
     const uint64_t blocks = (bucket_capacity + per_block - 1) / per_block;
-    const size_t smem = sizeof(PixIn) * kWarps * 4 * 2 * 32;
+    const size_t smem = sizeof(SegStage) * kWarps * 4;
     static bool attr_done[256];
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);

@@ -9,8 +9,9 @@
  * (written for every bucket of every batch the tile processes, as the reference does), and
  * out = colour + (1 - alpha) * background.
  *
- * B200 organisation: each warp owns an 8x4 pixel block of the tile.  After a batch of 256
- * instances is staged in shared memory, every warp builds the ordered list of staged instances
+ * B200 organisation: each warp owns an 8x4 pixel block of the tile.  After a round of up to 512
+ * instances is staged in shared memory (long rounds keep the warps, whose lists differ in length,
+ * from waiting on each other at barriers), every warp builds the ordered list of staged instances
  * whose opacity-aware footprint can reach its block: the exact minimum of the instance's
  * quadratic form over the block's pixel-centre rectangle is compared with ln(255 * opacity) plus
  * a safety margin (the conic is bounded by the +0.3 dilation, so the float rounding of a pixel's
@@ -25,6 +26,14 @@ namespace {
 
 constexpr int kThreads = GSX_TILE_PIXELS;
 constexpr int kWarps = kThreads / 32;
+constexpr int kChunk = 512; /* instances staged per round: 2 per thread */
+
+struct FwdSmem {
+    float4 a[kChunk]; /* mean2d.x, mean2d.y, conic.x / 2, conic.y */
+    float4 b[kChunk]; /* conic.z / 2, opacity, clamped r, g */
+    float4 c[kChunk]; /* clamped b, cull threshold, 1/conic.x, 1/conic.z */
+    uint16_t list[kWarps][kChunk];
+};
 
 /* minimum of q(d) = hcx dx^2 + cy dx dy + hcz dy^2, d = m - p, over p in [x0,x1] x [y0,y1] */
 __device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, float cy, float hcz, float icx, float icz,
@@ -53,10 +62,8 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, float *__restrict__ out_rgb,
     float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile)
 {
-    __shared__ float4 s_a[kThreads]; /* mean2d.x, mean2d.y, conic.x / 2, conic.y */
-    __shared__ float4 s_b[kThreads]; /* conic.z / 2, opacity, clamped r, g */
-    __shared__ float4 s_c[kThreads]; /* clamped b, cull threshold, 1/conic.x, 1/conic.z */
-    __shared__ uint8_t s_list[kWarps][kThreads];
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    FwdSmem &S = *reinterpret_cast<FwdSmem *>(smem_raw);
     __shared__ uint32_t s_max[kWarps];
     const int tile = blockIdx.x;
     const int tx = tile % grid_w, ty = tile / grid_w;
@@ -76,18 +83,21 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     uint32_t ncon = 0;
     bool done = !inside;
     const int total = (int)(range.y - range.x);
-    for(int start = 0; start < total; start += kThreads) {
+    for(int start = 0; start < total; start += kChunk) {
         if(__syncthreads_count(done) == kThreads) break;
-        const int fetch = start + (int)threadIdx.x;
-        if(fetch < total) {
-            const PrimRec r = rec[vals[range.x + fetch]];
-            const float thr = __logf(r.b.y * 255.0f);
-            s_a[threadIdx.x] = make_float4(r.a.x, r.a.y, 0.5f * r.a.z, r.a.w);
-            s_b[threadIdx.x] = make_float4(0.5f * r.b.x, r.b.y, fmaxf(r.b.z, 0.0f), fmaxf(r.b.w, 0.0f));
-            s_c[threadIdx.x] = make_float4(fmaxf(r.c.x, 0.0f), thr + 0.05f + 1e-3f * fabsf(thr), 1.0f / r.a.z, 1.0f / r.b.x);
+        const int batch = total - start < kChunk ? total - start : kChunk;
+#pragma unroll
+        for(int q = 0; q < kChunk / kThreads; ++q) {
+            const int e = q * kThreads + (int)threadIdx.x;
+            if(e < batch) {
+                const PrimRec r = rec[vals[range.x + start + e]];
+                const float thr = __logf(r.b.y * 255.0f);
+                S.a[e] = make_float4(r.a.x, r.a.y, 0.5f * r.a.z, r.a.w);
+                S.b[e] = make_float4(0.5f * r.b.x, r.b.y, fmaxf(r.b.z, 0.0f), fmaxf(r.b.w, 0.0f));
+                S.c[e] = make_float4(fmaxf(r.c.x, 0.0f), thr + 0.05f + 1e-3f * fabsf(thr), 1.0f / r.a.z, 1.0f / r.b.x);
+            }
         }
         __syncthreads();
-        const int batch = total - start < kThreads ? total - start : kThreads;
         /* ordered list of the staged instances that can reach this warp's 8x4 block */
         int cnt = 0;
         if(__any_sync(0xffffffffu, !done)) {
@@ -96,11 +106,11 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
                 const int e = k * 32 + lane;
                 bool pass = false;
                 if(e < batch) {
-                    const float4 a = s_a[e], b = s_b[e], c = s_c[e];
+                    const float4 a = S.a[e], b = S.b[e], c = S.c[e];
                     pass = rect_min_power(a.x, a.y, a.z, a.w, b.x, c.z, c.w, rx0, rx1, ry0, ry1) <= c.y;
                 }
                 const unsigned m = __ballot_sync(0xffffffffu, pass);
-                if(pass) s_list[warp][cnt + __popc(m & ((1u << lane) - 1u))] = (uint8_t)e;
+                if(pass) S.list[warp][cnt + __popc(m & ((1u << lane) - 1u))] = (uint16_t)e;
                 cnt += __popc(m);
             }
         }
@@ -111,12 +121,12 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
             ++bucket;
             const int bend = (kb + 1) * 32;
             for(; li < cnt; ++li) {
-                const int e = s_list[warp][li];
+                const int e = S.list[warp][li];
                 if(e >= bend) break;
                 if(done) continue;
-                const float4 a = s_a[e];
+                const float4 a = S.a[e];
                 const float dx = a.x - pxf, dy = a.y - pyf;
-                const float4 b = s_b[e];
+                const float4 b = S.b[e];
                 const float sigma = fmaf(dx, fmaf(a.z, dx, a.w * dy), (b.x * dy) * dy);
                 if(sigma < 0.0f || sigma > 5.6f) continue;
                 const float g = gsx_expf_inrange(-sigma);
@@ -125,13 +135,12 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
                 const float w = T * alpha;
                 cr = fmaf(w, b.z, cr);
                 cg = fmaf(w, b.w, cg);
-                cb = fmaf(w, s_c[e].x, cb);
+                cb = fmaf(w, S.c[e].x, cb);
                 T = T * (1.0f - alpha);
                 ncon = (uint32_t)(start + e + 1);
                 if(T < 1e-4f) done = true;
             }
         }
-        __syncthreads();
     }
     if(inside) {
         const size_t P = (size_t)width * (size_t)height;
@@ -165,7 +174,16 @@ cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_ti
                                      uint32_t *bucket_tile, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
-    blend_forward_kernel<<<(unsigned)n_tiles, kThreads, 0, stream>>>(
+    static bool attr_done[256];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if(err != cudaSuccess) return err;
+    if(dev < 0 || dev >= 256 || !attr_done[dev]) {
+        err = cudaFuncSetAttribute(blend_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FwdSmem));
+        if(err != cudaSuccess) return err;
+        if(dev >= 0 && dev < 256) attr_done[dev] = true;
+    }
+    blend_forward_kernel<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(
         width, height, grid_w, ranges, bucket_offsets, vals, rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
         tile_max, snap, bucket_tile);
     return cudaGetLastError();

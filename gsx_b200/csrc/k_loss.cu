@@ -31,20 +31,22 @@ constexpr int kIn = kOut + 4 * kR;  /* 52: input region */
 
 __constant__ float c_gauss[11];
 
+/* row strides are odd (53, 43, 33) so that lanes walking down a column hit distinct banks */
 struct LossSmem {
     float in_p[kIn][kIn + 1];
     float in_t[kIn][kIn + 1];
     union {
-        float h[5][kIn][kMid];   /* horizontal blur of p, p^2, t, t^2, pt */
-        float h2[3][kMid][kOut]; /* horizontal blur of the partials (h is dead by then) */
+        float h[5][kIn][kMid + 1];   /* horizontal blur of p, p^2, t, t^2, pt */
+        float h2[3][kMid][kOut + 1]; /* horizontal blur of the partials (h is dead by then) */
     };
-    float part[3][kMid][kMid];
+    float part[3][kMid][kMid + 1];
 };
 
 /*
  * Work items: every separable pass gives each thread a short run of adjacent outputs and keeps the
  * 11-tap window in registers, so each shared-memory value is loaded once per run instead of once
- * per tap.
+ * per tap.  Horizontal passes put consecutive lanes on consecutive rows, vertical passes on
+ * consecutive columns.
  */
 template <bool DO_LOSS, bool DO_GRAD, bool WITH_L1>
 __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__restrict__ pred, const float *__restrict__ target,
@@ -80,7 +82,7 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
         __syncthreads();
         /* stage 1: horizontal blur of the five moments; item = (row, run of 6 columns) */
         for(int j = threadIdx.x; j < kIn * 7; j += kThreads) {
-            const int y = j / 7, x0 = (j % 7) * 6;
+            const int y = j % kIn, x0 = (j / kIn) * 6;
             float vp[16], vt[16];
 #pragma unroll
             for(int k = 0; k < 16; ++k) {
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
             __syncthreads();
             /* stage 3: horizontal blur of the partials; item = (row, run of 8 columns) */
             for(int j = threadIdx.x; j < kMid * 4; j += kThreads) {
-                const int y = j / 4, x0 = (j % 4) * 8;
+                const int y = j % kMid, x0 = (j / kMid) * 8;
 #pragma unroll
                 for(int q = 0; q < 3; ++q) {
                     float v[18];
