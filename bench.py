@@ -264,6 +264,14 @@ def main():
         }
         dom_ms = stage_avg[dom]
         achieved = algo_bytes[dom] / (dom_ms / 1000.0) / 1e9
+        traffic = None
+        tpath = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tpath):
+            with open(tpath) as f:
+                tr = json.load(f).get(dom)
+            if tr:
+                units = {"instances": I, "parameters": model.numel, "gaussians": n, "pixels": P}[tr["unit"]]
+                traffic = tr["dram_bytes"] / tr["units"] * units
         n_tiles = ((W + 15) // 16) * ((H + 15) // 16)
         sort_passes = (32 + (n_tiles - 1).bit_length() + 7) // 8
         # preprocess, emit, histogram + one onesweep per pass, ranges + bucket scan, blend fwd,
@@ -292,7 +300,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
             "gpu_launches": kernel_launches * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None, "peak_source": peak_kind,
+                         "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_kind,
                          "avg_ms": dom_ms, "algorithmic_bytes": algo_bytes[dom]},
             "stages_ms": {k: round(v, 4) for k, v in stage_avg.items()},
             "cpu_baseline": cpu_baseline,

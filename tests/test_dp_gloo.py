@@ -1,0 +1,108 @@
+"""Host-side data-parallel logic on CPU (gloo, world size 2): no GPU needed.
+
+Covers what the multi-GPU training step does besides the kernels: the flat gradient layout (one
+collective per step), the averaging all-reduce (NCCL AVG on the GPU, SUM + scale on gloo), replicas
+staying identical after an update, and a rank that dies before the collective being detected by the
+survivor as an error instead of a hang.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from gsx_b200.train import FIELD_ORDER, GaussianModel, allreduce_mean
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _scene(n, seed):
+    rng = np.random.default_rng(seed)
+    return dict(mean3d=rng.normal(size=(n, 3)).astype(np.float32), rotation=rng.normal(size=(n, 4)).astype(np.float32),
+                logscale=rng.normal(size=(n, 3)).astype(np.float32), opacity=rng.normal(size=n).astype(np.float32),
+                sh0=rng.normal(size=(n, 3)).astype(np.float32), sh1=rng.normal(size=(n, 3, 3)).astype(np.float32))
+
+
+def _worker(rank, world, port, mode, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    try:
+        model = GaussianModel(_scene(101, 0), device="cpu", sh_degree=1)
+        if mode == "dead_peer":
+            if rank == 1:
+                os._exit(0)  # leaves between steps, before the collective
+            try:
+                allreduce_mean(model.flat_grad, dist.group.WORLD)
+                out.put((rank, "no error"))
+            except Exception as e:  # noqa: BLE001 - any backend error is the detection we want
+                out.put((rank, "detected: " + type(e).__name__))
+            return
+        # rank-specific gradients, then one averaging collective over the whole flat span
+        for i, f in enumerate(model.fields):
+            model.grads[f].fill_(float(rank + 1) * (i + 1))
+        allreduce_mean(model.flat_grad, dist.group.WORLD)
+        lr = 0.1
+        model.flat_param.sub_(lr * model.flat_grad)  # stand-in update: identical on every rank
+        out.put((rank, model.flat_grad.numpy().copy(), model.flat_param.numpy().copy(),
+                 {f: (model.params[f].data_ptr() - model.flat_param.data_ptr()) for f in model.fields}))
+    finally:
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                pass
+
+
+def _run(mode, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    for _ in range(world if mode != "dead_peer" else 1):
+        results.append(q.get(timeout=60))
+    for p in procs:
+        p.join(timeout=60)
+    return results
+
+
+def test_flat_layout_is_aligned_and_in_gsx_field_order():
+    m = GaussianModel(_scene(37, 1), device="cpu", sh_degree=1)
+    assert m.fields == [f for f in FIELD_ORDER if f in m.fields]
+    prev = -1
+    for f in m.fields:
+        off = m.params[f].data_ptr() - m.flat_param.data_ptr()
+        assert off % 16 == 0 and off > prev
+        prev = off
+        assert m.grads[f].data_ptr() - m.flat_grad.data_ptr() == off
+    np.testing.assert_array_equal(m.params["sh1"].numpy(), _scene(37, 1)["sh1"])
+
+
+def test_gradient_average_and_replicas_stay_identical():
+    res = sorted(_run("ok"), key=lambda r: r[0])
+    (_, g0, p0, off0), (_, g1, p1, off1) = res
+    np.testing.assert_array_equal(g0, g1)
+    np.testing.assert_array_equal(p0, p1)
+    assert off0 == off1
+    # mean of (1 * k) and (2 * k) for field k
+    m = GaussianModel(_scene(101, 0), device="cpu", sh_degree=1)
+    for i, f in enumerate(m.fields):
+        a = off0[f] // 4
+        assert g0[a] == pytest.approx(1.5 * (i + 1))
+
+
+def test_dead_peer_is_detected_not_hung():
+    res = _run("dead_peer")
+    assert res[0][0] == 0
+    assert res[0][1].startswith("detected"), res
