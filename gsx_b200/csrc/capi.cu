@@ -116,6 +116,10 @@ CameraParams make_camera(const gsx_b200_camera &c)
     p.height = c.height;
     p.grid_w = (c.width + GSX_TILE - 1) / GSX_TILE;
     p.grid_h = (c.height + GSX_TILE - 1) / GSX_TILE;
+    p.clip_l = (-0.15f * p.width_f - p.cx) / p.fx;
+    p.clip_r = (1.15f * p.width_f - p.cx) / p.fx;
+    p.clip_t = (-0.15f * p.height_f - p.cy) / p.fy;
+    p.clip_b = (1.15f * p.height_f - p.cy) / p.fy;
     return p;
 }
 
@@ -124,7 +128,7 @@ CameraParams make_camera(const gsx_b200_camera &c)
 struct gsx_b200_context {
     int device = 0;
     /* per primitive */
-    DevBuf rec, offsets, counts, block_sums, grad_acc;
+    DevBuf rec, offsets, counts, tile_masks, block_sums, grad_acc;
     int64_t prim_cap = 0;
     /* per instance; hist = per-digit-position key histograms written by the emission kernel */
     DevBuf keys, vals, sort_scratch, hist;
@@ -222,7 +226,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     if(ctx == nullptr) return 0;
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
-    DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
+    DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->tile_masks, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
                       &ctx->bucket_tile, &ctx->snap, &ctx->words, &ctx->hist };
     for(DevBuf *b : all) release(*b);
@@ -278,6 +282,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     }
     if(int rc = ensure(ctx->offsets, sizeof(uint32_t) * (size_t)(n + 1))) return rc;
     if(int rc = ensure(ctx->counts, sizeof(uint32_t) * (size_t)(n + 1))) return rc;
+    if(int rc = ensure(ctx->tile_masks, sizeof(uint32_t) * (size_t)(n + 1))) return rc;
     if(int rc = ensure(ctx->block_sums, sizeof(uint32_t) * (size_t)(pblocks + 1))) return rc;
     if(int rc = ensure(ctx->ranges, sizeof(uint2) * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->bucket_offsets, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
@@ -286,6 +291,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     uint32_t *words = (uint32_t *)ctx->words.ptr;
     uint32_t *offsets = (uint32_t *)ctx->offsets.ptr;
     uint32_t *counts = (uint32_t *)ctx->counts.ptr;
+    uint32_t *tile_masks = (uint32_t *)ctx->tile_masks.ptr;
     uint32_t *block_sums = (uint32_t *)ctx->block_sums.ptr;
 
     /* preprocess -> block-total scan -> emission into the current instance capacity (with the key
@@ -310,7 +316,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         GSX_CUDA_TRY(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 8 * 256, stream), "memset");
         GSX_CUDA_TRY(cudaMemsetAsync(words, 0, sizeof(uint32_t), stream), "memset");
         StageTimer st(ctx, 1, stream);
-        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, block_sums, offsets, cam.grid_w,
+        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets, cam.grid_w,
                                      (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr, ctx->inst_cap, words,
                                      hist, n_digits, stream),
                      "emit launch");
@@ -320,8 +326,8 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         {
             StageTimer st0(ctx, 0, stream);
             GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2,
-                                               g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, block_sums,
-                                               stream),
+                                               g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, tile_masks,
+                                               block_sums, stream),
                          "preprocess launch");
         }
         if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;

@@ -5,6 +5,7 @@
  *   per primitive (capacity N):
  *     rec      PrimRec[N]   48 B: {mean2d.xy, conic.xy} {conic.z, opacity, rgb.rg} {rgb.b, depth, bx, by}
  *     counts   u32[N]       exact tile-overlap count (0 = culled); block_sums u32[N/256+1]
+ *     tile_masks u32[N]     which tiles of the bounding rectangle (row-major, rectangles <= 32 tiles) overlap
  *     offsets  u32[N+1]     exclusive prefix of the counts (written by the emission kernel)
  *     grad_acc float4[3N]   per-primitive 2-D gradient accumulators of the blend backward
  *   per instance (capacity I): keys u64[2I], values u32[2I] (double-buffered radix sort)
@@ -45,6 +46,9 @@ struct CameraParams {
     float near_plane, far_plane;
     int width, height;
     int grid_w, grid_h;
+    /* frustum clamp of the EWA Jacobian in normalised image coordinates (kernels_forward.cuh:324-327),
+     * divided once on the host (IEEE, identical bits to a device division) */
+    float clip_l, clip_r, clip_t, clip_b;
 };
 
 /* Decoupled-lookback status word: 2-bit flag in the top bits, 30-bit count below. */
@@ -125,8 +129,9 @@ struct RenderScratch;
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
-                                  uint32_t *counts, uint32_t *block_sums, cudaStream_t stream);
-cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *block_offsets,
+                                  uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, cudaStream_t stream);
+cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
+                            const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
                             uint32_t *flags, uint32_t *hist, int n_digits, cudaStream_t stream);
 cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,

@@ -198,6 +198,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
                 T = sn.w;
             }
         }
+        /* whole warp past every pixel's last contributor: nothing to add, state unchanged */
+        if(!__any_sync(0xffffffffu, valid && tpi[0] < last)) continue;
         if(!valid) continue;
         const float fx = (float)qx, fy = (float)qy;
 #pragma unroll

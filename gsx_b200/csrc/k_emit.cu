@@ -18,6 +18,7 @@ constexpr int kThreads = 256;
 
 __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec *__restrict__ rec,
                                                         const uint32_t *__restrict__ counts,
+                                                        const uint32_t *__restrict__ tile_masks,
                                                         const uint32_t *__restrict__ block_offsets,
                                                         uint32_t *__restrict__ offsets, unsigned grid_w,
                                                         unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
@@ -71,6 +72,21 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
         }
     }
     uint32_t wpos = start;
+    if(tmax > 0 && tmax <= 32u) {
+        /* the preprocess already ran the exact overlap test for rectangles of up to 32 tiles */
+        unsigned m = tile_masks[i];
+        while(m) {
+            const unsigned k = (unsigned)__ffs(m) - 1u;
+            m &= m - 1u;
+            const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
+            const unsigned long long key = ((unsigned long long)(ty * grid_w + tx) << 32) | dbits;
+            keys[wpos] = key;
+            vals[wpos] = (uint32_t)i;
+            ++wpos;
+            for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
+        }
+        tmax = 0; /* done: neither the sequential nor the cooperative pass below runs */
+    }
     const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
     for(unsigned k = 0; k < nseq; ++k) {
         const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
@@ -121,13 +137,14 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 
 } // namespace
 
-cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *block_offsets,
+cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
+                            const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
                             uint32_t *flags, uint32_t *hist, int n_digits, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
-    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, block_offsets, offsets, (unsigned)grid_w, keys,
+    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, keys,
                                                             vals, capacity, flags, hist, n_digits);
     return cudaGetLastError();
 }

@@ -80,7 +80,8 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     const float *__restrict__ mean3d, const float *__restrict__ rotation, const float *__restrict__ logscale,
     const float *__restrict__ opacity_raw, const float *__restrict__ sh0, const float *__restrict__ sh1,
     const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n, CameraParams cam,
-    PrimRec *__restrict__ rec, uint32_t *__restrict__ counts, uint32_t *__restrict__ block_sums)
+    PrimRec *__restrict__ rec, uint32_t *__restrict__ counts, uint32_t *__restrict__ tile_masks,
+    uint32_t *__restrict__ block_sums)
 {
     __shared__ float s_m[kThreads * 3];
     __shared__ float s_s[kThreads * 3];
@@ -146,8 +147,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
             const float c33 = RS[6] * R[6] + RS[7] * R[7] + RS[8] * R[8];
             const float x = (w[0] * m[0] + w[1] * m[1] + w[2] * m[2] + w[3]) / depth;
             const float y = (w[4] * m[0] + w[5] * m[1] + w[6] * m[2] + w[7]) / depth;
-            const float clip_l = (-0.15f * cam.width_f - cam.cx) / cam.fx, clip_r = (1.15f * cam.width_f - cam.cx) / cam.fx;
-            const float clip_t = (-0.15f * cam.height_f - cam.cy) / cam.fy, clip_b = (1.15f * cam.height_f - cam.cy) / cam.fy;
+            const float clip_l = cam.clip_l, clip_r = cam.clip_r, clip_t = cam.clip_t, clip_b = cam.clip_b;
             const float tx = fmaxf(clip_l, fminf(x, clip_r));
             const float ty = fmaxf(clip_t, fminf(y, clip_b));
             const float j11 = cam.fx / depth, j13 = -j11 * tx, j22 = cam.fy / depth, j23 = -j22 * ty;
@@ -191,10 +191,13 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     const unsigned bw = bx1 - bx0;
     const unsigned tmax = active ? bw * (by1 - by0) : 0u;
     const float msx = m2x - 0.5f, msy = m2y - 0.5f;
-    unsigned cnt = 0;
+    unsigned cnt = 0, tmask = 0;
     const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
     for(unsigned k = 0; k < nseq; ++k) {
-        if(gsx_tile_contributes(msx, msy, conx, cony, conz, bx0 + k % bw, by0 + k / bw, pt)) ++cnt;
+        if(gsx_tile_contributes(msx, msy, conx, cony, conz, bx0 + k % bw, by0 + k / bw, pt)) {
+            ++cnt;
+            tmask |= 1u << k;
+        }
     }
     unsigned coop = __ballot_sync(0xffffffffu, tmax > GSX_SEQ_TILES);
     while(coop) {
@@ -205,13 +208,18 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
         const float lmx = __shfl_sync(0xffffffffu, msx, L), lmy = __shfl_sync(0xffffffffu, msy, L);
         const float lcx = __shfl_sync(0xffffffffu, conx, L), lcy = __shfl_sync(0xffffffffu, cony, L);
         const float lcz = __shfl_sync(0xffffffffu, conz, L), lpt = __shfl_sync(0xffffffffu, pt, L);
-        unsigned sum = 0;
+        unsigned sum = 0, first = 0;
         for(unsigned base = GSX_SEQ_TILES; base < ltmax; base += 32u) {
             const unsigned k = base + (unsigned)lane;
             const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, lbx0 + k % lbw, lby0 + k / lbw, lpt);
-            sum += (unsigned)__popc(__ballot_sync(0xffffffffu, c));
+            const unsigned b = __ballot_sync(0xffffffffu, c);
+            if(base == GSX_SEQ_TILES) first = b;
+            sum += (unsigned)__popc(b);
         }
-        if(lane == L) cnt += sum;
+        if(lane == L) {
+            cnt += sum;
+            if(ltmax <= 32u) tmask |= first << GSX_SEQ_TILES;
+        }
     }
     if(cnt == 0) active = false;
 
@@ -225,7 +233,10 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
         rec[i] = r;
     }
 
-    if(i < n) counts[i] = cnt;
+    if(i < n) {
+        counts[i] = cnt;
+        tile_masks[i] = tmask;
+    }
     unsigned sum = cnt;
 #pragma unroll
     for(int d = 16; d > 0; d >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, d);
@@ -275,13 +286,13 @@ __global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t *__restrict__
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
-                                  uint32_t *counts, uint32_t *block_sums, cudaStream_t stream)
+                                  uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
     preprocess_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(
         mean3d, rotation, logscale, opacity, sh0, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, rec, counts,
-        block_sums);
+        tile_masks, block_sums);
     block_scan_kernel<<<1, 1024, 0, stream>>>(block_sums, (int)blocks);
     return cudaGetLastError();
 }

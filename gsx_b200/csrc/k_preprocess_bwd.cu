@@ -160,8 +160,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
 #pragma unroll
         for(int b = 0; b < 3; ++b)
             cov[a][b] = R[a * 3 + 0] * var[0] * R[b * 3 + 0] + R[a * 3 + 1] * var[1] * R[b * 3 + 1] + R[a * 3 + 2] * var[2] * R[b * 3 + 2];
-    const float cl = (-0.15f * cam.width_f - cam.cx) / cam.fx, cr = (1.15f * cam.width_f - cam.cx) / cam.fx;
-    const float ct = (-0.15f * cam.height_f - cam.cy) / cam.fy, cb = (1.15f * cam.height_f - cam.cy) / cam.fy;
+    const float cl = cam.clip_l, cr = cam.clip_r, ct = cam.clip_t, cb = cam.clip_b;
     const float tx = fmaxf(cl, fminf(x, cr)), ty = fmaxf(ct, fminf(y, cb));
     const float j11 = cam.fx / depth, j13 = -j11 * tx, j22 = cam.fy / depth, j23 = -j22 * ty;
     const float a1[3] = { j11 * w[0] + j13 * w[8], j11 * w[1] + j13 * w[9], j11 * w[2] + j13 * w[10] };
