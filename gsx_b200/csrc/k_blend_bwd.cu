@@ -28,8 +28,46 @@ constexpr int kWarps = 8;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kPerLane = 4;
 
-struct Frag {
-    float mx, my, hcx, cy, hcz, op, r, g, b;
+/* A pair of f32 in one 64-bit register: Blackwell's packed FP32 instructions (add/sub/mul/fma
+ * .rn.f32x2) do both lanes of a pair in one issue, with the same IEEE rounding as two scalar ops. */
+typedef unsigned long long f2;
+
+__device__ __forceinline__ f2 pk(float lo, float hi)
+{
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk(f2 v, float &lo, float &hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b)
+{
+    f2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b)
+{
+    f2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b)
+{
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c)
+{
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+/* two consecutive instances of a lane, field by field (lo = the earlier instance); conic terms
+ * scaled by -log2(e), lop = log2(opacity), colours clamped at 0 */
+struct FragPair {
+    f2 mx, my, nhcx, ncy, nhcz, lop, r, g, b;
 };
 
 struct PixIn {
@@ -107,30 +145,46 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     }
     if(__ballot_sync(0xffffffffu, seg_active) == 0) return;
 
-    /* this lane's four instances */
-    Frag f[kPerLane];
+    /* this lane's four instances, as two pairs */
+    FragPair f[kPerLane / 2];
     uint32_t prim[kPerLane];
     int tpi[kPerLane];
+    float fv[kPerLane][9];
 #pragma unroll
     for(int k = 0; k < kPerLane; ++k) {
         tpi[k] = tb * 32 + sub * kPerLane + k;
         prim[k] = 0xffffffffu;
-        f[k] = Frag{ 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f };
+#pragma unroll
+        for(int q = 0; q < 9; ++q) fv[k][q] = 0.0f;
+        fv[k][5] = -126.0f; /* log2 opacity of an empty slot: alpha underflows to 0 */
         if(seg_active && tpi[k] < n_inst) {
             prim[k] = vals[inst0 + tpi[k]];
             const PrimRec r = rec[prim[k]];
-            f[k] = Frag{ r.a.x - 0.5f, r.a.y - 0.5f, 0.5f * r.a.z, r.a.w, 0.5f * r.b.x, r.b.y,
-                         fmaxf(r.b.z, 0.0f), fmaxf(r.b.w, 0.0f), fmaxf(r.c.x, 0.0f) };
+            constexpr float kNL2E = -1.4426950408889634f;
+            fv[k][0] = r.a.x - 0.5f;
+            fv[k][1] = r.a.y - 0.5f;
+            fv[k][2] = (0.5f * kNL2E) * r.a.z;
+            fv[k][3] = kNL2E * r.a.w;
+            fv[k][4] = (0.5f * kNL2E) * r.b.x;
+            fv[k][5] = __log2f(r.b.y);
+            fv[k][6] = fmaxf(r.b.z, 0.0f);
+            fv[k][7] = fmaxf(r.b.w, 0.0f);
+            fv[k][8] = fmaxf(r.c.x, 0.0f);
         } else {
             tpi[k] = 0x7fffffff; /* never below a last-contributor count */
         }
     }
-    float a_mx[kPerLane], a_my[kPerLane], a_cx[kPerLane], a_cy[kPerLane], a_cz[kPerLane], a_op[kPerLane];
-    float a_r[kPerLane], a_g[kPerLane], a_b[kPerLane];
 #pragma unroll
-    for(int k = 0; k < kPerLane; ++k) {
-        a_mx[k] = a_my[k] = a_cx[k] = a_cy[k] = a_cz[k] = a_op[k] = a_r[k] = a_g[k] = a_b[k] = 0.0f;
+    for(int j = 0; j < kPerLane / 2; ++j) {
+        const float *lo = fv[2 * j], *hi = fv[2 * j + 1];
+        f[j] = FragPair{ pk(lo[0], hi[0]), pk(lo[1], hi[1]), pk(lo[2], hi[2]), pk(lo[3], hi[3]), pk(lo[4], hi[4]),
+                         pk(lo[5], hi[5]), pk(lo[6], hi[6]), pk(lo[7], hi[7]), pk(lo[8], hi[8]) };
     }
+    /* accumulators per pair: mean (sum part * d), conic (sum part * d d^T), raw opacity, colour */
+    f2 a_mx[kPerLane / 2], a_my[kPerLane / 2], a_cx[kPerLane / 2], a_cy[kPerLane / 2], a_cz[kPerLane / 2];
+    f2 a_op[kPerLane / 2], a_r[kPerLane / 2], a_g[kPerLane / 2], a_b[kPerLane / 2];
+#pragma unroll
+    for(int j = 0; j < kPerLane / 2; ++j) a_mx[j] = a_my[j] = a_cx[j] = a_cy[j] = a_cz[j] = a_op[j] = a_r[j] = a_g[j] = a_b[j] = 0ull;
 
     const int tx0 = (int)(tile % (uint32_t)grid_w) * GSX_TILE, ty0 = (int)(tile / (uint32_t)grid_w) * GSX_TILE;
     const size_t P = (size_t)width * (size_t)height;
@@ -201,31 +255,61 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         /* whole warp past every pixel's last contributor: nothing to add, state unchanged */
         if(!__any_sync(0xffffffffu, valid && tpi[0] < last)) continue;
         if(!valid) continue;
-        const float fx = (float)qx, fy = (float)qy;
+        const f2 fx2 = pk((float)qx, (float)qx), fy2 = pk((float)qy, (float)qy);
+        const f2 gr2 = pk(gr, gr), gg2 = pk(gg, gg), gb2 = pk(gb, gb);
 #pragma unroll
-        for(int k = 0; k < kPerLane; ++k) {
-            const float dx = f[k].mx - fx, dy = f[k].my - fy;
-            const float dxx = dx * dx, dxy = dx * dy, dyy = dy * dy;
-            const float sig = fmaxf(fmaf(f[k].hcx, dxx, fmaf(f[k].hcz, dyy, f[k].cy * dxy)), 0.0f);
-            const float a_pre = f[k].op * fast_exp2(sig * -1.4426950408889634f);
-            const float alpha = tpi[k] < last ? fminf(a_pre, 0.999f) : 0.0f;
-            const float w = T * alpha;
-            a_r[k] = fmaf(w, gr, a_r[k]);
-            a_g[k] = fmaf(w, gg, a_g[k]);
-            a_b[k] = fmaf(w, gb, a_b[k]);
-            const float cdg = fmaf(f[k].r, gr, fmaf(f[k].g, gg, f[k].b * gb));
-            adg = fmaf(-w, cdg, adg);
-            const float oma = 1.0f - alpha;
-            const float dl = fmaf(T, cdg, -adg * fast_rcp(fmaxf(oma, 1e-4f)));
-            const float part = a_pre >= 0.999f ? 0.0f : alpha * dl;
-            a_cx[k] = fmaf(part, dxx, a_cx[k]);
-            a_cy[k] = fmaf(part, dxy, a_cy[k]);
-            a_cz[k] = fmaf(part, dyy, a_cz[k]);
-            a_mx[k] = fmaf(part, dx, a_mx[k]);
-            a_my[k] = fmaf(part, dy, a_my[k]);
-            a_op[k] += part;
-            T *= oma;
+        for(int j = 0; j < kPerLane / 2; ++j) {
+            /* independent per instance: geometry, alpha, colour . gradient (packed pairs) */
+            const f2 dx = sub2(f[j].mx, fx2), dy = sub2(f[j].my, fy2);
+            const f2 dxx = mul2(dx, dx), dxy = mul2(dx, dy), dyy = mul2(dy, dy);
+            float n0, n1;
+            upk(fma2(f[j].nhcx, dxx, fma2(f[j].nhcz, dyy, mul2(f[j].ncy, dxy))), n0, n1);
+            /* opacity * exp(-max(sigma, 0)) = 2^(min(-sigma log2 e, 0) + log2 opacity) */
+            float e0, e1;
+            upk(add2(pk(fminf(n0, 0.0f), fminf(n1, 0.0f)), f[j].lop), e0, e1);
+            const float ap0 = fast_exp2(e0), ap1 = fast_exp2(e1);
+            const float al0 = tpi[2 * j] < last ? fminf(ap0, 0.999f) : 0.0f;
+            const float al1 = tpi[2 * j + 1] < last ? fminf(ap1, 0.999f) : 0.0f;
+            const f2 cdg = fma2(f[j].r, gr2, fma2(f[j].g, gg2, mul2(f[j].b, gb2)));
+            float c0, c1;
+            upk(cdg, c0, c1);
+            /* sequential along the pixel's chain: transmittance and colour still to come */
+            const float T0 = T, w0 = T * al0;
+            const float adg0 = fmaf(-w0, c0, adg);
+            const float oma0 = 1.0f - al0;
+            const float T1 = T0 * oma0, w1 = T1 * al1;
+            adg = fmaf(-w1, c1, adg0);
+            const float oma1 = 1.0f - al1;
+            T = T1 * oma1;
+            const f2 nr = mul2(pk(-adg0, -adg), pk(fast_rcp(fmaxf(oma0, 1e-4f)), fast_rcp(fmaxf(oma1, 1e-4f))));
+            const f2 dl = fma2(pk(T0, T1), cdg, nr);
+            const f2 pa = pk(ap0 >= 0.999f ? 0.0f : al0, ap1 >= 0.999f ? 0.0f : al1);
+            const f2 part = mul2(pa, dl);
+            const f2 w = pk(w0, w1);
+            a_r[j] = fma2(w, gr2, a_r[j]);
+            a_g[j] = fma2(w, gg2, a_g[j]);
+            a_b[j] = fma2(w, gb2, a_b[j]);
+            a_cx[j] = fma2(part, dxx, a_cx[j]);
+            a_cy[j] = fma2(part, dxy, a_cy[j]);
+            a_cz[j] = fma2(part, dyy, a_cz[j]);
+            a_mx[j] = fma2(part, dx, a_mx[j]);
+            a_my[j] = fma2(part, dy, a_my[j]);
+            a_op[j] = add2(a_op[j], part);
         }
+    }
+    float u_mx[kPerLane], u_my[kPerLane], u_cx[kPerLane], u_cy[kPerLane], u_cz[kPerLane], u_op[kPerLane];
+    float u_r[kPerLane], u_g[kPerLane], u_b[kPerLane];
+#pragma unroll
+    for(int j = 0; j < kPerLane / 2; ++j) {
+        upk(a_mx[j], u_mx[2 * j], u_mx[2 * j + 1]);
+        upk(a_my[j], u_my[2 * j], u_my[2 * j + 1]);
+        upk(a_cx[j], u_cx[2 * j], u_cx[2 * j + 1]);
+        upk(a_cy[j], u_cy[2 * j], u_cy[2 * j + 1]);
+        upk(a_cz[j], u_cz[2 * j], u_cz[2 * j + 1]);
+        upk(a_op[j], u_op[2 * j], u_op[2 * j + 1]);
+        upk(a_r[j], u_r[2 * j], u_r[2 * j + 1]);
+        upk(a_g[j], u_g[2 * j], u_g[2 * j + 1]);
+        upk(a_b[j], u_b[2 * j], u_b[2 * j + 1]);
     }
 #pragma unroll
     for(int k = 0; k < kPerLane; ++k) {
@@ -235,10 +319,10 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         float4 *acc = grad_acc + (size_t)prim[k] * 3;
         /* sum(part * (conic . d)) = conic . sum(part * d): the mean gradient is finished here */
         const float cx = r.a.z, cy = r.a.w, cz = r.b.x;
-        const float gmx = fmaf(cx, a_mx[k], cy * a_my[k]), gmy = fmaf(cy, a_mx[k], cz * a_my[k]);
-        atomicAdd(acc + 0, make_float4(-gmx, -gmy, -0.5f * a_cx[k], -a_cy[k]));
-        atomicAdd(acc + 1, make_float4(-0.5f * a_cz[k], a_op[k] * (1.0f - f[k].op), a_r[k] * fr, a_g[k] * fg));
-        atomicAdd(&acc[2].x, a_b[k] * fb);
+        const float gmx = fmaf(cx, u_mx[k], cy * u_my[k]), gmy = fmaf(cy, u_mx[k], cz * u_my[k]);
+        atomicAdd(acc + 0, make_float4(-gmx, -gmy, -0.5f * u_cx[k], -u_cy[k]));
+        atomicAdd(acc + 1, make_float4(-0.5f * u_cz[k], u_op[k] * (1.0f - r.b.y), u_r[k] * fr, u_g[k] * fg));
+        atomicAdd(&acc[2].x, u_b[k] * fb);
     }
 }
 
