@@ -35,6 +35,61 @@ struct FwdSmem {
     uint16_t list[kWarps][kChunk];
 };
 
+/* A pair of f32 in one 64-bit register for Blackwell's packed FP32 instructions (.rn.f32x2): one
+ * issue does both halves, each rounded exactly as the scalar instruction, so results stay
+ * bit-identical to the scalar (and oracle) arithmetic. */
+typedef unsigned long long f2;
+
+__device__ __forceinline__ f2 pk(float lo, float hi)
+{
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk(f2 v, float &lo, float &hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+__device__ __forceinline__ f2 sub2(f2 a, f2 b)
+{
+    f2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b)
+{
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c)
+{
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+/* gsx_expf_inrange on a pair, operation for operation (bit-identical results) for x in
+ * [-87.33, 0]: with m = rint(-x log2 e) = -n (rint and the product are sign-symmetric),
+ * r = fma(m, ln2_hi, x) = fma(-n, ln2_hi, x), the same degree-7 polynomial, times 2^n. */
+__device__ __forceinline__ f2 expf_inrange2(f2 x)
+{
+    const f2 nlog2e = pk(-1.44269502162933349609f, -1.44269502162933349609f);
+    float y0, y1;
+    upk(mul2(x, nlog2e), y0, y1);
+    const float m0 = rintf(y0), m1 = rintf(y1);
+    const f2 m = pk(m0, m1);
+    f2 r = fma2(m, pk(0.693145751953125f, 0.693145751953125f), x);
+    r = fma2(m, pk(1.42860682030941723212e-06f, 1.42860682030941723212e-06f), r);
+    f2 p = pk(1.98412698412698412698e-04f, 1.98412698412698412698e-04f);
+    p = fma2(p, r, pk(1.38888888888888888889e-03f, 1.38888888888888888889e-03f));
+    p = fma2(p, r, pk(8.33333333333333333333e-03f, 8.33333333333333333333e-03f));
+    p = fma2(p, r, pk(4.16666666666666666667e-02f, 4.16666666666666666667e-02f));
+    p = fma2(p, r, pk(1.66666666666666666667e-01f, 1.66666666666666666667e-01f));
+    p = fma2(p, r, pk(0.5f, 0.5f));
+    p = fma2(p, r, pk(1.0f, 1.0f));
+    p = fma2(p, r, pk(1.0f, 1.0f));
+    const f2 sc = pk(__uint_as_float((uint32_t)(127 - (int)m0) << 23), __uint_as_float((uint32_t)(127 - (int)m1) << 23));
+    return mul2(p, sc);
+}
+
 /* minimum of q(d) = hcx dx^2 + cy dx dy + hcz dy^2, d = m - p, over p in [x0,x1] x [y0,y1] */
 __device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, float cy, float hcz, float icx, float icz,
                                                 float x0, float x1, float y0, float y1)
@@ -120,25 +175,48 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
             snap[(size_t)bucket * kThreads + prank] = make_float4(cr, cg, cb, T);
             ++bucket;
             const int bend = (kb + 1) * 32;
-            for(; li < cnt; ++li) {
-                const int e = S.list[warp][li];
-                if(e >= bend) break;
+            /* two listed instances per iteration: geometry and exp on packed pairs, then the
+             * blend applied in order (the second only if the first did not finish the pixel) */
+            while(li < cnt) {
+                const int e0 = S.list[warp][li];
+                if(e0 >= bend) break;
+                const bool has1 = li + 1 < cnt && S.list[warp][li + 1] < bend;
+                const int e1 = has1 ? S.list[warp][li + 1] : e0;
+                li += has1 ? 2 : 1;
                 if(done) continue;
-                const float4 a = S.a[e];
-                const float dx = a.x - pxf, dy = a.y - pyf;
-                const float4 b = S.b[e];
-                const float sigma = fmaf(dx, fmaf(a.z, dx, a.w * dy), (b.x * dy) * dy);
-                if(sigma < 0.0f || sigma > 5.6f) continue;
-                const float g = gsx_expf_inrange(-sigma);
-                const float alpha = fminf(b.y * g, 0.999f);
-                if(alpha < 1.0f / 255.0f) continue;
-                const float w = T * alpha;
-                cr = fmaf(w, b.z, cr);
-                cg = fmaf(w, b.w, cg);
-                cb = fmaf(w, S.c[e].x, cb);
-                T = T * (1.0f - alpha);
-                ncon = (uint32_t)(start + e + 1);
-                if(T < 1e-4f) done = true;
+                const float4 a0 = S.a[e0], a1 = S.a[e1];
+                const float4 b0 = S.b[e0], b1 = S.b[e1];
+                const f2 dx = sub2(pk(a0.x, a1.x), pk(pxf, pxf)), dy = sub2(pk(a0.y, a1.y), pk(pyf, pyf));
+                float s0, s1;
+                upk(fma2(dx, fma2(pk(a0.z, a1.z), dx, mul2(pk(a0.w, a1.w), dy)), mul2(mul2(pk(b0.x, b1.x), dy), dy)), s0,
+                    s1);
+                const bool ok0 = !(s0 < 0.0f || s0 > 5.6f);
+                const bool ok1 = has1 && !(s1 < 0.0f || s1 > 5.6f);
+                if(!ok0 && !ok1) continue;
+                float g0, g1;
+                upk(expf_inrange2(pk(ok0 ? -s0 : 0.0f, ok1 ? -s1 : 0.0f)), g0, g1);
+                float q0, q1;
+                upk(mul2(pk(b0.y, b1.y), pk(g0, g1)), q0, q1);
+                const float alpha0 = fminf(q0, 0.999f);
+                if(ok0 && alpha0 >= 1.0f / 255.0f) {
+                    const float w = T * alpha0;
+                    cr = fmaf(w, b0.z, cr);
+                    cg = fmaf(w, b0.w, cg);
+                    cb = fmaf(w, S.c[e0].x, cb);
+                    T = T * (1.0f - alpha0);
+                    ncon = (uint32_t)(start + e0 + 1);
+                    if(T < 1e-4f) done = true;
+                }
+                const float alpha1 = fminf(q1, 0.999f);
+                if(ok1 && !done && alpha1 >= 1.0f / 255.0f) {
+                    const float w = T * alpha1;
+                    cr = fmaf(w, b1.z, cr);
+                    cg = fmaf(w, b1.w, cg);
+                    cb = fmaf(w, S.c[e1].x, cb);
+                    T = T * (1.0f - alpha1);
+                    ncon = (uint32_t)(start + e1 + 1);
+                    if(T < 1e-4f) done = true;
+                }
             }
         }
     }
