@@ -22,6 +22,7 @@
  */
 #include "gsx_b200_kernels.cuh"
 
+
 namespace {
 
 constexpr int kWarps = 8;
@@ -214,9 +215,9 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     prefetch(0);
 
     /* per-pixel state travelling along the 8 lanes of a segment: upstream gradient, last
-     * contributor, transmittance, and adg = (colour still to come) . (upstream gradient), kept as one
-     * scalar because every fragment changes it by -w * (colour . gradient) */
-    float gr = 0.0f, gg = 0.0f, gb = 0.0f, adg = 0.0f, T = 0.0f;
+     * contributor, transmittance, and nadg = -(colour still to come) . (upstream gradient), kept as one
+     * scalar because every fragment raises it by w * (colour . gradient) */
+    float gr = 0.0f, gg = 0.0f, gb = 0.0f, nadg = 0.0f, T = 0.0f;
     int last = 0;
     for(int i = 0; i < GSX_TILE_PIXELS + 7; ++i) {
         if((i & 31) == 0 && i < GSX_TILE_PIXELS) {
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         gr = __shfl_up_sync(0xffffffffu, gr, 1);
         gg = __shfl_up_sync(0xffffffffu, gg, 1);
         gb = __shfl_up_sync(0xffffffffu, gb, 1);
-        adg = __shfl_up_sync(0xffffffffu, adg, 1);
+        nadg = __shfl_up_sync(0xffffffffu, nadg, 1);
         T = __shfl_up_sync(0xffffffffu, T, 1);
         last = __shfl_up_sync(0xffffffffu, last, 1);
         const int p = i - sub;
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
                 gg = in.grad.y;
                 gb = in.grad.z;
                 last = (int)__float_as_uint(img.w);
-                adg = (img.x - sn.x) * gr + (img.y - sn.y) * gg + (img.z - sn.z) * gb;
+                nadg = (sn.x - img.x) * gr + (sn.y - img.y) * gg + (sn.z - img.z) * gb;
                 T = sn.w;
             }
         }
@@ -257,44 +258,45 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         if(!valid) continue;
         const f2 fx2 = pk((float)qx, (float)qx), fy2 = pk((float)qy, (float)qy);
         const f2 gr2 = pk(gr, gr), gg2 = pk(gg, gg), gb2 = pk(gb, gb);
+        {
 #pragma unroll
-        for(int j = 0; j < kPerLane / 2; ++j) {
-            /* independent per instance: geometry, alpha, colour . gradient (packed pairs) */
-            const f2 dx = sub2(f[j].mx, fx2), dy = sub2(f[j].my, fy2);
-            const f2 dxx = mul2(dx, dx), dxy = mul2(dx, dy), dyy = mul2(dy, dy);
-            float n0, n1;
-            upk(fma2(f[j].nhcx, dxx, fma2(f[j].nhcz, dyy, mul2(f[j].ncy, dxy))), n0, n1);
-            /* opacity * exp(-max(sigma, 0)) = 2^(min(-sigma log2 e, 0) + log2 opacity) */
-            float e0, e1;
-            upk(add2(pk(fminf(n0, 0.0f), fminf(n1, 0.0f)), f[j].lop), e0, e1);
-            const float ap0 = fast_exp2(e0), ap1 = fast_exp2(e1);
-            const float al0 = tpi[2 * j] < last ? fminf(ap0, 0.999f) : 0.0f;
-            const float al1 = tpi[2 * j + 1] < last ? fminf(ap1, 0.999f) : 0.0f;
-            const f2 cdg = fma2(f[j].r, gr2, fma2(f[j].g, gg2, mul2(f[j].b, gb2)));
-            float c0, c1;
-            upk(cdg, c0, c1);
-            /* sequential along the pixel's chain: transmittance and colour still to come */
-            const float T0 = T, w0 = T * al0;
-            const float adg0 = fmaf(-w0, c0, adg);
-            const float oma0 = 1.0f - al0;
-            const float T1 = T0 * oma0, w1 = T1 * al1;
-            adg = fmaf(-w1, c1, adg0);
-            const float oma1 = 1.0f - al1;
-            T = T1 * oma1;
-            const f2 nr = mul2(pk(-adg0, -adg), pk(fast_rcp(fmaxf(oma0, 1e-4f)), fast_rcp(fmaxf(oma1, 1e-4f))));
-            const f2 dl = fma2(pk(T0, T1), cdg, nr);
-            const f2 pa = pk(ap0 >= 0.999f ? 0.0f : al0, ap1 >= 0.999f ? 0.0f : al1);
-            const f2 part = mul2(pa, dl);
-            const f2 w = pk(w0, w1);
-            a_r[j] = fma2(w, gr2, a_r[j]);
-            a_g[j] = fma2(w, gg2, a_g[j]);
-            a_b[j] = fma2(w, gb2, a_b[j]);
-            a_cx[j] = fma2(part, dxx, a_cx[j]);
-            a_cy[j] = fma2(part, dxy, a_cy[j]);
-            a_cz[j] = fma2(part, dyy, a_cz[j]);
-            a_mx[j] = fma2(part, dx, a_mx[j]);
-            a_my[j] = fma2(part, dy, a_my[j]);
-            a_op[j] = add2(a_op[j], part);
+            for(int j = 0; j < kPerLane / 2; ++j) {
+                /* independent per instance: geometry, alpha, colour . gradient (packed pairs).
+                 * opacity * exp(-sigma) = 2^(-sigma log2 e + log2 opacity); sigma >= 0 for the
+                 * positive-definite conic up to rounding, where the reference's clamp at 0 moves
+                 * alpha by ~1e-7 relative, so it is not applied */
+                const f2 dx = sub2(f[j].mx, fx2), dy = sub2(f[j].my, fy2);
+                const f2 dxx = mul2(dx, dx), dxy = mul2(dx, dy), dyy = mul2(dy, dy);
+                float e0, e1;
+                upk(add2(fma2(f[j].nhcx, dxx, fma2(f[j].nhcz, dyy, mul2(f[j].ncy, dxy))), f[j].lop), e0, e1);
+                const float ap0 = fast_exp2(e0), ap1 = fast_exp2(e1);
+                const float al0 = tpi[2 * j] < last ? fminf(ap0, 0.999f) : 0.0f;
+                const float al1 = tpi[2 * j + 1] < last ? fminf(ap1, 0.999f) : 0.0f;
+                const f2 cdg = fma2(f[j].r, gr2, fma2(f[j].g, gg2, mul2(f[j].b, gb2)));
+                float c0, c1;
+                upk(cdg, c0, c1);
+                float oma0, oma1;
+                upk(sub2(pk(1.0f, 1.0f), pk(al0, al1)), oma0, oma1);
+                /* sequential along the pixel's chain: transmittance and -(colour still to come).g;
+                 * alpha <= 0.999 keeps 1 - alpha >= 1e-3, above the reference's 1e-4 floor */
+                const float T0 = T, w0 = T * al0;
+                const float nadg0 = fmaf(w0, c0, nadg);
+                const float T1 = T0 * oma0, w1 = T1 * al1;
+                nadg = fmaf(w1, c1, nadg0);
+                T = T1 * oma1;
+                const f2 dl = fma2(pk(nadg0, nadg), pk(fast_rcp(oma0), fast_rcp(oma1)), mul2(pk(T0, T1), cdg));
+                const f2 part = mul2(pk(ap0 >= 0.999f ? 0.0f : al0, ap1 >= 0.999f ? 0.0f : al1), dl);
+                const f2 w = pk(w0, w1);
+                a_r[j] = fma2(w, gr2, a_r[j]);
+                a_g[j] = fma2(w, gg2, a_g[j]);
+                a_b[j] = fma2(w, gb2, a_b[j]);
+                a_cx[j] = fma2(part, dxx, a_cx[j]);
+                a_cy[j] = fma2(part, dxy, a_cy[j]);
+                a_cz[j] = fma2(part, dyy, a_cz[j]);
+                a_mx[j] = fma2(part, dx, a_mx[j]);
+                a_my[j] = fma2(part, dy, a_my[j]);
+                a_op[j] = add2(a_op[j], part);
+            }
         }
     }
     float u_mx[kPerLane], u_my[kPerLane], u_cx[kPerLane], u_cy[kPerLane], u_cz[kPerLane], u_op[kPerLane];
