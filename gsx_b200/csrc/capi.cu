@@ -135,11 +135,16 @@ struct gsx_b200_context {
     uint64_t inst_cap = 0;
     uint32_t *host_hist = nullptr; /* pinned copy of hist */
     /* per tile / pixel / bucket */
-    DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap;
-    /* small device words: [0] flags, [1] preprocess tile counter, [2..3] pad */
+    DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap, tile_count, class_tiles;
+    /* small device words: [0] flags; from the tile scan: [2] instance total, [3] largest tile,
+     * [4..8] tiles per per-tile-sort size class */
     DevBuf words;
-    uint32_t *host_words = nullptr; /* pinned: [0] instance total, [1] flags */
-    int sort_passes = 0;            /* digit passes the last forward's sort ran */
+    uint32_t *host_words = nullptr; /* pinned: [0] instance total, [1] flags, [2] largest tile, [3..7] class sizes */
+    bool global_sort = false;       /* the last forward needed the global radix sort (a tile > GSX_SEG_MAX) */
+    /* side streams and fork/join events of the per-tile sort's size classes (created on first use) */
+    cudaStream_t side[GSX_SORT_CLASSES - 1] = {};
+    cudaEvent_t side_ev[GSX_SORT_CLASSES] = {};
+    bool side_created = false;
     /* retained forward state */
     bool has_train = false;
     gsx_b200_gaussians g{};
@@ -228,7 +233,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     cudaDeviceSynchronize();
     DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->tile_masks, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
-                      &ctx->bucket_tile, &ctx->snap, &ctx->words, &ctx->hist };
+                      &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->words, &ctx->hist };
     for(DevBuf *b : all) release(*b);
     if(ctx->ev_created)
         for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
@@ -236,6 +241,10 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
                 cudaEventDestroy(ctx->ev[s][k][0]);
                 cudaEventDestroy(ctx->ev[s][k][1]);
             }
+    if(ctx->side_created) {
+        for(int k = 0; k < GSX_SORT_CLASSES - 1; ++k) cudaStreamDestroy(ctx->side[k]);
+        for(int k = 0; k < GSX_SORT_CLASSES; ++k) cudaEventDestroy(ctx->side_ev[k]);
+    }
     if(ctx->host_words) cudaFreeHost(ctx->host_words);
     if(ctx->host_hist) cudaFreeHost(ctx->host_hist);
     delete ctx;
@@ -294,16 +303,20 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     uint32_t *tile_masks = (uint32_t *)ctx->tile_masks.ptr;
     uint32_t *block_sums = (uint32_t *)ctx->block_sums.ptr;
 
-    /* preprocess -> block-total scan -> emission into the current instance capacity (with the key
-     * histograms) -> ONE host synchronisation (instance total, histograms); if the capacity was too
-     * small the emission is repeated into grown buffers (rare: capacity keeps 25% headroom). */
+    /* preprocess -> block-total scan -> emission into the current instance capacity (each instance
+     * takes its rank in its tile) -> tile scan (ranges, bucket prefix, total, largest tile) -> ONE host
+     * synchronisation; if the capacity was too small the emission is repeated into grown buffers (rare:
+     * capacity keeps 25% headroom).  Then the tile binning + per-tile depth sort, or, when a tile holds
+     * more instances than shared memory sorts, the global radix sort of the tile|depth keys. */
     int tile_bits = 0;
     while((1 << tile_bits) < n_tiles) ++tile_bits;
     const int end_bit = 32 + tile_bits;
-    const int n_digits = (end_bit + 7) / 8;
-    if(int rc = ensure(ctx->hist, sizeof(uint32_t) * 8 * 256)) return rc;
-    uint32_t *hist = (uint32_t *)ctx->hist.ptr;
+    if(int rc = ensure(ctx->tile_count, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
+    if(int rc = ensure(ctx->class_tiles, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
+    uint32_t *tile_count = (uint32_t *)ctx->tile_count.ptr;
+    uint32_t *class_tiles = (uint32_t *)ctx->class_tiles.ptr;
     uint64_t total = 0;
+    uint32_t max_tile = 0;
     auto emit_into_capacity = [&](uint64_t cap) -> int {
         /* capacity in pairs; ensure() only reallocates when the request exceeds what is held, and
          * inst_cap is the exact floor of what is held, so a steady workload never reallocates */
@@ -313,13 +326,20 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         ctx->inst_cap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
         const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
         if(vcap < ctx->inst_cap) ctx->inst_cap = vcap;
-        GSX_CUDA_TRY(cudaMemsetAsync(hist, 0, sizeof(uint32_t) * 8 * 256, stream), "memset");
         GSX_CUDA_TRY(cudaMemsetAsync(words, 0, sizeof(uint32_t), stream), "memset");
-        StageTimer st(ctx, 1, stream);
-        GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets, cam.grid_w,
-                                     (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr, ctx->inst_cap, words,
-                                     hist, n_digits, stream),
-                     "emit launch");
+        GSX_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * (size_t)n_tiles, stream), "memset");
+        {
+            StageTimer st(ctx, 1, stream);
+            /* ranks go to the second half of the value buffer (free until the sort) */
+            GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets,
+                                         cam.grid_w, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
+                                         ctx->inst_cap, words, nullptr, 0, tile_count, stream),
+                         "emit launch");
+        }
+        StageTimer st3(ctx, 3, stream);
+        GSX_CUDA_TRY(gsx_launch_tile_scan(tile_count, n_tiles, (uint2 *)ctx->ranges.ptr,
+                                          (uint32_t *)ctx->bucket_offsets.ptr, class_tiles, words + 2, stream),
+                     "tile scan launch");
         return 0;
     };
     if(n > 0) {
@@ -333,22 +353,25 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
         GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
                      "D2H");
-        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_hist, hist, sizeof(uint32_t) * 8 * 256, cudaMemcpyDeviceToHost, stream), "D2H");
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (1 + GSX_SORT_CLASSES) * sizeof(uint32_t),
+                                     cudaMemcpyDeviceToHost, stream),
+                     "D2H");
         GSX_CUDA_TRY(cudaStreamSynchronize(stream), "forward");
         total = ctx->host_words[0];
         if(total > ctx->inst_cap) {
             if(int rc = emit_into_capacity(total + total / 4 + 1024)) return rc;
-            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_hist, hist, sizeof(uint32_t) * 8 * 256, cudaMemcpyDeviceToHost, stream),
+            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (1 + GSX_SORT_CLASSES) * sizeof(uint32_t),
+                                         cudaMemcpyDeviceToHost, stream),
                          "D2H");
             GSX_CUDA_TRY(cudaStreamSynchronize(stream), "forward");
         }
+        max_tile = ctx->host_words[2];
     } else {
         GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
         if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
     }
     ctx->n_instances = total;
     const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
-    if(int rc = ensure(ctx->sort_scratch, gsx_sort_scratch_bytes(total + 1))) return rc;
     if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
     if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
     const uint64_t kcap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
@@ -357,33 +380,32 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     uint32_t *vals_a = (uint32_t *)ctx->vals.ptr;
     uint32_t *vals_b = vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t));
     int in_b = 0;
-    ctx->sort_passes = 0;
+    ctx->global_sort = false;
     if(total > 0) {
-        /* plan: one onesweep pass per 8-bit digit position whose digit is not the same for all keys */
-        int positions[8], shifts[8], widths[8], np = 0;
-        for(int p = 0; p < n_digits; ++p) {
-            bool trivial = false;
-            for(int b = 0; b < 256; ++b) trivial |= ctx->host_hist[p * 256 + b] == total;
-            if(trivial) continue;
-            positions[np] = p;
-            shifts[np] = 8 * p;
-            widths[np] = end_bit - 8 * p < 8 ? end_bit - 8 * p : 8;
-            ++np;
-        }
-        ctx->sort_passes = np;
         StageTimer st(ctx, 2, stream);
-        GSX_CUDA_TRY(gsx_launch_sort_passes(keys_a, vals_a, keys_b, vals_b, total, positions, shifts, widths, np, hist,
-                                            ctx->sort_scratch.ptr, ctx->sort_scratch.bytes, words, &in_b, stream),
-                     "sort launch");
+        if(max_tile <= (uint32_t)GSX_SEG_MAX) {
+            if(!ctx->side_created) {
+                for(int k = 0; k < GSX_SORT_CLASSES - 1; ++k)
+                    GSX_CUDA_TRY(cudaStreamCreateWithFlags(&ctx->side[k], cudaStreamNonBlocking), "cudaStreamCreate");
+                for(int k = 0; k < GSX_SORT_CLASSES; ++k)
+                    GSX_CUDA_TRY(cudaEventCreateWithFlags(&ctx->side_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+                ctx->side_created = true;
+            }
+            GSX_CUDA_TRY(gsx_launch_tile_sort(keys_a, vals_a, total, n_tiles, (const uint2 *)ctx->ranges.ptr, tile_count,
+                                              class_tiles, ctx->host_words + 3, keys_b, keys_a, vals_a, stream, ctx->side,
+                                              ctx->side_ev),
+                         "tile sort launch");
+        } else {
+            /* a tile too large for shared memory: stable global radix sort of the tile|depth keys
+             * (emitted in primitive order, so equal depths stay in primitive order) */
+            ctx->global_sort = true;
+            if(int rc = ensure(ctx->sort_scratch, gsx_sort_scratch_bytes(total + 1))) return rc;
+            GSX_CUDA_TRY(gsx_launch_sort_pairs(keys_a, vals_a, keys_b, vals_b, total, 0, end_bit, ctx->sort_scratch.ptr,
+                                               ctx->sort_scratch.bytes, words, &in_b, stream),
+                         "sort launch");
+        }
     }
-    const unsigned long long *keys = in_b ? keys_b : keys_a;
     const uint32_t *vals = in_b ? vals_b : vals_a;
-    {
-    StageTimer st3(ctx, 3, stream);
-    GSX_CUDA_TRY(gsx_launch_tile_ranges(keys, total, n_tiles, (uint2 *)ctx->ranges.ptr, (uint32_t *)ctx->bucket_offsets.ptr,
-                                        (uint32_t *)ctx->bucket_tile.ptr, bucket_cap, words, stream),
-                 "ranges launch");
-    }
     {
     StageTimer st4(ctx, 4, stream);
     GSX_CUDA_TRY(gsx_launch_blend_forward(camera->width, camera->height, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,

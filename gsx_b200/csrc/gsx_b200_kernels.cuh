@@ -26,6 +26,7 @@
 #define GSX_TILE_PIXELS 256
 #define GSX_SEQ_TILES 8
 #define GSX_SPIN_LIMIT (1u << 22)
+#define GSX_SEG_MAX 16384 /* largest tile (instances) sorted in shared memory by k_tilesort.cu */
 
 /* device-side error flags (bitwise-or into ctx->dev_flags[0]) */
 #define GSX_FLAG_LOOKBACK_TIMEOUT 1u
@@ -133,7 +134,7 @@ cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, co
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
-                            uint32_t *flags, uint32_t *hist, int n_digits, cudaStream_t stream);
+                            uint32_t *flags, uint32_t *hist, int n_digits, uint32_t *tile_count, cudaStream_t stream);
 cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
                                    uint32_t *vals_b, uint64_t count, const int *positions, const int *shifts,
                                    const int *widths, int npasses, const uint32_t *hist, void *scratch,
@@ -142,6 +143,14 @@ size_t gsx_sort_scratch_bytes(uint64_t capacity);
 cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
                                   uint32_t *vals_b, uint64_t count, int begin_bit, int end_bit, void *scratch,
                                   size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream);
+#define GSX_SORT_CLASSES 5 /* per-tile sort size classes of k_tilesort.cu */
+cudaError_t gsx_launch_tile_scan(const uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
+                                 uint32_t *class_tiles, uint32_t *words_out, cudaStream_t stream);
+/* side: GSX_SORT_CLASSES - 1 streams; ev: GSX_SORT_CLASSES events (fork and join) */
+cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t *vals, uint64_t n, int n_tiles,
+                                 const uint2 *ranges, uint32_t *tile_count, const uint32_t *class_tiles,
+                                 const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
+                                 uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev);
 cudaError_t gsx_launch_tile_ranges(const unsigned long long *keys, uint64_t count, int n_tiles, uint2 *ranges,
                                    uint32_t *bucket_offsets, uint32_t *bucket_tile, uint64_t bucket_capacity,
                                    uint32_t *flags, cudaStream_t stream);

@@ -6,8 +6,10 @@
  * (the same exact overlap test as the preprocess count), but writes the combined tile|depth key
  * so that one stable LSD radix sort yields the reference's (tile, then depth) order
  * (forward.cu:155-161 depth sort followed by the stable 16-bit tile sort at :214-220).
- * It also counts, per 8-bit digit position of the emitted keys, a 256-bin histogram, from which the
- * host plans the radix-sort passes (passes whose digit is the same for every key are skipped).
+ * With tile counters it also counts the instances of every tile (for the tile binning of
+ * k_tilesort.cu); without them it counts, per 8-bit digit position of the emitted keys, a 256-bin
+ * histogram from which the host plans the global radix-sort passes (passes whose digit is the same
+ * for every key are skipped).
  * Compiled with -fmad=false (bit-identical overlap decisions with the preprocess and the oracle).
  */
 #include "gsx_b200_kernels.cuh"
@@ -23,11 +25,12 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                                                         uint32_t *__restrict__ offsets, unsigned grid_w,
                                                         unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
                                                         uint64_t capacity, uint32_t *__restrict__ flags,
-                                                        uint32_t *__restrict__ hist, int n_digits)
+                                                        uint32_t *__restrict__ hist, int n_digits,
+                                                        uint32_t *__restrict__ tile_count)
 {
     __shared__ uint32_t s_warp[kThreads / 32];
     __shared__ uint32_t s_hist[8][256];
-    for(int j = threadIdx.x; j < 8 * 256; j += kThreads) (&s_hist[0][0])[j] = 0u;
+    for(int j = threadIdx.x; j < n_digits * 256; j += kThreads) (&s_hist[0][0])[j] = 0u;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
     uint32_t cnt = i < n ? counts[i] : 0u;
@@ -79,9 +82,11 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned k = (unsigned)__ffs(m) - 1u;
             m &= m - 1u;
             const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
-            const unsigned long long key = ((unsigned long long)(ty * grid_w + tx) << 32) | dbits;
+            const unsigned t = ty * grid_w + tx;
+            const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
+            if(tile_count) atomicAdd(&tile_count[t], 1u);
             ++wpos;
             for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
@@ -91,9 +96,11 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
     for(unsigned k = 0; k < nseq; ++k) {
         const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
         if(gsx_tile_contributes(msx, msy, cx, cy, cz, tx, ty, pt)) {
-            const unsigned long long key = ((unsigned long long)(ty * grid_w + tx) << 32) | dbits;
+            const unsigned t = ty * grid_w + tx;
+            const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
+            if(tile_count) atomicAdd(&tile_count[t], 1u);
             ++wpos;
             for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
@@ -118,9 +125,11 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned ballot = __ballot_sync(0xffffffffu, c);
             if(c) {
                 const uint32_t p = lpos + (uint32_t)__popc(ballot & lt_mask);
-                const unsigned long long key = ((unsigned long long)(ty * grid_w + tx) << 32) | ldb;
+                const unsigned t = ty * grid_w + tx;
+                const unsigned long long key = ((unsigned long long)t << 32) | ldb;
                 keys[p] = key;
                 vals[p] = lidx;
+                if(tile_count) atomicAdd(&tile_count[t], 1u);
                 for(int q = 0; q < n_digits; ++q) atomicAdd(&s_hist[q][(uint32_t)(key >> (8 * q)) & 0xffu], 1u);
             }
             lpos += (uint32_t)__popc(ballot);
@@ -140,11 +149,11 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
-                            uint32_t *flags, uint32_t *hist, int n_digits, cudaStream_t stream)
+                            uint32_t *flags, uint32_t *hist, int n_digits, uint32_t *tile_count, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
     emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, keys,
-                                                            vals, capacity, flags, hist, n_digits);
+                                                            vals, capacity, flags, hist, n_digits, tile_count);
     return cudaGetLastError();
 }

@@ -166,3 +166,43 @@ def test_repeated_forward_is_deterministic(ctx):
     a = render(ctx, gd, cam).clone()
     b = render(ctx, gd, cam).clone()
     assert torch.equal(a, b)
+
+
+def _cluster_scene(seed, n, width, height, z_levels=None):
+    """n small Gaussians packed into a width x height view (every tile holds thousands of
+    instances); with z_levels, depths take only that many distinct values (ties broken by index)."""
+    rng = np.random.default_rng(seed)
+    z = rng.uniform(2.0, 6.0, n) if z_levels is None else rng.choice(np.linspace(2.0, 6.0, z_levels), n)
+    g = dict(mean3d=np.stack([rng.uniform(-0.5, 0.5, n) * z, rng.uniform(-0.5, 0.5, n) * z, z], 1).astype(np.float32),
+             rotation=scenes._unit_quats(rng, n), logscale=rng.normal(-2.5, 0.3, (n, 3)).astype(np.float32),
+             opacity=rng.normal(-1.0, 1.0, n).astype(np.float32), sh0=rng.uniform(0.0, 1.0, (n, 3)).astype(np.float32))
+    cam = gb.Camera(width, height, float(width), float(width), width / 2.0, height / 2.0, near_plane=0.2, far_plane=100.0)
+    return g, cam
+
+
+@pytest.mark.parametrize("n,size,z_levels", [(5000, 16, None), (3000, 24, 7), (60000, 32, None)],
+                         ids=["one_tile_5k", "depth_ties", "tiles_over_16384_global_sort"])
+def test_dense_tiles_order_and_gradients(ctx, n, size, z_levels):
+    """Dense tiles: the shared-memory per-tile sort (segments up to 16384, heavy depth ties) and the
+    global radix sort fallback (a tile above 16384) give the oracle's exact order and results."""
+    g, cam = _cluster_scene(21, n, size, size, z_levels)
+    ref = po.render_forward(g, _ocam(cam), 0, (0, 0, 0))
+    seg = ref["ranges"][:, 1] - ref["ranges"][:, 0]
+    if size == 32:
+        assert seg.max() > 16384
+    gd = to_dev(g)
+    out = render(ctx, gd, cam)
+    ctx.check()
+    v = fetch_view(ctx, n)
+    np.testing.assert_array_equal(v["keys"], ref["keys"])
+    np.testing.assert_array_equal(v["vals"], ref["vals"])
+    np.testing.assert_array_equal(v["ranges"], ref["ranges"])
+    np.testing.assert_array_equal(out.cpu().numpy(), ref["rgb"])
+    grad_rgb = np.random.default_rng(5).normal(0, 1, (3, size, size)).astype(np.float32)
+    ref_b = po.render_backward(g, _ocam(cam), ref, grad_rgb, 0)
+    grads = zeros_like_fields(gd)
+    gb.Renderer(size, size).backward(ctx, torch.from_numpy(grad_rgb).cuda(), grads)
+    ctx.check()
+    for k in gd:
+        err = rel_l2(grads[k].cpu().numpy(), ref_b[k])
+        assert err <= GRAD_TOL, f"{k}: rel-L2 {err:.3e}"
