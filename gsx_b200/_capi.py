@@ -85,6 +85,9 @@ SIGNATURES = {
                                            ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]),
     "gsx_b200_sort_pairs_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32,
                                                    ctypes.c_int32, ctypes.c_void_p]),
+    "gsx_b200_fill_pattern": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint32,
+                                             ctypes.c_void_p]),
+    "gsx_b200_count_nonfinite_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]),
 }
 NOALLOC_SORT_MAX_PAIRS = 1 << 20
 

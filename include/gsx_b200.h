@@ -217,6 +217,18 @@ GSX_B200_API int gsx_b200_sort_pairs(gsx_b200_context *ctx, uint64_t *keys, uint
 GSX_B200_API int gsx_b200_sort_pairs_noalloc(uint64_t *keys, uint32_t *values, uint64_t count, int32_t begin_bit,
                                              int32_t end_bit, void *stream);
 
+/*
+ * Buffer helpers behind the GSX backend-buffer interface (gsx/src/gsx-impl.h:302-458), used by the
+ * GSX provider in gsx_b200/provider/.
+ * gsx_b200_fill_pattern: repeats a 1/2/4/8-byte pattern over size_bytes of device memory at dst
+ * (size a multiple of the pattern, dst aligned to it); replaces the backend's fill_tensor
+ * (gsx-impl.h:349-353, gsx-cuda/buffer.c).
+ * gsx_b200_count_nonfinite_f32: ADDS the number of NaN/Inf values among n floats at x to the
+ * device word device_count (clear it first); backs check_finite_tensor (gsx-impl.h:377-381).
+ */
+GSX_B200_API int gsx_b200_fill_pattern(void *dst, uint64_t size_bytes, const void *pattern, uint32_t pattern_bytes, void *stream);
+GSX_B200_API int gsx_b200_count_nonfinite_f32(const float *x, uint64_t n, uint32_t *device_count, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

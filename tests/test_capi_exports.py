@@ -52,3 +52,20 @@ def test_host_side_validation_without_gpu():
     L = _capi.lib()
     assert L.gsx_b200_adam_step(None, 17, None) == gsx_b200.OUT_OF_RANGE
     assert L.gsx_b200_loss_l1_ssim(4, None, None, None, None, None, 1, 1, 1, 0, 0, 0, 0, None) == gsx_b200.INVALID_ARGUMENT
+
+
+def test_gsx_provider_links_into_gsx_without_gpu():
+    """The GSX library built with the gsx_b200 provider as its CUDA backend (oracle/Makefile.ref,
+    target b200) exports the provider bootstrap, resolves every gsx_b200 symbol, and on a machine
+    without a GPU lets GSX start with the CUDA backend reported as unavailable."""
+    import pytest
+    from oracle import pyoracle as po
+    path = os.path.join(ROOT, "oracle", "_ref", "libgsx_ref_b200.so")
+    if not os.path.exists(path) or not po.ref_available("b200"):
+        pytest.skip("GSX + gsx_b200 provider library not built")
+    L = ctypes.CDLL(path)
+    assert hasattr(L, "gsx_cuda_backend_provider_bootstrap")
+    import torch
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="device"):
+            po.ref("b200")
