@@ -135,7 +135,7 @@ struct gsx_b200_context {
     uint64_t inst_cap = 0;
     uint32_t *host_hist = nullptr; /* pinned copy of hist */
     /* per tile / pixel / bucket */
-    DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap, tile_count, class_tiles;
+    DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap, tile_count, class_tiles, tile_aux;
     /* small device words: [0] flags; from the tile scan: [2] instance total, [3] largest tile,
      * [4..8] tiles per per-tile-sort size class */
     DevBuf words;
@@ -233,7 +233,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     cudaDeviceSynchronize();
     DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->tile_masks, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
-                      &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->words, &ctx->hist };
+                      &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->tile_aux, &ctx->words, &ctx->hist };
     for(DevBuf *b : all) release(*b);
     if(ctx->ev_created)
         for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
@@ -311,8 +311,9 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     int tile_bits = 0;
     while((1 << tile_bits) < n_tiles) ++tile_bits;
     const int end_bit = 32 + tile_bits;
-    if(int rc = ensure(ctx->tile_count, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
+    if(int rc = ensure(ctx->tile_count, sizeof(uint32_t) * GSX_TILE_SUBCOUNTERS * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->class_tiles, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
+    if(int rc = ensure(ctx->tile_aux, sizeof(uint32_t) * gsx_tile_scan_aux_words(n_tiles))) return rc;
     uint32_t *tile_count = (uint32_t *)ctx->tile_count.ptr;
     uint32_t *class_tiles = (uint32_t *)ctx->class_tiles.ptr;
     uint64_t total = 0;
@@ -327,7 +328,8 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
         if(vcap < ctx->inst_cap) ctx->inst_cap = vcap;
         GSX_CUDA_TRY(cudaMemsetAsync(words, 0, sizeof(uint32_t), stream), "memset");
-        GSX_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * (size_t)n_tiles, stream), "memset");
+        GSX_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * GSX_TILE_SUBCOUNTERS * (size_t)n_tiles, stream),
+                     "memset");
         {
             StageTimer st(ctx, 1, stream);
             /* ranks go to the second half of the value buffer (free until the sort) */
@@ -338,7 +340,8 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         }
         StageTimer st3(ctx, 3, stream);
         GSX_CUDA_TRY(gsx_launch_tile_scan(tile_count, n_tiles, (uint2 *)ctx->ranges.ptr,
-                                          (uint32_t *)ctx->bucket_offsets.ptr, class_tiles, words + 2, stream),
+                                          (uint32_t *)ctx->bucket_offsets.ptr, class_tiles,
+                                          (uint32_t *)ctx->tile_aux.ptr, words + 2, stream),
                      "tile scan launch");
         return 0;
     };

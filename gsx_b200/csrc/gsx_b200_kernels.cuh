@@ -144,11 +144,13 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
                                   uint32_t *vals_b, uint64_t count, int begin_bit, int end_bit, void *scratch,
                                   size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream);
 #define GSX_SORT_CLASSES 5 /* per-tile sort size classes of k_tilesort.cu */
-cudaError_t gsx_launch_tile_scan(const uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
-                                 uint32_t *class_tiles, uint32_t *words_out, cudaStream_t stream);
+#define GSX_TILE_SUBCOUNTERS 8 /* instance counters per tile (emission, binning) */
+size_t gsx_tile_scan_aux_words(int n_tiles);
+cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
+                                 uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream);
 /* side: GSX_SORT_CLASSES - 1 streams; ev: GSX_SORT_CLASSES events (fork and join) */
 cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t *vals, uint64_t n, int n_tiles,
-                                 const uint2 *ranges, uint32_t *tile_count, const uint32_t *class_tiles,
+                                 const uint2 *ranges, uint32_t *tile_end, const uint32_t *class_tiles,
                                  const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
                                  uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev);
 cudaError_t gsx_launch_tile_ranges(const unsigned long long *keys, uint64_t count, int n_tiles, uint2 *ranges,

@@ -7,9 +7,10 @@
  * so that one stable LSD radix sort yields the reference's (tile, then depth) order
  * (forward.cu:155-161 depth sort followed by the stable 16-bit tile sort at :214-220).
  * With tile counters it also counts the instances of every tile (for the tile binning of
- * k_tilesort.cu); without them it counts, per 8-bit digit position of the emitted keys, a 256-bin
- * histogram from which the host plans the global radix-sort passes (passes whose digit is the same
- * for every key are skipped).
+ * k_tilesort.cu) on GSX_TILE_SUBCOUNTERS counters per tile, picked by the instance's index, so that
+ * the atomics of a crowded tile spread over several addresses; without them it counts, per 8-bit
+ * digit position of the emitted keys, a 256-bin histogram from which the host plans the global
+ * radix-sort passes (passes whose digit is the same for every key are skipped).
  * Compiled with -fmad=false (bit-identical overlap decisions with the preprocess and the oracle).
  */
 #include "gsx_b200_kernels.cuh"
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
-            if(tile_count) atomicAdd(&tile_count[t], 1u);
+            if(tile_count) atomicAdd(&tile_count[t * GSX_TILE_SUBCOUNTERS + (wpos & (GSX_TILE_SUBCOUNTERS - 1))], 1u);
             ++wpos;
             for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
@@ -100,7 +101,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
-            if(tile_count) atomicAdd(&tile_count[t], 1u);
+            if(tile_count) atomicAdd(&tile_count[t * GSX_TILE_SUBCOUNTERS + (wpos & (GSX_TILE_SUBCOUNTERS - 1))], 1u);
             ++wpos;
             for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
@@ -129,7 +130,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                 const unsigned long long key = ((unsigned long long)t << 32) | ldb;
                 keys[p] = key;
                 vals[p] = lidx;
-                if(tile_count) atomicAdd(&tile_count[t], 1u);
+                if(tile_count) atomicAdd(&tile_count[t * GSX_TILE_SUBCOUNTERS + (p & (GSX_TILE_SUBCOUNTERS - 1))], 1u);
                 for(int q = 0; q < n_digits; ++q) atomicAdd(&s_hist[q][(uint32_t)(key >> (8 * q)) & 0xffu], 1u);
             }
             lpos += (uint32_t)__popc(ballot);

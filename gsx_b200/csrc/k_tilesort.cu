@@ -8,11 +8,13 @@
  * (frequent: 32-bit depths of millions of Gaussians collide) in primitive order here.
  *
  * B200 organisation, exploiting that a tile holds few instances (hundreds to a few thousand):
- *   1. the emission kernel counts the instances of every tile (atomic adds);
- *   2. tile_scan_kernel (one CTA) turns the counts into tile ranges [start, end), the inclusive
- *      bucket prefix, the instance total and the largest tile;
- *   3. bin_kernel moves every instance into a slot of its tile's range (taken by counting the
- *      tile's count back down: arbitrary order) as a 64-bit sort key depth_bits << 32 | primitive;
+ *   1. the emission kernel counts the instances of every tile (atomic adds on GSX_TILE_SUBCOUNTERS
+ *      counters per tile, chosen by instance index, to spread the atomics of crowded tiles);
+ *   2. the tile scan (three short launches, one thread per tile) turns the counts into tile ranges
+ *      [start, end), the inclusive bucket prefix, the instance total and the largest tile, the
+ *      per-class tile lists, and every sub-counter into the absolute end of its slice of the range;
+ *   3. bin_kernel moves every instance into a slot of its tile's range (taken by counting its
+ *      sub-counter's end back down: arbitrary order) as a 64-bit sort key depth_bits << 32 | primitive;
  *   4. segsort_kernel (one CTA per tile) radix-sorts the tile's (depth, primitive) keys in shared
  *      memory and writes the final tile|depth keys and primitive values: the order is fully
  *      determined.  Five size classes (up to 512, 1024, 2048, 4096 and 16384 instances), each launched
@@ -24,7 +26,6 @@
 
 namespace {
 
-constexpr int kScanThreads = 1024;
 constexpr int kBinThreads = 256;
 /* per-tile sort size classes: (threads, items per thread), capacity = threads * items */
 constexpr int kClasses = 5;
@@ -39,101 +40,189 @@ __device__ __forceinline__ int size_class(uint32_t n)
     return n <= 512u ? 0 : n <= 1024u ? 1 : n <= 2048u ? 2 : n <= 4096u ? 3 : 4; /* kClassMax */
 }
 
-/* words_out[0] = instance total, words_out[1] = largest tile count, words_out[2 + c] = number of
- * non-empty tiles of size class c (kClassMax[c-1] < n <= kClassMax[c]); class_tiles[] lists the
- * tile ids class by class, each class in increasing tile order */
-__global__ void __launch_bounds__(kScanThreads) tile_scan_kernel(const uint32_t *__restrict__ tile_count, int n_tiles,
-                                                                 uint2 *__restrict__ ranges,
-                                                                 uint32_t *__restrict__ bucket_offsets,
-                                                                 uint32_t *__restrict__ class_tiles,
-                                                                 uint32_t *__restrict__ words_out)
+/* Tile scan, three launches (one thread per tile, 256 tiles per CTA):
+ *   tile_reduce_kernel: per CTA, the sums of (instances, buckets, tiles per size class) and the
+ *     largest tile -> block_aux[block * kAux + v];
+ *   block_scan_aux_kernel (one CTA): exclusive scan of those over the CTAs; the class lists are laid
+ *     end to end, class by class; words_out[0] = instance total, [1] = largest tile,
+ *     [2 + c] = tiles of size class c;
+ *   tile_write_kernel: ranges [start, end) (empty tiles [0, 0)), the inclusive bucket prefix, the
+ *     class lists (each class in increasing tile order), and every sub-counter turned into the
+ *     absolute end position of its slice of the tile's range. */
+constexpr int kTileThreads = 256;
+constexpr int kAux = 2 + kClasses + 1; /* instances, buckets, per-class tiles, max */
+
+__device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub, int t, uint32_t part[GSX_TILE_SUBCOUNTERS])
 {
-    constexpr int kV = 2 + kClasses; /* scanned values: instances, buckets, one count per class */
-    __shared__ uint32_t s_v[kV][kScanThreads / 32], s_m[kScanThreads / 32];
+    const uint4 *p = reinterpret_cast<const uint4 *>(sub + (size_t)t * GSX_TILE_SUBCOUNTERS);
+    const uint4 a = p[0], b = p[1];
+    part[0] = a.x, part[1] = a.y, part[2] = a.z, part[3] = a.w, part[4] = b.x, part[5] = b.y, part[6] = b.z, part[7] = b.w;
+    uint32_t c = 0;
+#pragma unroll
+    for(int k = 0; k < GSX_TILE_SUBCOUNTERS; ++k) c += part[k];
+    return c;
+}
+
+__global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_t *__restrict__ sub, int n_tiles,
+                                                                   uint32_t *__restrict__ block_aux)
+{
+    static_assert(GSX_TILE_SUBCOUNTERS == 8, "two 16-byte loads per tile");
+    __shared__ uint32_t s[kTileThreads / 32][kAux];
+    const int t = blockIdx.x * kTileThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int per = (n_tiles + kScanThreads - 1) / kScanThreads;
-    const int t0 = threadIdx.x * per;
-    uint32_t loc[kV], lm = 0;
+    uint32_t v[kAux];
 #pragma unroll
-    for(int v = 0; v < kV; ++v) loc[v] = 0u;
-    for(int t = t0; t < t0 + per && t < n_tiles; ++t) {
-        const uint32_t c = tile_count[t];
-        loc[0] += c;
-        loc[1] += (c + 31u) / 32u;
-        lm = max(lm, c);
-        if(c) loc[2 + size_class(c)] += 1u;
+    for(int q = 0; q < kAux; ++q) v[q] = 0u;
+    if(t < n_tiles) {
+        uint32_t part[GSX_TILE_SUBCOUNTERS];
+        const uint32_t c = tile_total(sub, t, part);
+        v[0] = c;
+        v[1] = (c + 31u) / 32u;
+        if(c) v[2 + size_class(c)] = 1u;
+        v[kAux - 1] = c;
     }
-    uint32_t inc[kV];
 #pragma unroll
-    for(int v = 0; v < kV; ++v) inc[v] = loc[v];
-    uint32_t im = lm;
+    for(int q = 0; q < kAux; ++q) v[q] = q == kAux - 1 ? __reduce_max_sync(0xffffffffu, v[q]) : __reduce_add_sync(0xffffffffu, v[q]);
+    if(lane == 0)
 #pragma unroll
-    for(int d = 1; d < 32; d <<= 1) {
-#pragma unroll
-        for(int v = 0; v < kV; ++v) {
-            const uint32_t x = __shfl_up_sync(0xffffffffu, inc[v], d);
-            if(lane >= d) inc[v] += x;
-        }
-        im = max(im, __shfl_xor_sync(0xffffffffu, im, d));
-    }
-    if(lane == 31)
-#pragma unroll
-        for(int v = 0; v < kV; ++v) s_v[v][warp] = inc[v];
-    if(lane == 0) s_m[warp] = im;
+        for(int q = 0; q < kAux; ++q) s[warp][q] = v[q];
     __syncthreads();
-    uint32_t run[kV], tot[kV], mm = 0;
-#pragma unroll
-    for(int v = 0; v < kV; ++v) {
-        uint32_t o = 0, t = 0;
-        for(int w = 0; w < kScanThreads / 32; ++w) {
-            o += w < warp ? s_v[v][w] : 0u;
-            t += s_v[v][w];
-        }
-        run[v] = o + inc[v] - loc[v];
-        tot[v] = t;
-    }
-    for(int w = 0; w < kScanThreads / 32; ++w) mm = max(mm, s_m[w]);
-    uint32_t cbase = 0;
-#pragma unroll
-    for(int c = 0; c < kClasses; ++c) {
-        run[2 + c] += cbase; /* class c's list starts after the smaller classes' lists */
-        cbase += tot[2 + c];
-    }
-    for(int t = t0; t < t0 + per && t < n_tiles; ++t) {
-        const uint32_t c = tile_count[t];
-        /* empty tiles keep [0, 0), as the reference's memset ranges */
-        ranges[t] = c ? make_uint2(run[0], run[0] + c) : make_uint2(0u, 0u);
-        run[0] += c;
-        run[1] += (c + 31u) / 32u;
-        bucket_offsets[t] = run[1];
-        if(c) {
-            const int k = size_class(c);
-#pragma unroll
-            for(int q = 0; q < kClasses; ++q)
-                if(q == k) class_tiles[run[2 + q]++] = (uint32_t)t;
-        }
-    }
-    if(threadIdx.x == 0) {
-        words_out[0] = tot[0];
-        words_out[1] = mm;
-#pragma unroll
-        for(int c = 0; c < kClasses; ++c) words_out[2 + c] = tot[2 + c];
+    if(threadIdx.x < kAux) {
+        uint32_t acc = 0;
+        for(int w = 0; w < kTileThreads / 32; ++w)
+            acc = threadIdx.x == kAux - 1 ? max(acc, s[w][threadIdx.x]) : acc + s[w][threadIdx.x];
+        block_aux[(size_t)blockIdx.x * kAux + threadIdx.x] = acc;
     }
 }
 
-/* each instance takes a slot of its tile by counting the tile's instance count back down (the scan
- * has consumed the counts; they end at zero) */
+/* one CTA of 1024 threads, at most 1024 tile blocks (262144 tiles) */
+__global__ void __launch_bounds__(1024) block_scan_aux_kernel(uint32_t *__restrict__ block_aux, int n_blocks,
+                                                              uint32_t *__restrict__ words_out)
+{
+    __shared__ uint32_t s_w[32][kAux];
+    __shared__ uint32_t s_tot[kAux];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int b = threadIdx.x;
+    uint32_t v[kAux], inc[kAux];
+#pragma unroll
+    for(int q = 0; q < kAux; ++q) inc[q] = v[q] = b < n_blocks ? block_aux[(size_t)b * kAux + q] : 0u;
+#pragma unroll
+    for(int d = 1; d < 32; d <<= 1)
+#pragma unroll
+        for(int q = 0; q < kAux - 1; ++q) {
+            const uint32_t x = __shfl_up_sync(0xffffffffu, inc[q], d);
+            if(lane >= d) inc[q] += x;
+        }
+    inc[kAux - 1] = __reduce_max_sync(0xffffffffu, v[kAux - 1]);
+    if(lane == 31)
+#pragma unroll
+        for(int q = 0; q < kAux - 1; ++q) s_w[warp][q] = inc[q];
+    if(lane == 0) s_w[warp][kAux - 1] = inc[kAux - 1];
+    __syncthreads();
+    uint32_t off[kAux];
+#pragma unroll
+    for(int q = 0; q < kAux; ++q) off[q] = 0u;
+    for(int w = 0; w < 32; ++w)
+#pragma unroll
+        for(int q = 0; q < kAux - 1; ++q) off[q] += w < warp ? s_w[w][q] : 0u;
+    if(threadIdx.x < kAux) {
+        uint32_t acc = 0;
+        for(int w = 0; w < 32; ++w) acc = threadIdx.x == kAux - 1 ? max(acc, s_w[w][threadIdx.x]) : acc + s_w[w][threadIdx.x];
+        s_tot[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    if(b < n_blocks) {
+        /* exclusive offsets; class c's list starts after the lists of the smaller classes */
+        uint32_t cbase = 0;
+#pragma unroll
+        for(int q = 0; q < kAux - 1; ++q) {
+            uint32_t e = off[q] + inc[q] - v[q];
+            if(q >= 2) {
+                e += cbase;
+                cbase += s_tot[q];
+            }
+            block_aux[(size_t)b * kAux + q] = e;
+        }
+    }
+    if(threadIdx.x == 0) {
+        words_out[0] = s_tot[0];
+        words_out[1] = s_tot[kAux - 1];
+#pragma unroll
+        for(int c = 0; c < kClasses; ++c) words_out[2 + c] = s_tot[2 + c];
+    }
+}
+
+__global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__restrict__ sub, int n_tiles,
+                                                                  const uint32_t *__restrict__ block_aux,
+                                                                  uint2 *__restrict__ ranges, uint32_t *__restrict__ bucket_offsets,
+                                                                  uint32_t *__restrict__ class_tiles)
+{
+    __shared__ uint32_t s[kTileThreads / 32][kAux - 1];
+    const int t = blockIdx.x * kTileThreads + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned lt = (1u << lane) - 1u;
+    uint32_t part[GSX_TILE_SUBCOUNTERS];
+    uint32_t c = 0;
+    if(t < n_tiles) c = tile_total(sub, t, part);
+    const int cls = c ? size_class(c) : -1;
+    /* in-warp exclusive prefixes: instances and buckets by shuffles, class memberships by ballots */
+    uint32_t vi = c, vb = (c + 31u) / 32u;
+    uint32_t ii = vi, ib = vb;
+#pragma unroll
+    for(int d = 1; d < 32; d <<= 1) {
+        const uint32_t xi = __shfl_up_sync(0xffffffffu, ii, d), xb = __shfl_up_sync(0xffffffffu, ib, d);
+        if(lane >= d) {
+            ii += xi;
+            ib += xb;
+        }
+    }
+    uint32_t cpos = 0, cmask[kClasses];
+#pragma unroll
+    for(int k = 0; k < kClasses; ++k) {
+        cmask[k] = __ballot_sync(0xffffffffu, cls == k);
+        if(cls == k) cpos = (uint32_t)__popc(cmask[k] & lt);
+    }
+    if(lane == 31) {
+        s[warp][0] = ii;
+        s[warp][1] = ib;
+    }
+    if(lane < kClasses) s[warp][2 + lane] = (uint32_t)__popc(cmask[lane]);
+    __syncthreads();
+    if(t >= n_tiles) return;
+    uint32_t oi = block_aux[(size_t)blockIdx.x * kAux + 0], ob = block_aux[(size_t)blockIdx.x * kAux + 1];
+    for(int w = 0; w < warp; ++w) {
+        oi += s[w][0];
+        ob += s[w][1];
+    }
+    const uint32_t start = oi + ii - vi;
+    ranges[t] = c ? make_uint2(start, start + c) : make_uint2(0u, 0u);
+    bucket_offsets[t] = ob + ib;
+    uint32_t run = start;
+#pragma unroll
+    for(int k = 0; k < GSX_TILE_SUBCOUNTERS; ++k) {
+        run += part[k];
+        sub[(size_t)t * GSX_TILE_SUBCOUNTERS + k] = run;
+    }
+    if(cls >= 0) {
+        uint32_t pos = block_aux[(size_t)blockIdx.x * kAux + 2 + cls] + cpos;
+        for(int w = 0; w < warp; ++w) pos += s[w][2 + cls];
+        class_tiles[pos] = (uint32_t)t;
+    }
+}
+
+/* each instance takes a slot of its tile by counting its sub-counter's end position back down (the
+ * scan turned the counts into end positions) */
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(const unsigned long long *__restrict__ keys,
                                                           const uint32_t *__restrict__ vals, uint64_t n,
-                                                          const uint2 *__restrict__ ranges, uint32_t *__restrict__ tile_count,
+                                                          uint32_t *__restrict__ tile_end,
                                                           unsigned long long *__restrict__ sort_keys)
 {
     const uint64_t i = (uint64_t)blockIdx.x * kBinThreads + threadIdx.x;
     if(i >= n) return;
     const unsigned long long k = keys[i];
     const uint32_t tile = (uint32_t)(k >> 32);
-    const uint32_t slot = atomicSub(&tile_count[tile], 1u) - 1u;
-    sort_keys[ranges[tile].x + slot] = (k << 32) | (unsigned long long)vals[i];
+    const uint32_t slot = atomicSub(&tile_end[tile * GSX_TILE_SUBCOUNTERS + (uint32_t)(i & (GSX_TILE_SUBCOUNTERS - 1))], 1u) - 1u;
+    sort_keys[slot] = (k << 32) | (unsigned long long)vals[i];
 }
 
 /* One CTA per tile (blockIdx -> tile directly, or through `tile_list`) holding kMinN < n <=
@@ -266,11 +355,17 @@ constexpr size_t segsort_smem(int threads, int items) { return (size_t)8 * threa
 
 } // namespace
 
-cudaError_t gsx_launch_tile_scan(const uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
-                                 uint32_t *class_tiles, uint32_t *words_out, cudaStream_t stream)
+size_t gsx_tile_scan_aux_words(int n_tiles) { return (size_t)((n_tiles + kTileThreads - 1) / kTileThreads) * kAux; }
+
+cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
+                                 uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
-    tile_scan_kernel<<<1, kScanThreads, 0, stream>>>(tile_count, n_tiles, ranges, bucket_offsets, class_tiles, words_out);
+    const int blocks = (n_tiles + kTileThreads - 1) / kTileThreads;
+    if(blocks > 1024) return cudaErrorInvalidValue;
+    tile_reduce_kernel<<<blocks, kTileThreads, 0, stream>>>(tile_count, n_tiles, block_aux);
+    block_scan_aux_kernel<<<1, 1024, 0, stream>>>(block_aux, blocks, words_out);
+    tile_write_kernel<<<blocks, kTileThreads, 0, stream>>>(tile_count, n_tiles, block_aux, ranges, bucket_offsets, class_tiles);
     return cudaGetLastError();
 }
 
@@ -300,7 +395,7 @@ cudaError_t launch_class(const uint2 *ranges, const uint32_t *list, uint32_t cou
 } // namespace
 
 cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t *vals, uint64_t n, int n_tiles,
-                                 const uint2 *ranges, uint32_t *tile_count, const uint32_t *class_tiles,
+                                 const uint2 *ranges, uint32_t *tile_end, const uint32_t *class_tiles,
                                  const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
                                  uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev)
 {
@@ -310,8 +405,8 @@ cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t 
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
-    bin_kernel<<<(unsigned)((n + kBinThreads - 1) / kBinThreads), kBinThreads, 0, stream>>>(keys, vals, n, ranges,
-                                                                                          tile_count, sort_keys);
+    bin_kernel<<<(unsigned)((n + kBinThreads - 1) / kBinThreads), kBinThreads, 0, stream>>>(keys, vals, n, tile_end,
+                                                                                          sort_keys);
     err = cudaGetLastError();
     if(err != cudaSuccess) return err;
     /* fork: class c > 0 runs on side[c - 1] after the binning, class 0 on the caller's stream; join */
