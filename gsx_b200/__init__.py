@@ -106,6 +106,12 @@ class RenderContext:
                                           _stream_handle(stream)))
         return dict(n_visible=v.value, n_instances=i.value, n_buckets=b.value)
 
+    def launch_count(self) -> int:
+        """Kernels this context has launched since it was created (host-side count)."""
+        c = ctypes.c_uint64()
+        check(lib().gsx_b200_context_launch_count(self.handle, ctypes.byref(c)))
+        return c.value
+
     def set_profiling(self, enable: bool = True):
         """Record per-stage CUDA events on the launching stream (see read_profile)."""
         check(lib().gsx_b200_context_set_profiling(self.handle, 1 if enable else 0))

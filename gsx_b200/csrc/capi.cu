@@ -145,6 +145,7 @@ struct gsx_b200_context {
     cudaStream_t side[GSX_SORT_CLASSES - 1] = {};
     cudaEvent_t side_ev[GSX_SORT_CLASSES] = {};
     bool side_created = false;
+    uint64_t launches = 0; /* kernels launched by this context (host-side count) */
     /* retained forward state */
     bool has_train = false;
     gsx_b200_gaussians g{};
@@ -332,17 +333,18 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
                      "memset");
         {
             StageTimer st(ctx, 1, stream);
-            /* ranks go to the second half of the value buffer (free until the sort) */
             GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets,
                                          cam.grid_w, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
                                          ctx->inst_cap, words, nullptr, 0, tile_count, stream),
                          "emit launch");
+            ctx->launches += n > 0 ? 1 : 0;
         }
         StageTimer st3(ctx, 3, stream);
         GSX_CUDA_TRY(gsx_launch_tile_scan(tile_count, n_tiles, (uint2 *)ctx->ranges.ptr,
                                           (uint32_t *)ctx->bucket_offsets.ptr, class_tiles,
                                           (uint32_t *)ctx->tile_aux.ptr, words + 2, stream),
                      "tile scan launch");
+        ctx->launches += n_tiles > 0 ? 3 : 0;
         return 0;
     };
     if(n > 0) {
@@ -352,6 +354,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
                                                g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, tile_masks,
                                                block_sums, stream),
                          "preprocess launch");
+            ctx->launches += 2;
         }
         if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
         GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
@@ -398,6 +401,8 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
                                               class_tiles, ctx->host_words + 3, keys_b, keys_a, vals_a, stream, ctx->side,
                                               ctx->side_ev),
                          "tile sort launch");
+            ctx->launches += 1;
+            for(int c = 0; c < GSX_SORT_CLASSES; ++c) ctx->launches += ctx->host_words[3 + c] ? 1 : 0;
         } else {
             /* a tile too large for shared memory: stable global radix sort of the tile|depth keys
              * (emitted in primitive order, so equal depths stay in primitive order) */
@@ -406,6 +411,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
             GSX_CUDA_TRY(gsx_launch_sort_pairs(keys_a, vals_a, keys_b, vals_b, total, 0, end_bit, ctx->sort_scratch.ptr,
                                                ctx->sort_scratch.bytes, words, &in_b, stream),
                          "sort launch");
+            ctx->launches += 1 + (uint64_t)((end_bit + 7) / 8);
         }
     }
     const uint32_t *vals = in_b ? vals_b : vals_a;
@@ -416,6 +422,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
                                           out_rgb, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
                                           (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr, stream),
                  "blend launch");
+    ctx->launches += n_tiles > 0 ? 1 : 0;
     }
     ctx->keys_in_b = in_b;
     ctx->bucket_cap = bucket_cap;
@@ -459,6 +466,7 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
                                                (const uint32_t *)ctx->tile_max.ptr, (const float4 *)ctx->snap.ptr, grad_rgb,
                                                (float4 *)ctx->grad_acc.ptr, n, stream),
                      "blend backward launch");
+        ctx->launches += 1;
     }
     StageTimer st6(ctx, 6, stream);
     GSX_CUDA_TRY(gsx_launch_preprocess_backward(ctx->g.mean3d, ctx->g.rotation, ctx->g.logscale, ctx->g.sh1, ctx->g.sh2,
@@ -466,6 +474,14 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
                                                 (float4 *)ctx->grad_acc.ptr, gr->mean3d, gr->rotation, gr->logscale,
                                                 gr->opacity, gr->sh0, gr->sh1, gr->sh2, gr->sh3, stream),
                  "preprocess backward launch");
+    ctx->launches += 1;
+    return 0;
+}
+
+int gsx_b200_context_launch_count(gsx_b200_context *ctx, uint64_t *out_count)
+{
+    if(ctx == nullptr || out_count == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx and out_count must be non-null");
+    *out_count = ctx->launches;
     return 0;
 }
 

@@ -153,9 +153,6 @@ cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t 
                                  const uint2 *ranges, uint32_t *tile_end, const uint32_t *class_tiles,
                                  const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
                                  uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev);
-cudaError_t gsx_launch_tile_ranges(const unsigned long long *keys, uint64_t count, int n_tiles, uint2 *ranges,
-                                   uint32_t *bucket_offsets, uint32_t *bucket_tile, uint64_t bucket_capacity,
-                                   uint32_t *flags, cudaStream_t stream);
 cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max,

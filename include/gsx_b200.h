@@ -143,6 +143,9 @@ GSX_B200_API int gsx_b200_render_get_view(gsx_b200_context *ctx, gsx_b200_render
  * lookback waits that timed out, capacity overflows) as GSX_B200_UNKNOWN; clears them. */
 GSX_B200_API int gsx_b200_context_check(gsx_b200_context *ctx, void *stream);
 
+/* Number of kernels ctx has launched since it was created (a host-side count, for benchmarks). */
+GSX_B200_API int gsx_b200_context_launch_count(gsx_b200_context *ctx, uint64_t *out_count);
+
 /* Per-stage device timing of the render pipeline with CUDA events on the launching stream (the
  * reference's session timing syncs the stream at every stage instead, gsx-runtime.c:619-680).
  * enable != 0 starts recording (up to 256 launches per stage), enable == 0 stops.  Stages:
