@@ -144,7 +144,7 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
                                   uint32_t *vals_b, uint64_t count, int begin_bit, int end_bit, void *scratch,
                                   size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream);
 #define GSX_SORT_CLASSES 5 /* per-tile sort size classes of k_tilesort.cu */
-#define GSX_TILE_SUBCOUNTERS 8 /* instance counters per tile (emission, binning) */
+#define GSX_TILE_SUBCOUNTERS 32 /* instance counters per tile (emission, binning); a multiple of 4 */
 size_t gsx_tile_scan_aux_words(int n_tiles);
 cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
                                  uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream);

@@ -55,8 +55,11 @@ constexpr int kAux = 2 + kClasses + 1; /* instances, buckets, per-class tiles, m
 __device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub, int t, uint32_t part[GSX_TILE_SUBCOUNTERS])
 {
     const uint4 *p = reinterpret_cast<const uint4 *>(sub + (size_t)t * GSX_TILE_SUBCOUNTERS);
-    const uint4 a = p[0], b = p[1];
-    part[0] = a.x, part[1] = a.y, part[2] = a.z, part[3] = a.w, part[4] = b.x, part[5] = b.y, part[6] = b.z, part[7] = b.w;
+#pragma unroll
+    for(int q = 0; q < GSX_TILE_SUBCOUNTERS / 4; ++q) {
+        const uint4 v = p[q];
+        part[4 * q] = v.x, part[4 * q + 1] = v.y, part[4 * q + 2] = v.z, part[4 * q + 3] = v.w;
+    }
     uint32_t c = 0;
 #pragma unroll
     for(int k = 0; k < GSX_TILE_SUBCOUNTERS; ++k) c += part[k];
@@ -66,7 +69,7 @@ __device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub,
 __global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_t *__restrict__ sub, int n_tiles,
                                                                    uint32_t *__restrict__ block_aux)
 {
-    static_assert(GSX_TILE_SUBCOUNTERS == 8, "two 16-byte loads per tile");
+    static_assert(GSX_TILE_SUBCOUNTERS % 4 == 0, "16-byte loads of the sub-counters");
     __shared__ uint32_t s[kTileThreads / 32][kAux];
     const int t = blockIdx.x * kTileThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -198,10 +201,15 @@ __global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__re
     ranges[t] = c ? make_uint2(start, start + c) : make_uint2(0u, 0u);
     bucket_offsets[t] = ob + ib;
     uint32_t run = start;
+    uint4 *ends = reinterpret_cast<uint4 *>(sub + (size_t)t * GSX_TILE_SUBCOUNTERS);
 #pragma unroll
-    for(int k = 0; k < GSX_TILE_SUBCOUNTERS; ++k) {
-        run += part[k];
-        sub[(size_t)t * GSX_TILE_SUBCOUNTERS + k] = run;
+    for(int q = 0; q < GSX_TILE_SUBCOUNTERS / 4; ++q) {
+        uint4 e;
+        e.x = run += part[4 * q];
+        e.y = run += part[4 * q + 1];
+        e.z = run += part[4 * q + 2];
+        e.w = run += part[4 * q + 3];
+        ends[q] = e;
     }
     if(cls >= 0) {
         uint32_t pos = block_aux[(size_t)blockIdx.x * kAux + 2 + cls] + cpos;
