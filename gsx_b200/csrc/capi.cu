@@ -378,8 +378,11 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     }
     ctx->n_instances = total;
     const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
-    if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
-    if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
+    if(forward_type == GSX_B200_FORWARD_TRAIN) {
+        /* bucket snapshots and the bucket -> tile table exist for the backward only */
+        if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
+        if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
+    }
     const uint64_t kcap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
     unsigned long long *keys_a = (unsigned long long *)ctx->keys.ptr;
     unsigned long long *keys_b = keys_a + kcap;
@@ -420,7 +423,8 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     GSX_CUDA_TRY(gsx_launch_blend_forward(camera->width, camera->height, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
                                           (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
                                           out_rgb, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
-                                          (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr, stream),
+                                          (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr,
+                                          forward_type == GSX_B200_FORWARD_TRAIN, stream),
                  "blend launch");
     ctx->launches += n_tiles > 0 ? 1 : 0;
     }

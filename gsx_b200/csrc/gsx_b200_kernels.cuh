@@ -156,7 +156,7 @@ cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t 
 cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max,
-                                     float4 *snap, uint32_t *bucket_tile, cudaStream_t stream);
+                                     float4 *snap, uint32_t *bucket_tile, bool train, cudaStream_t stream);
 cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const uint2 *ranges,
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
                                       int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,

@@ -6,7 +6,8 @@
  * alpha = min(opacity * exp(-sigma), 0.999), fragments with sigma < 0 or alpha < 1/255 skipped,
  * the pixel stops after the fragment that takes transmittance below 1e-4, a (colour,
  * transmittance) snapshot per pixel before every 32-instance bucket for the backward pass
- * (written for every bucket of every batch the tile processes, as the reference does), and
+ * (written for every bucket of every batch the tile processes, as the reference does; TRAIN
+ * forwards only, an INFERENCE forward has no backward), and
  * out = colour + (1 - alpha) * background.
  *
  * B200 organisation: each warp owns an 8x4 pixel block of the tile.  After a round of up to 512
@@ -112,6 +113,7 @@ __device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, f
     return best;
 }
 
+template <bool kTrain>
 __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     int width, int height, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, float *__restrict__ out_rgb,
@@ -131,8 +133,11 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     const float rx0 = (float)(tx * GSX_TILE + (warp & 1) * 8) + 0.5f, rx1 = rx0 + 7.0f;
     const float ry0 = (float)(ty * GSX_TILE + (warp >> 1) * 4) + 0.5f, ry1 = ry0 + 3.0f;
     const uint2 range = ranges[tile];
-    uint32_t bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
-    for(uint32_t b = bucket + threadIdx.x; b < bucket_offsets[tile]; b += kThreads) bucket_tile[b] = (uint32_t)tile;
+    uint32_t bucket = 0;
+    if(kTrain) {
+        bucket = tile == 0 ? 0u : bucket_offsets[tile - 1];
+        for(uint32_t b = bucket + threadIdx.x; b < bucket_offsets[tile]; b += kThreads) bucket_tile[b] = (uint32_t)tile;
+    }
 
     float cr = 0.0f, cg = 0.0f, cb = 0.0f, T = 1.0f;
     uint32_t ncon = 0;
@@ -172,8 +177,10 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
         __syncwarp();
         int li = 0;
         for(int kb = 0; kb * 32 < batch; ++kb) {
-            snap[(size_t)bucket * kThreads + prank] = make_float4(cr, cg, cb, T);
-            ++bucket;
+            if(kTrain) {
+                snap[(size_t)bucket * kThreads + prank] = make_float4(cr, cg, cb, T);
+                ++bucket;
+            }
             const int bend = (kb + 1) * 32;
             /* two listed instances per iteration: geometry and exp on packed pairs, then the
              * blend applied in order (the second only if the first did not finish the pixel) */
@@ -249,20 +256,21 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
 cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max, float4 *snap,
-                                     uint32_t *bucket_tile, cudaStream_t stream)
+                                     uint32_t *bucket_tile, bool train, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
-    static bool attr_done[256];
+    static bool attr_done[2][256];
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
-    if(dev < 0 || dev >= 256 || !attr_done[dev]) {
-        err = cudaFuncSetAttribute(blend_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FwdSmem));
+    auto kern = train ? blend_forward_kernel<true> : blend_forward_kernel<false>;
+    if(dev < 0 || dev >= 256 || !attr_done[train][dev]) {
+        err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FwdSmem));
         if(err != cudaSuccess) return err;
-        if(dev >= 0 && dev < 256) attr_done[dev] = true;
+        if(dev >= 0 && dev < 256) attr_done[train][dev] = true;
     }
-    blend_forward_kernel<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(
-        width, height, grid_w, ranges, bucket_offsets, vals, rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
-        tile_max, snap, bucket_tile);
+    kern<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(width, height, grid_w, ranges, bucket_offsets, vals, rec,
+                                                                   make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
+                                                                   tile_max, snap, bucket_tile);
     return cudaGetLastError();
 }
