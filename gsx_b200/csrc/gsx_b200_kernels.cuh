@@ -185,6 +185,27 @@ struct AdamTable {
     int count;
 };
 cudaError_t gsx_launch_adam(AdamTable &table, cudaStream_t stream);
+
+/* One Adam element update, gsx-cuda/gsx-cuda-kernels.cu:279-321 (max_grad clamp, decoupled weight
+ * decay, bias corrections in double).  Written with round-to-nearest intrinsics so that no
+ * multiply-add contraction happens whatever the translation unit's -fmad setting: any kernel that
+ * calls it gives the standalone Adam kernel's bits (and the oracle's). */
+__device__ __forceinline__ float gsx_adam_one(float p, float g, float &m1, float &m2, const AdamGroupDev &G)
+{
+    if(G.max_grad > 0.0f) {
+        if(g > G.max_grad) g = G.max_grad;
+        else if(g < -G.max_grad) g = -G.max_grad;
+    }
+    const float a = __fadd_rn(__fmul_rn(G.beta1, m1), __fmul_rn(__fsub_rn(1.0f, G.beta1), g));
+    const float b = __fadd_rn(__fmul_rn(G.beta2, m2), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, G.beta2), g), g));
+    const float ah = (float)((double)a * G.inv_c1);
+    const float bh = (float)((double)b * G.inv_c2);
+    m1 = a;
+    m2 = b;
+    if(G.weight_decay > 0.0f) p = __fsub_rn(p, __fmul_rn(__fmul_rn(G.lr, G.weight_decay), p));
+    return __fsub_rn(p, __fmul_rn(G.lr, ah / __fadd_rn(sqrtf(bh), G.eps)));
+}
+
 cudaError_t gsx_launch_l1_ssim(int mode, const float *pred, const float *target, float *loss_map, float *grad,
                                float *loss_sum, int planes, int height, int width, float l1_scale, float ssim_scale,
                                float l1_grad_scale, float ssim_grad_scale, cudaStream_t stream);

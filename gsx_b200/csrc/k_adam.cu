@@ -16,23 +16,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kChunk = 4096;
 
-__device__ __forceinline__ float adam_one(float p, float g, float &m1, float &m2, const AdamGroupDev &G)
-{
-    if(G.max_grad > 0.0f) {
-        if(g > G.max_grad) g = G.max_grad;
-        else if(g < -G.max_grad) g = -G.max_grad;
-    }
-    const float a = G.beta1 * m1 + (1.0f - G.beta1) * g;
-    const float b = G.beta2 * m2 + (1.0f - G.beta2) * g * g;
-    const float ah = (float)((double)a * G.inv_c1);
-    const float bh = (float)((double)b * G.inv_c2);
-    m1 = a;
-    m2 = b;
-    if(G.weight_decay > 0.0f) p -= G.lr * G.weight_decay * p;
-    p -= G.lr * (ah / (sqrtf(bh) + G.eps));
-    return p;
-}
-
 __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ AdamTable table)
 {
     int gi = 0;
@@ -49,24 +32,24 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
             const float4 g = __ldcs(reinterpret_cast<const float4 *>(G.grad + i));
             float4 a = *reinterpret_cast<const float4 *>(G.m1 + i);
             float4 b = *reinterpret_cast<const float4 *>(G.m2 + i);
-            p.x = adam_one(p.x, g.x, a.x, b.x, G);
-            p.y = adam_one(p.y, g.y, a.y, b.y, G);
-            p.z = adam_one(p.z, g.z, a.z, b.z, G);
-            p.w = adam_one(p.w, g.w, a.w, b.w, G);
+            p.x = gsx_adam_one(p.x, g.x, a.x, b.x, G);
+            p.y = gsx_adam_one(p.y, g.y, a.y, b.y, G);
+            p.z = gsx_adam_one(p.z, g.z, a.z, b.z, G);
+            p.w = gsx_adam_one(p.w, g.w, a.w, b.w, G);
             *reinterpret_cast<float4 *>(G.param + i) = p;
             *reinterpret_cast<float4 *>(G.m1 + i) = a;
             *reinterpret_cast<float4 *>(G.m2 + i) = b;
         }
         for(uint64_t i = vend + threadIdx.x; i < end; i += kThreads) {
             float a = G.m1[i], b = G.m2[i];
-            G.param[i] = adam_one(G.param[i], G.grad[i], a, b, G);
+            G.param[i] = gsx_adam_one(G.param[i], G.grad[i], a, b, G);
             G.m1[i] = a;
             G.m2[i] = b;
         }
     } else {
         for(uint64_t i = start + threadIdx.x; i < end; i += kThreads) {
             float a = G.m1[i], b = G.m2[i];
-            G.param[i] = adam_one(G.param[i], G.grad[i], a, b, G);
+            G.param[i] = gsx_adam_one(G.param[i], G.grad[i], a, b, G);
             G.m1[i] = a;
             G.m2[i] = b;
         }
