@@ -46,7 +46,7 @@ def _ptr(t):
     if not t.is_contiguous():
         raise GsxError(INVALID_ARGUMENT, "tensor must be contiguous")
     import torch
-    if t.dtype != torch.float32 and t.dtype not in (torch.int64, torch.int32, torch.uint64, torch.uint32):
+    if t.dtype not in (torch.float32, torch.bfloat16, torch.int64, torch.int32, torch.uint64, torch.uint32):
         raise GsxError(NOT_SUPPORTED, f"unsupported dtype {t.dtype}")
     return ctypes.c_void_p(t.data_ptr())
 
@@ -130,6 +130,28 @@ class RenderContext:
         return v
 
 
+def _c_gaussians(gaussians: dict):
+    g = _CGaussians()
+    g.count = int(gaussians["mean3d"].shape[0])
+    for k in FIELDS:
+        t = gaussians.get(k)
+        setattr(g, k, _ptr(t).value if t is not None else None)
+    return g
+
+
+def band_rows(height: int, rank: int, world_size: int):
+    """Rows [begin, end) of a frame of `height` rows that rank `rank` of `world_size` renders: whole
+    16-row tile rows dealt out as evenly as possible (earlier ranks take the remainder), so every
+    band starts on a tile row; a rank with no tile row gets an empty band (begin == end)."""
+    if height <= 0 or world_size <= 0 or not 0 <= rank < world_size:
+        raise GsxError(INVALID_ARGUMENT, "band_rows: height, world_size positive and 0 <= rank < world_size")
+    tiles = (height + 15) // 16
+    base, extra = divmod(tiles, world_size)
+    t0 = rank * base + min(rank, extra)
+    t1 = t0 + base + (1 if rank < extra else 0)
+    return min(16 * t0, height), min(16 * t1, height)
+
+
 class Renderer:
     """gsx_renderer: a fixed output size; render()/backward() run on a RenderContext."""
 
@@ -145,17 +167,34 @@ class Renderer:
             raise GsxError(INVALID_ARGUMENT, "camera size must match the renderer size")
         if tuple(out_rgb.shape) != (3, self.height, self.width):
             raise GsxError(INVALID_ARGUMENT, "out_rgb must be [3, H, W]")
-        g = _CGaussians()
-        g.count = int(gaussians["mean3d"].shape[0])
-        for k in FIELDS:
-            t = gaussians.get(k)
-            setattr(g, k, _ptr(t).value if t is not None else None)
+        g = _c_gaussians(gaussians)
         bg = (ctypes.c_float * 3)(*[float(v) for v in background])
         cam = camera.c_struct()
         context._keep = gaussians
         check(lib().gsx_b200_render_forward(context.handle, ctypes.byref(g), int(sh_degree), ctypes.byref(cam), bg,
                                             int(forward_type), _ptr(out_rgb), _stream_handle(stream)))
         return out_rgb
+
+    def render_rows(self, context: RenderContext, gaussians: dict, camera: Camera, row_begin: int, row_end: int,
+                    out, background=(0.0, 0.0, 0.0), sh_degree: int = 0, forward_type: int = FORWARD_TRAIN,
+                    stream=None):
+        """Rows [row_begin, row_end) of the full frame into out ([3, rows, W], f32 or bf16 CUDA tensor);
+        bit-identical to those rows of render().  row_begin must be a multiple of 16."""
+        import torch
+        if camera.width != self.width or camera.height != self.height:
+            raise GsxError(INVALID_ARGUMENT, "camera size must match the renderer size")
+        if tuple(out.shape) != (3, int(row_end) - int(row_begin), self.width):
+            raise GsxError(INVALID_ARGUMENT, "out must be [3, row_end - row_begin, W]")
+        if out.dtype not in (torch.float32, torch.bfloat16):
+            raise GsxError(INVALID_ARGUMENT, "out must be float32 or bfloat16")
+        g = _c_gaussians(gaussians)
+        bg = (ctypes.c_float * 3)(*[float(v) for v in background])
+        cam = camera.c_struct()
+        context._keep = gaussians
+        check(lib().gsx_b200_render_forward_rows(context.handle, ctypes.byref(g), int(sh_degree), ctypes.byref(cam),
+                                                 int(row_begin), int(row_end), bg, int(forward_type), _ptr(out),
+                                                 1 if out.dtype == torch.bfloat16 else 0, _stream_handle(stream)))
+        return out
 
     def backward(self, context: RenderContext, grad_rgb, grads: dict, stream=None):
         """Parameter gradients of the last TRAIN render on `context` (written, not accumulated)."""

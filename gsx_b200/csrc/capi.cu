@@ -72,7 +72,7 @@ void release(DevBuf &b)
     b.bytes = 0;
 }
 
-CameraParams make_camera(const gsx_b200_camera &c)
+CameraParams make_camera(const gsx_b200_camera &c, int row_begin, int row_end)
 {
     /* gsx-cuda/render.c:870-921: normalised quaternion -> row-major R, camera centre -R^T t */
     CameraParams p;
@@ -113,9 +113,10 @@ CameraParams make_camera(const gsx_b200_camera &c)
     p.near_plane = c.near_plane;
     p.far_plane = c.far_plane;
     p.width = c.width;
-    p.height = c.height;
+    p.height = row_end - row_begin;
     p.grid_w = (c.width + GSX_TILE - 1) / GSX_TILE;
-    p.grid_h = (c.height + GSX_TILE - 1) / GSX_TILE;
+    p.grid_h = (p.height + GSX_TILE - 1) / GSX_TILE;
+    p.trow0 = row_begin / GSX_TILE;
     p.clip_l = (-0.15f * p.width_f - p.cx) / p.fx;
     p.clip_r = (1.15f * p.width_f - p.cx) / p.fx;
     p.clip_t = (-0.15f * p.height_f - p.cy) / p.fy;
@@ -252,9 +253,11 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     return 0;
 }
 
-int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int sh_degree,
-                            const gsx_b200_camera *camera, const float background[3], int forward_type, float *out_rgb,
-                            void *stream_)
+namespace {
+
+int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int sh_degree, const gsx_b200_camera *camera,
+                        int row_begin, int row_end, const float background[3], int forward_type, void *out_rgb,
+                        bool out_bf16, void *stream_)
 {
     if(ctx == nullptr || g == nullptr || camera == nullptr || out_rgb == nullptr)
         return fail(GSX_B200_INVALID_ARGUMENT, "ctx, gaussians, camera and out_rgb must be non-null");
@@ -262,6 +265,8 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     if(forward_type != GSX_B200_FORWARD_INFERENCE && forward_type != GSX_B200_FORWARD_TRAIN)
         return fail(GSX_B200_OUT_OF_RANGE, "forward_type must be INFERENCE or TRAIN");
     if(camera->width <= 0 || camera->height <= 0) return fail(GSX_B200_INVALID_ARGUMENT, "camera size must be positive");
+    if(row_begin < 0 || row_begin % GSX_TILE != 0 || row_end <= row_begin || row_end > camera->height)
+        return fail(GSX_B200_OUT_OF_RANGE, "rows must satisfy 0 <= row_begin < row_end <= height, row_begin a multiple of 16");
     if(!(camera->near_plane > 0.0f) || !(camera->far_plane > camera->near_plane))
         return fail(GSX_B200_INVALID_ARGUMENT, "near_plane must be positive and below far_plane");
     if(g->count < 0 || g->count > (int64_t)INT32_MAX) return fail(GSX_B200_OUT_OF_RANGE, "gaussian count out of range");
@@ -273,10 +278,10 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     if(((uintptr_t)g->rotation & 15u) != 0) return fail(GSX_B200_INVALID_ARGUMENT, "rotation must be 16-byte aligned");
     GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
     cudaStream_t stream = (cudaStream_t)stream_;
-    const CameraParams cam = make_camera(*camera);
+    const CameraParams cam = make_camera(*camera, row_begin, row_end);
     const int n_tiles = cam.grid_w * cam.grid_h;
     const int64_t n = g->count;
-    const size_t P = (size_t)camera->width * (size_t)camera->height;
+    const size_t P = (size_t)cam.width * (size_t)cam.height;
     const float bg[3] = { background ? background[0] : 0.0f, background ? background[1] : 0.0f,
                           background ? background[2] : 0.0f };
     ctx->has_train = false;
@@ -334,7 +339,7 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         {
             StageTimer st(ctx, 1, stream);
             GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets,
-                                         cam.grid_w, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
+                                         cam.grid_w, cam.trow0, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
                                          ctx->inst_cap, words, nullptr, 0, tile_count, stream),
                          "emit launch");
             ctx->launches += n > 0 ? 1 : 0;
@@ -420,9 +425,9 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
     const uint32_t *vals = in_b ? vals_b : vals_a;
     {
     StageTimer st4(ctx, 4, stream);
-    GSX_CUDA_TRY(gsx_launch_blend_forward(camera->width, camera->height, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
+    GSX_CUDA_TRY(gsx_launch_blend_forward(cam.width, cam.height, row_begin, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
                                           (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
-                                          out_rgb, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
+                                          out_rgb, out_bf16, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
                                           (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr,
                                           forward_type == GSX_B200_FORWARD_TRAIN, stream),
                  "blend launch");
@@ -438,6 +443,26 @@ int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, 
         ctx->sh_degree = sh_degree;
     }
     return 0;
+}
+
+} // namespace
+
+int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int sh_degree,
+                            const gsx_b200_camera *camera, const float background[3], int forward_type, float *out_rgb,
+                            void *stream)
+{
+    if(camera == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "camera must be non-null");
+    return render_forward_impl(ctx, g, sh_degree, camera, 0, camera->height, background, forward_type, out_rgb, false,
+                               stream);
+}
+
+int gsx_b200_render_forward_rows(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int sh_degree,
+                                 const gsx_b200_camera *camera, int row_begin, int row_end, const float background[3],
+                                 int forward_type, void *out_rgb, int out_bf16, void *stream)
+{
+    if(camera == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "camera must be non-null");
+    return render_forward_impl(ctx, g, sh_degree, camera, row_begin, row_end, background, forward_type, out_rgb,
+                               out_bf16 != 0, stream);
 }
 
 int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const gsx_b200_gaussian_grads *gr,
@@ -463,7 +488,7 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
     const uint32_t *vals = ctx->keys_in_b ? vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t)) : vals_a;
     if(ctx->n_instances > 0) {
         StageTimer st(ctx, 5, stream);
-        GSX_CUDA_TRY(gsx_launch_blend_backward(ctx->cam.width, ctx->cam.height, ctx->cam.grid_w, (const uint2 *)ctx->ranges.ptr,
+        GSX_CUDA_TRY(gsx_launch_blend_backward(ctx->cam.width, ctx->cam.height, ctx->cam.trow0 * GSX_TILE, ctx->cam.grid_w, (const uint2 *)ctx->ranges.ptr,
                                                (const uint32_t *)ctx->bucket_offsets.ptr,
                                                (const uint32_t *)ctx->bucket_tile.ptr, ctx->bucket_cap, ctx->n_tiles, vals,
                                                (const PrimRec *)ctx->rec.ptr, (const float4 *)ctx->pix.ptr,

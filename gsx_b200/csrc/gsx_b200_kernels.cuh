@@ -50,6 +50,10 @@ struct CameraParams {
     /* frustum clamp of the EWA Jacobian in normalised image coordinates (kernels_forward.cuh:324-327),
      * divided once on the host (IEEE, identical bits to a device division) */
     float clip_l, clip_r, clip_t, clip_b;
+    /* band rendering: the image is rows [16 trow0, 16 trow0 + height) of a full frame of height
+     * height_f; every projection, tile test and pixel position uses full-frame coordinates, only
+     * the tile rows kept (grid_h from trow0) and the output rows are the band's.  0 = full frame. */
+    int trow0;
 };
 
 /* Decoupled-lookback status word: 2-bit flag in the top bits, 30-bit count below. */
@@ -133,7 +137,7 @@ cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, co
                                   uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, cudaStream_t stream);
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
-                            uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
+                            uint32_t *offsets, int grid_w, int trow0, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
                             uint32_t *flags, uint32_t *hist, int n_digits, uint32_t *tile_count, cudaStream_t stream);
 cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
                                    uint32_t *vals_b, uint64_t count, const int *positions, const int *shifts,
@@ -153,11 +157,13 @@ cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t 
                                  const uint2 *ranges, uint32_t *tile_end, const uint32_t *class_tiles,
                                  const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
                                  uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev);
-cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
+/* out_rgb: [3, height, width] f32, or bf16 (round to nearest even) when out_bf16; row0 = first pixel
+ * row of the band in the full frame (a multiple of 16, 0 for a full frame) */
+cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
-                                     const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max,
+                                     const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
                                      float4 *snap, uint32_t *bucket_tile, bool train, cudaStream_t stream);
-cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const uint2 *ranges,
+cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_w, const uint2 *ranges,
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
                                       int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,
                                       const uint32_t *tile_max, const float4 *snap, const float *grad_rgb,

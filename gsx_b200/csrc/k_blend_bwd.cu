@@ -118,7 +118,7 @@ __device__ __forceinline__ void cp_async_wait()
 }
 
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
-    int width, int height, int grid_w, int n_tiles, const uint2 *__restrict__ ranges,
+    int width, int height, int row0, int grid_w, int n_tiles, const uint2 *__restrict__ ranges,
     const uint32_t *__restrict__ bucket_offsets, const uint32_t *__restrict__ bucket_tile,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, const float4 *__restrict__ pix,
     const uint32_t *__restrict__ tile_max, const float4 *__restrict__ snap, const float *__restrict__ grad_rgb,
@@ -256,7 +256,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         /* whole warp past every pixel's last contributor: nothing to add, state unchanged */
         if(!__any_sync(0xffffffffu, valid && tpi[0] < last)) continue;
         if(!valid) continue;
-        const f2 fx2 = pk((float)qx, (float)qx), fy2 = pk((float)qy, (float)qy);
+        /* full-frame pixel coordinates (a band starts at row row0) */
+        const f2 fx2 = pk((float)qx, (float)qx), fy2 = pk((float)(qy + row0), (float)(qy + row0));
         const f2 gr2 = pk(gr, gr), gg2 = pk(gg, gg), gb2 = pk(gb, gb);
         {
 #pragma unroll
@@ -330,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
 
 } // namespace
 
-cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const uint2 *ranges,
+cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_w, const uint2 *ranges,
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile,
                                       uint64_t bucket_capacity, int n_tiles, const uint32_t *vals, const PrimRec *rec,
                                       const float4 *pix, const uint32_t *tile_max, const float4 *snap,
@@ -350,7 +351,7 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int grid_w, const u
         if(err != cudaSuccess) return err;
         if(dev >= 0 && dev < 256) attr_done[dev] = true;
     }
-    blend_backward_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, grid_w, n_tiles, ranges,
+    blend_backward_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, row0, grid_w, n_tiles, ranges,
                                                                       bucket_offsets, bucket_tile, vals, rec, pix,
                                                                       tile_max, snap, grad_rgb, grad_acc);
     return cudaGetLastError();

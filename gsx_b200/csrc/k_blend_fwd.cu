@@ -23,6 +23,8 @@
  */
 #include "gsx_b200_kernels.cuh"
 
+#include <cuda_bf16.h>
+
 namespace {
 
 constexpr int kThreads = GSX_TILE_PIXELS;
@@ -113,10 +115,10 @@ __device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, f
     return best;
 }
 
-template <bool kTrain>
+template <bool kTrain, bool kBF16>
 __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
-    int width, int height, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
-    const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, float *__restrict__ out_rgb,
+    int width, int height, int row0, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
+    const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, void *__restrict__ out_rgb,
     float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -129,9 +131,10 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     const int prank = ly * GSX_TILE + lx; /* pixel rank in the tile: snapshot slot */
     const int px = tx * GSX_TILE + lx, py = ty * GSX_TILE + ly;
     const bool inside = px < width && py < height;
-    const float pxf = (float)px + 0.5f, pyf = (float)py + 0.5f;
+    /* arithmetic in full-frame pixel coordinates (a band starts at row row0) */
+    const float pxf = (float)px + 0.5f, pyf = (float)(py + row0) + 0.5f;
     const float rx0 = (float)(tx * GSX_TILE + (warp & 1) * 8) + 0.5f, rx1 = rx0 + 7.0f;
-    const float ry0 = (float)(ty * GSX_TILE + (warp >> 1) * 4) + 0.5f, ry1 = ry0 + 3.0f;
+    const float ry0 = (float)(ty * GSX_TILE + (warp >> 1) * 4 + row0) + 0.5f, ry1 = ry0 + 3.0f;
     const uint2 range = ranges[tile];
     uint32_t bucket = 0;
     if(kTrain) {
@@ -233,9 +236,18 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
         const float a = 1.0f - T;
         const float tr = 1.0f - a;
         const float o0 = cr + tr * bg.x, o1 = cg + tr * bg.y, o2 = cb + tr * bg.z;
-        out_rgb[idx] = o0;
-        out_rgb[P + idx] = o1;
-        out_rgb[2 * P + idx] = o2;
+        if(kBF16) {
+            /* f32 accumulation, one rounding (to nearest even) at the store */
+            __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(out_rgb);
+            o[idx] = __float2bfloat16_rn(o0);
+            o[P + idx] = __float2bfloat16_rn(o1);
+            o[2 * P + idx] = __float2bfloat16_rn(o2);
+        } else {
+            float *o = static_cast<float *>(out_rgb);
+            o[idx] = o0;
+            o[P + idx] = o1;
+            o[2 * P + idx] = o2;
+        }
         pix[idx] = make_float4(o0, o1, o2, __uint_as_float(ncon));
     }
     uint32_t m = ncon;
@@ -253,24 +265,26 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
 
 } // namespace
 
-cudaError_t gsx_launch_blend_forward(int width, int height, int grid_w, int n_tiles, const uint2 *ranges,
+cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
-                                     const float bg[3], float *out_rgb, float4 *pix, uint32_t *tile_max, float4 *snap,
-                                     uint32_t *bucket_tile, bool train, cudaStream_t stream)
+                                     const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
+                                     float4 *snap, uint32_t *bucket_tile, bool train, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
-    static bool attr_done[2][256];
+    static bool attr_done[4][256];
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
-    auto kern = train ? blend_forward_kernel<true> : blend_forward_kernel<false>;
-    if(dev < 0 || dev >= 256 || !attr_done[train][dev]) {
+    const int variant = (train ? 2 : 0) + (out_bf16 ? 1 : 0);
+    auto kern = train ? (out_bf16 ? blend_forward_kernel<true, true> : blend_forward_kernel<true, false>)
+                      : (out_bf16 ? blend_forward_kernel<false, true> : blend_forward_kernel<false, false>);
+    if(dev < 0 || dev >= 256 || !attr_done[variant][dev]) {
         err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(FwdSmem));
         if(err != cudaSuccess) return err;
-        if(dev >= 0 && dev < 256) attr_done[train][dev] = true;
+        if(dev >= 0 && dev < 256) attr_done[variant][dev] = true;
     }
-    kern<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(width, height, grid_w, ranges, bucket_offsets, vals, rec,
-                                                                   make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
+    kern<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(width, height, row0, grid_w, ranges, bucket_offsets, vals,
+                                                                   rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
                                                                    tile_max, snap, bucket_tile);
     return cudaGetLastError();
 }

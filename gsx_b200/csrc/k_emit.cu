@@ -11,6 +11,7 @@
  * the atomics of a crowded tile spread over several addresses; without them it counts, per 8-bit
  * digit position of the emitted keys, a 256-bin histogram from which the host plans the global
  * radix-sort passes (passes whose digit is the same for every key are skipped).
+ * Tile rows are band-relative; the overlap tests use full-frame tile rows (trow0 + row).
  * Compiled with -fmad=false (bit-identical overlap decisions with the preprocess and the oracle).
  */
 #include "gsx_b200_kernels.cuh"
@@ -23,7 +24,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                                                         const uint32_t *__restrict__ counts,
                                                         const uint32_t *__restrict__ tile_masks,
                                                         const uint32_t *__restrict__ block_offsets,
-                                                        uint32_t *__restrict__ offsets, unsigned grid_w,
+                                                        uint32_t *__restrict__ offsets, unsigned grid_w, unsigned trow0,
                                                         unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
                                                         uint64_t capacity, uint32_t *__restrict__ flags,
                                                         uint32_t *__restrict__ hist, int n_digits,
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
     const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
     for(unsigned k = 0; k < nseq; ++k) {
         const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
-        if(gsx_tile_contributes(msx, msy, cx, cy, cz, tx, ty, pt)) {
+        if(gsx_tile_contributes(msx, msy, cx, cy, cz, tx, trow0 + ty, pt)) {
             const unsigned t = ty * grid_w + tx;
             const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
         for(unsigned base = GSX_SEQ_TILES; base < ltmax; base += 32u) {
             const unsigned k = base + (unsigned)lane;
             const unsigned tx = lbx0 + k % lbw, ty = lby0 + k / lbw;
-            const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, tx, ty, lpt);
+            const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, tx, trow0 + ty, lpt);
             const unsigned ballot = __ballot_sync(0xffffffffu, c);
             if(c) {
                 const uint32_t p = lpos + (uint32_t)__popc(ballot & lt_mask);
@@ -149,12 +150,12 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
-                            uint32_t *offsets, int grid_w, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
+                            uint32_t *offsets, int grid_w, int trow0, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
                             uint32_t *flags, uint32_t *hist, int n_digits, uint32_t *tile_count, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
-    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, keys,
+    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, (unsigned)trow0, keys,
                                                             vals, capacity, flags, hist, n_digits, tile_count);
     return cudaGetLastError();
 }

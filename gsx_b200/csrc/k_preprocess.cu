@@ -179,8 +179,10 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
                 int v;
                 v = f2i_rd((m2x - ex) / 16.0f); bx0 = (unsigned)(v > 0 ? v : 0); bx0 = bx0 > gw ? gw : bx0;
                 v = f2i_ru((m2x + ex) / 16.0f); bx1 = (unsigned)(v > 0 ? v : 0); bx1 = bx1 > gw ? gw : bx1;
-                v = f2i_rd((m2y - ey) / 16.0f); by0 = (unsigned)(v > 0 ? v : 0); by0 = by0 > gh ? gh : by0;
-                v = f2i_ru((m2y + ey) / 16.0f); by1 = (unsigned)(v > 0 ? v : 0); by1 = by1 > gh ? gh : by1;
+                /* tile rows in full-frame units clamped to the band [trow0, trow0 + gh), stored band-relative */
+                const int t0 = cam.trow0, t1 = cam.trow0 + (int)gh;
+                v = f2i_rd((m2y - ey) / 16.0f); v = v < t0 ? t0 : (v > t1 ? t1 : v); by0 = (unsigned)(v - t0);
+                v = f2i_ru((m2y + ey) / 16.0f); v = v < t0 ? t0 : (v > t1 ? t1 : v); by1 = (unsigned)(v - t0);
                 if((bx1 - bx0) * (by1 - by0) == 0) active = false;
             }
         }
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     unsigned cnt = 0, tmask = 0;
     const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
     for(unsigned k = 0; k < nseq; ++k) {
-        if(gsx_tile_contributes(msx, msy, conx, cony, conz, bx0 + k % bw, by0 + k / bw, pt)) {
+        if(gsx_tile_contributes(msx, msy, conx, cony, conz, bx0 + k % bw, (unsigned)cam.trow0 + by0 + k / bw, pt)) {
             ++cnt;
             tmask |= 1u << k;
         }
@@ -211,7 +213,8 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
         unsigned sum = 0, first = 0;
         for(unsigned base = GSX_SEQ_TILES; base < ltmax; base += 32u) {
             const unsigned k = base + (unsigned)lane;
-            const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, lbx0 + k % lbw, lby0 + k / lbw, lpt);
+            const bool c = k < ltmax && gsx_tile_contributes(lmx, lmy, lcx, lcy, lcz, lbx0 + k % lbw,
+                                                             (unsigned)cam.trow0 + lby0 + k / lbw, lpt);
             const unsigned b = __ballot_sync(0xffffffffu, c);
             if(base == GSX_SEQ_TILES) first = b;
             sum += (unsigned)__popc(b);

@@ -136,6 +136,12 @@ def teacher(g, seed=1, jitter=0.02, colour_sd=0.1):
     return t
 
 
+def config4_scene(seed=0, n=10_000_000):
+    """Config 4: 10M Gaussians built like config 3 (volume mixture + flat ground slab, 2:1)."""
+    n_slab = n // 3
+    return config3_scene(seed, n_volume=n - n_slab, n_slab=n_slab)
+
+
 def config4_cameras(count=16, width=3840, height=2160, f=2200.0, radius=8.0):
     return [look_at((radius * math.cos(2 * math.pi * k / count), radius * math.sin(2 * math.pi * k / count), 2.0),
                     (0, 0, 0), width, height, f) for k in range(count)]

@@ -109,6 +109,21 @@ GSX_B200_API int gsx_b200_render_forward(gsx_b200_context *ctx, const gsx_b200_g
                             float *out_rgb, void *stream);
 
 /*
+ * Band render: rows [row_begin, row_end) of the full frame that `camera` describes, written as a
+ * [3, row_end - row_begin, width] image.  Every projection, frustum clip, tile test and pixel position
+ * uses full-frame coordinates, so the band is bit-identical to the same rows of
+ * gsx_b200_render_forward; only the band's tiles are binned, sorted and blended.  row_begin must be a
+ * multiple of 16 (a tile row) and row_begin < row_end <= height.  out_bf16 != 0
+ * writes bf16 (round-to-nearest-even of the f32 result) instead of f32.  A TRAIN band is retained for
+ * gsx_b200_render_backward like a full frame, whose grad_rgb is then the band's [3, rows, width].
+ * The frame-split path of a large frame over several GPUs: rank r renders one band (no exchange).
+ */
+GSX_B200_API int gsx_b200_render_forward_rows(gsx_b200_context *ctx, const gsx_b200_gaussians *gaussians, int sh_degree,
+                                 const gsx_b200_camera *camera, int row_begin, int row_end,
+                                 const float background[3], int forward_type, void *out, int out_bf16,
+                                 void *stream);
+
+/*
  * Backward of the last TRAIN forward on ctx: grad_rgb (device [3,H,W]) -> parameter gradients.
  * Replaces gsx_cuda_fastgs_backward_launch (gsx-cuda/render-kernels.cu:249-343), i.e. the body of
  * gsx_cuda_renderer_backward (gsx-cuda/render.c:1425-1571).  Gradients are written for every

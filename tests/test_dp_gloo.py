@@ -106,3 +106,40 @@ def test_dead_peer_is_detected_not_hung():
     res = _run("dead_peer")
     assert res[0][0] == 0
     assert res[0][1].startswith("detected"), res
+
+
+def _band_worker(rank, world, port, height, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        from gsx_b200 import band_rows
+        mine = torch.tensor(band_rows(height, rank, world), dtype=torch.int64)
+        every = [torch.zeros(2, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(every, mine)
+        if rank == 0:
+            out.put([tuple(int(x) for x in t) for t in every])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("height,world", [(2160, 2), (2160, 8), (101, 3), (20, 4)])
+def test_band_rows_partition_the_frame(height, world):
+    """Each rank's band starts on a tile row; the bands, gathered over gloo, tile [0, height) in rank order."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_band_worker, args=(r, world, port, height, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    bands = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    pos = 0
+    for b0, b1 in bands:
+        assert b0 == pos and b1 >= b0 and (b0 % 16 == 0 or b1 == b0)
+        pos = b1
+    assert pos == height
+    tiles = [(b1 - b0 + 15) // 16 for b0, b1 in bands if b1 > b0]
+    assert max(tiles) - min(tiles) <= 1
