@@ -106,6 +106,13 @@ class RenderContext:
                                           _stream_handle(stream)))
         return dict(n_visible=v.value, n_instances=i.value, n_buckets=b.value)
 
+    def bind_aux(self, visible_counter=None, max_screen_radius=None, grad_acc=None, absgrad_acc=None):
+        """Bind the [N] f32 density-control accumulators (None = unbound) for later TRAIN renders
+        (visible_counter, max_screen_radius) and backwards (grad_acc, absgrad_acc)."""
+        self._aux = (visible_counter, max_screen_radius, grad_acc, absgrad_acc)
+        check(lib().gsx_b200_render_bind_aux(self.handle, _ptr(visible_counter), _ptr(max_screen_radius),
+                                             _ptr(grad_acc), _ptr(absgrad_acc)))
+
     def launch_count(self) -> int:
         """Kernels this context has launched since it was created (host-side count)."""
         c = ctypes.c_uint64()

@@ -149,6 +149,8 @@ struct gsx_b200_context {
     uint64_t launches = 0; /* kernels launched by this context (host-side count) */
     /* retained forward state */
     bool has_train = false;
+    /* bound ADC auxiliary accumulators (device [N] f32, NULL = not bound) */
+    float *aux_visible = nullptr, *aux_radius = nullptr, *aux_grad = nullptr, *aux_absgrad = nullptr;
     gsx_b200_gaussians g{};
     int sh_degree = 0;
     CameraParams cam{};
@@ -357,7 +359,8 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
             StageTimer st0(ctx, 0, stream);
             GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2,
                                                g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, tile_masks,
-                                               block_sums, stream),
+                                               block_sums, forward_type == GSX_B200_FORWARD_TRAIN ? ctx->aux_visible : nullptr,
+                                               forward_type == GSX_B200_FORWARD_TRAIN ? ctx->aux_radius : nullptr, stream),
                          "preprocess launch");
             ctx->launches += 2;
         }
@@ -493,7 +496,7 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
                                                (const uint32_t *)ctx->bucket_tile.ptr, ctx->bucket_cap, ctx->n_tiles, vals,
                                                (const PrimRec *)ctx->rec.ptr, (const float4 *)ctx->pix.ptr,
                                                (const uint32_t *)ctx->tile_max.ptr, (const float4 *)ctx->snap.ptr, grad_rgb,
-                                               (float4 *)ctx->grad_acc.ptr, n, stream),
+                                               (float4 *)ctx->grad_acc.ptr, n, ctx->aux_absgrad != nullptr, stream),
                      "blend backward launch");
         ctx->launches += 1;
     }
@@ -501,9 +504,21 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
     GSX_CUDA_TRY(gsx_launch_preprocess_backward(ctx->g.mean3d, ctx->g.rotation, ctx->g.logscale, ctx->g.sh1, ctx->g.sh2,
                                                 ctx->g.sh3, ctx->sh_degree, n, ctx->cam, (const uint32_t *)ctx->counts.ptr,
                                                 (float4 *)ctx->grad_acc.ptr, gr->mean3d, gr->rotation, gr->logscale,
-                                                gr->opacity, gr->sh0, gr->sh1, gr->sh2, gr->sh3, stream),
+                                                gr->opacity, gr->sh0, gr->sh1, gr->sh2, gr->sh3, ctx->aux_grad,
+                                                ctx->aux_absgrad, stream),
                  "preprocess backward launch");
     ctx->launches += 1;
+    return 0;
+}
+
+int gsx_b200_render_bind_aux(gsx_b200_context *ctx, float *visible_counter, float *max_screen_radius, float *grad_acc,
+                             float *absgrad_acc)
+{
+    if(ctx == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx must be non-null");
+    ctx->aux_visible = visible_counter;
+    ctx->aux_radius = max_screen_radius;
+    ctx->aux_grad = grad_acc;
+    ctx->aux_absgrad = absgrad_acc;
     return 0;
 }
 

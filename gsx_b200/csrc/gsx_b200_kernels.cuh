@@ -134,7 +134,8 @@ struct RenderScratch;
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
-                                  uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, cudaStream_t stream);
+                                  uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, float *visible_counter,
+                                  float *max_screen_radius, cudaStream_t stream);
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, int trow0, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
@@ -167,12 +168,13 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
                                       int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,
                                       const uint32_t *tile_max, const float4 *snap, const float *grad_rgb,
-                                      float4 *grad_acc, int64_t n, cudaStream_t stream);
+                                      float4 *grad_acc, int64_t n, bool abs_grad, cudaStream_t stream);
 cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rotation, const float *logscale,
                                            const float *sh1, const float *sh2, const float *sh3, int sh_degree,
                                            int64_t n, const CameraParams &cam, const uint32_t *counts,
                                            float4 *grad_acc, float *g_mean3d, float *g_rotation, float *g_logscale,
                                            float *g_opacity, float *g_sh0, float *g_sh1, float *g_sh2, float *g_sh3,
+                                           float *grad_norm_acc, float *absgrad_norm_acc,
                                            cudaStream_t stream);
 
 #define GSX_ADAM_MAX_GROUPS 16

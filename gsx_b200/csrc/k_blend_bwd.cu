@@ -117,6 +117,11 @@ __device__ __forceinline__ void cp_async_wait()
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+__device__ __forceinline__ f2 abs2(f2 a) { return a & 0x7fffffff7fffffffull; }
+
+/* kAbs: also accumulate sum over pixels of |d loss / d mean2d| per component (the absolute
+ * screen-space gradient behind GSX's gs_absgrad_acc), into grad_acc[3i+2].yz */
+template <bool kAbs>
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     int width, int height, int row0, int grid_w, int n_tiles, const uint2 *__restrict__ ranges,
     const uint32_t *__restrict__ bucket_offsets, const uint32_t *__restrict__ bucket_tile,
@@ -184,8 +189,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     /* accumulators per pair: mean (sum part * d), conic (sum part * d d^T), raw opacity, colour */
     f2 a_mx[kPerLane / 2], a_my[kPerLane / 2], a_cx[kPerLane / 2], a_cy[kPerLane / 2], a_cz[kPerLane / 2];
     f2 a_op[kPerLane / 2], a_r[kPerLane / 2], a_g[kPerLane / 2], a_b[kPerLane / 2];
+    f2 a_ax[kPerLane / 2], a_ay[kPerLane / 2];
 #pragma unroll
     for(int j = 0; j < kPerLane / 2; ++j) a_mx[j] = a_my[j] = a_cx[j] = a_cy[j] = a_cz[j] = a_op[j] = a_r[j] = a_g[j] = a_b[j] = 0ull;
+#pragma unroll
+    for(int j = 0; j < kPerLane / 2; ++j) a_ax[j] = a_ay[j] = 0ull;
 
     const int tx0 = (int)(tile % (uint32_t)grid_w) * GSX_TILE, ty0 = (int)(tile / (uint32_t)grid_w) * GSX_TILE;
     const size_t P = (size_t)width * (size_t)height;
@@ -297,11 +305,20 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
                 a_mx[j] = fma2(part, dx, a_mx[j]);
                 a_my[j] = fma2(part, dy, a_my[j]);
                 a_op[j] = add2(a_op[j], part);
+                if constexpr(kAbs) {
+                    /* |part (conic . d)| per component; the conic terms are held scaled by -log2 e
+                     * (x: -log2e/2), so this is log2 e times the value, rescaled at the flush */
+                    const f2 tx = fma2(f[j].nhcx, add2(dx, dx), mul2(f[j].ncy, dy));
+                    const f2 ty = fma2(f[j].ncy, dx, mul2(f[j].nhcz, add2(dy, dy)));
+                    const f2 ap = abs2(part);
+                    a_ax[j] = fma2(ap, abs2(tx), a_ax[j]);
+                    a_ay[j] = fma2(ap, abs2(ty), a_ay[j]);
+                }
             }
         }
     }
     float u_mx[kPerLane], u_my[kPerLane], u_cx[kPerLane], u_cy[kPerLane], u_cz[kPerLane], u_op[kPerLane];
-    float u_r[kPerLane], u_g[kPerLane], u_b[kPerLane];
+    float u_r[kPerLane], u_g[kPerLane], u_b[kPerLane], u_ax[kPerLane], u_ay[kPerLane];
 #pragma unroll
     for(int j = 0; j < kPerLane / 2; ++j) {
         upk(a_mx[j], u_mx[2 * j], u_mx[2 * j + 1]);
@@ -313,6 +330,8 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         upk(a_r[j], u_r[2 * j], u_r[2 * j + 1]);
         upk(a_g[j], u_g[2 * j], u_g[2 * j + 1]);
         upk(a_b[j], u_b[2 * j], u_b[2 * j + 1]);
+        upk(a_ax[j], u_ax[2 * j], u_ax[2 * j + 1]);
+        upk(a_ay[j], u_ay[2 * j], u_ay[2 * j + 1]);
     }
 #pragma unroll
     for(int k = 0; k < kPerLane; ++k) {
@@ -325,7 +344,12 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         const float gmx = fmaf(cx, u_mx[k], cy * u_my[k]), gmy = fmaf(cy, u_mx[k], cz * u_my[k]);
         atomicAdd(acc + 0, make_float4(-gmx, -gmy, -0.5f * u_cx[k], -u_cy[k]));
         atomicAdd(acc + 1, make_float4(-0.5f * u_cz[k], u_op[k] * (1.0f - r.b.y), u_r[k] * fr, u_g[k] * fg));
-        atomicAdd(&acc[2].x, u_b[k] * fb);
+        if constexpr(kAbs) {
+            constexpr float kLn2 = 0.6931471805599453f; /* 1 / log2(e) */
+            atomicAdd(acc + 2, make_float4(u_b[k] * fb, kLn2 * u_ax[k], kLn2 * u_ay[k], 0.0f));
+        } else {
+            atomicAdd(&acc[2].x, u_b[k] * fb);
+        }
     }
 }
 
@@ -335,23 +359,25 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile,
                                       uint64_t bucket_capacity, int n_tiles, const uint32_t *vals, const PrimRec *rec,
                                       const float4 *pix, const uint32_t *tile_max, const float4 *snap,
-                                      const float *grad_rgb, float4 *grad_acc, int64_t n, cudaStream_t stream)
+                                      const float *grad_rgb, float4 *grad_acc, int64_t n, bool abs_grad,
+                                      cudaStream_t stream)
 {
     (void)n;
     if(bucket_capacity == 0 || n_tiles <= 0) return cudaSuccess;
     const uint64_t per_block = (uint64_t)kWarps * 4;
     const uint64_t blocks = (bucket_capacity + per_block - 1) / per_block;
     const size_t smem = sizeof(SegStage) * kWarps * 4;
-    static bool attr_done[256];
+    static bool attr_done[2][256];
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
-    if(dev < 0 || dev >= 256 || !attr_done[dev]) {
-        err = cudaFuncSetAttribute(blend_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kernel = abs_grad ? blend_backward_kernel<true> : blend_backward_kernel<false>;
+    if(dev < 0 || dev >= 256 || !attr_done[abs_grad][dev]) {
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if(err != cudaSuccess) return err;
-        if(dev >= 0 && dev < 256) attr_done[dev] = true;
+        if(dev >= 0 && dev < 256) attr_done[abs_grad][dev] = true;
     }
-    blend_backward_kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, row0, grid_w, n_tiles, ranges,
+    kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, row0, grid_w, n_tiles, ranges,
                                                                       bucket_offsets, bucket_tile, vals, rec, pix,
                                                                       tile_max, snap, grad_rgb, grad_acc);
     return cudaGetLastError();

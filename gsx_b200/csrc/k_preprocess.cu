@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     const float *__restrict__ opacity_raw, const float *__restrict__ sh0, const float *__restrict__ sh1,
     const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n, CameraParams cam,
     PrimRec *__restrict__ rec, uint32_t *__restrict__ counts, uint32_t *__restrict__ tile_masks,
-    uint32_t *__restrict__ block_sums)
+    uint32_t *__restrict__ block_sums, float *__restrict__ vis_counter, float *__restrict__ max_radius)
 {
     __shared__ float s_m[kThreads * 3];
     __shared__ float s_s[kThreads * 3];
@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     float m[3] = { 0.0f, 0.0f, 0.0f };
     float depth = 0.0f, op = 0.0f, m2x = 0.0f, m2y = 0.0f, conx = 0.0f, cony = 0.0f, conz = 0.0f, pt = 0.0f;
     unsigned bx0 = 0, bx1 = 0, by0 = 0, by1 = 0;
+    float srad = 0.0f;
     const float *w = cam.w2c;
     if(active) {
         m[0] = s_m[threadIdx.x * 3 + 0];
@@ -166,6 +167,13 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
             if(det < 1e-8f) {
                 active = false;
             } else {
+                if(max_radius != nullptr) {
+                    /* screen radius of gsx-metal/kernels/render.metal:432-438: 3 sigma of the larger
+                     * eigenvalue of the dilated 2-D covariance, rounded up */
+                    const float mid = 0.5f * (cov_x + cov_z);
+                    const float disc = sqrtf(fmaxf(0.1f, mid * mid - det));
+                    srad = ceilf(3.0f * sqrtf(fmaxf(mid + disc, mid - disc)));
+                }
                 conx = cov_z / det;
                 cony = -cov_y / det;
                 conz = cov_x / det;
@@ -234,6 +242,10 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
         r.b = make_float4(conz, op, col[0], col[1]);
         r.c = make_float4(col[2], depth, __uint_as_float(bx0 | (bx1 << 16)), __uint_as_float(by0 | (by1 << 16)));
         rec[i] = r;
+        /* TRAIN auxiliary accumulators of a visible (tile-touching) Gaussian,
+         * gsx-metal/kernels/render.metal:425-439 */
+        if(vis_counter != nullptr) vis_counter[i] += 1.0f;
+        if(max_radius != nullptr) max_radius[i] = fmaxf(max_radius[i], srad);
     }
 
     if(i < n) {
@@ -289,13 +301,14 @@ __global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t *__restrict__
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
-                                  uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, cudaStream_t stream)
+                                  uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, float *visible_counter,
+                                  float *max_screen_radius, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
     preprocess_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(
         mean3d, rotation, logscale, opacity, sh0, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, rec, counts,
-        tile_masks, block_sums);
+        tile_masks, block_sums, visible_counter, max_screen_radius);
     block_scan_kernel<<<1, 1024, 0, stream>>>(block_sums, (int)blocks);
     return cudaGetLastError();
 }

@@ -20,7 +20,8 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     const float *__restrict__ sh1, const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n,
     CameraParams cam, const uint32_t *__restrict__ counts, float4 *__restrict__ grad_acc, float *__restrict__ g_mean3d,
     float *__restrict__ g_rotation, float *__restrict__ g_logscale, float *__restrict__ g_opacity,
-    float *__restrict__ g_sh0, float *__restrict__ g_sh1, float *__restrict__ g_sh2, float *__restrict__ g_sh3)
+    float *__restrict__ g_sh0, float *__restrict__ g_sh1, float *__restrict__ g_sh2, float *__restrict__ g_sh3,
+    float *__restrict__ grad_norm_acc, float *__restrict__ absgrad_norm_acc)
 {
     __shared__ float s_m[kThreads * 3];  /* staged mean3d rows, then gradient mean3d rows */
     __shared__ float s_s[kThreads * 3];  /* staged logscale rows, then gradient logscale rows */
@@ -65,6 +66,20 @@ __global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
     const float dm2x = A0.x, dm2y = A0.y, dcx = A0.z, dcy = A0.w, dcz = A1.x;
     const float gc[3] = { A1.z, A1.w, A2.x };
     g_opacity[i] = A1.y;
+    if(grad_norm_acc != nullptr || absgrad_norm_acc != nullptr) {
+        /* ADC statistics, gsx-metal/kernels/render_backward.metal:700-714: screen-space mean gradient
+         * scaled to normalised device units (x W/2, y H/2 of the full frame), its norm and the norm
+         * of the per-pixel absolute gradient (grad_acc[3i+2].yz, written by the blend backward) */
+        const float sx = 0.5f * cam.width_f, sy = 0.5f * cam.height_f;
+        if(grad_norm_acc != nullptr) {
+            const float gx = dm2x * sx, gy = dm2y * sy;
+            grad_norm_acc[i] += sqrtf(gx * gx + gy * gy);
+        }
+        if(absgrad_norm_acc != nullptr) {
+            const float ax = A2.y * sx, ay = A2.z * sy;
+            absgrad_norm_acc[i] += sqrtf(ax * ax + ay * ay);
+        }
+    }
 
     /* SH colour backward */
     float dmc0 = 0.0f, dmc1 = 0.0f, dmc2 = 0.0f;
@@ -257,11 +272,11 @@ cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rot
                                            int64_t n, const CameraParams &cam, const uint32_t *counts,
                                            float4 *grad_acc, float *g_mean3d, float *g_rotation, float *g_logscale,
                                            float *g_opacity, float *g_sh0, float *g_sh1, float *g_sh2, float *g_sh3,
-                                           cudaStream_t stream)
+                                           float *grad_norm_acc, float *absgrad_norm_acc, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     preprocess_backward_kernel<<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, 0, stream>>>(
         mean3d, rotation, logscale, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, counts, grad_acc,
-        g_mean3d, g_rotation, g_logscale, g_opacity, g_sh0, g_sh1, g_sh2, g_sh3);
+        g_mean3d, g_rotation, g_logscale, g_opacity, g_sh0, g_sh1, g_sh2, g_sh3, grad_norm_acc, absgrad_norm_acc);
     return cudaGetLastError();
 }

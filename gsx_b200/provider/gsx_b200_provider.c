@@ -572,7 +572,10 @@ static gsx_error b200_renderer_render(gsx_renderer_t renderer, gsx_render_contex
     {
         const float bg[3] = { r->background_color.x, r->background_color.y, r->background_color.z };
         const int ft = r->forward_type == GSX_RENDER_FORWARD_TYPE_TRAIN ? GSX_B200_FORWARD_TRAIN : GSX_B200_FORWARD_INFERENCE;
-        rc = gsx_b200_render_forward(c->ctx, &g, (int)r->sh_degree, &cam, bg, ft, out, be->stream);
+        /* density-control statistics of a TRAIN forward (gsx-render.h:123-124) */
+        rc = gsx_b200_render_bind_aux(c->ctx, b200_tensor_f32(r->gs_visible_counter), b200_tensor_f32(r->gs_max_screen_radius),
+                                      NULL, NULL);
+        if(rc == 0) rc = gsx_b200_render_forward(c->ctx, &g, (int)r->sh_degree, &cam, bg, ft, out, be->stream);
     }
     if(rc != 0) return b200_lib_error(rc, "gsx_b200_render_forward failed");
     c->has_train = r->forward_type == GSX_RENDER_FORWARD_TYPE_TRAIN;
@@ -601,6 +604,10 @@ static gsx_error b200_renderer_backward(gsx_renderer_t renderer, gsx_render_cont
     if(grad_rgb == NULL || gr.mean3d == NULL || gr.rotation == NULL || gr.logscale == NULL || gr.opacity == NULL || gr.sh0 == NULL)
         return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gsx-b200 renderer requires device-backed gradient tensors");
     B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    /* density-control statistics of the backward (gsx-render.h:143-144) */
+    B200_TRY(b200_lib_error(gsx_b200_render_bind_aux(c->ctx, NULL, NULL, b200_tensor_f32(r->gs_grad_acc),
+                                                     b200_tensor_f32(r->gs_absgrad_acc)),
+                            "gsx_b200_render_bind_aux failed"));
     return b200_lib_error(gsx_b200_render_backward(c->ctx, grad_rgb, &gr, be->stream), "gsx_b200_render_backward failed");
 }
 

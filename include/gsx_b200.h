@@ -158,6 +158,20 @@ GSX_B200_API int gsx_b200_render_get_view(gsx_b200_context *ctx, gsx_b200_render
  * lookback waits that timed out, capacity overflows) as GSX_B200_UNKNOWN; clears them. */
 GSX_B200_API int gsx_b200_context_check(gsx_b200_context *ctx, void *stream);
 
+/*
+ * Bind the density-control statistics of gsx_render_forward_request / gsx_render_backward_request
+ * (gsx-render.h:123-124,143-144): device [N] f32 accumulators, each NULL to leave it unbound; they stay
+ * bound until the next call.  TRAIN forwards add 1 to visible_counter[i] and raise
+ * max_screen_radius[i] to the Gaussian's screen radius (ceil of 3 sigma of the larger eigenvalue of
+ * its dilated 2-D covariance) for every Gaussian that touches a tile; backwards add the norm of the
+ * screen-space mean gradient scaled by (W/2, H/2) to grad_acc[i], and the norm of the per-pixel
+ * absolute gradient, scaled the same way, to absgrad_acc[i].  The reference's CUDA backend fills
+ * none of them; the semantics are those of its Metal backend (gsx-metal/kernels/render.metal:425-439,
+ * render_backward.metal:700-714).  N must cover the Gaussian count of every later call.
+ */
+GSX_B200_API int gsx_b200_render_bind_aux(gsx_b200_context *ctx, float *visible_counter, float *max_screen_radius,
+                             float *grad_acc, float *absgrad_acc);
+
 /* Number of kernels ctx has launched since it was created (a host-side count, for benchmarks). */
 GSX_B200_API int gsx_b200_context_launch_count(gsx_b200_context *ctx, uint64_t *out_count);
 

@@ -162,10 +162,11 @@ static int orc_tile_contributes(float mx, float my, float cx, float cy, float cz
  *   n_touched[N], bounds[N*4] (x_min, x_max, y_min, y_max in tiles), mean2d[N*2],
  *   conic_op[N*4] (conic x,y,z, sigmoid opacity), color[N*3] (unclamped), depth[N].
  * Returns the total instance count. */
-uint64_t orc_preprocess(int64_t n, const float *mean3d, const float *rotation, const float *logscale, const float *opacity_raw,
-                        const float *sh0, const float *sh1, const float *sh2, const float *sh3, int sh_degree,
-                        const orc_camera *cam, uint32_t *n_touched, uint32_t *bounds, float *mean2d, float *conic_op,
-                        float *color, float *depth_out)
+static uint64_t orc_preprocess_impl(int64_t n, const float *mean3d, const float *rotation, const float *logscale,
+                                    const float *opacity_raw, const float *sh0, const float *sh1, const float *sh2,
+                                    const float *sh3, int sh_degree, const orc_camera *cam, uint32_t *n_touched,
+                                    uint32_t *bounds, float *mean2d, float *conic_op, float *color, float *depth_out,
+                                    float *screen_radius)
 {
     const unsigned gw = (unsigned)((cam->width + ORC_TILE - 1) / ORC_TILE);
     const unsigned gh = (unsigned)((cam->height + ORC_TILE - 1) / ORC_TILE);
@@ -244,6 +245,12 @@ uint64_t orc_preprocess(int64_t n, const float *mean3d, const float *rotation, c
         }
         if(cnt == 0) continue;
         n_touched[i] = cnt;
+        if(screen_radius) {
+            /* gsx-metal/kernels/render.metal:432-438 */
+            const float mid = 0.5f * (cov_x + cov_z);
+            const float disc = sqrtf(fmaxf(0.1f, mid * mid - det));
+            screen_radius[i] = ceilf(3.0f * sqrtf(fmaxf(mid + disc, mid - disc)));
+        }
         bounds[i * 4 + 0] = bx0; bounds[i * 4 + 1] = bx1; bounds[i * 4 + 2] = by0; bounds[i * 4 + 3] = by1;
         mean2d[i * 2 + 0] = m2x; mean2d[i * 2 + 1] = m2y;
         conic_op[i * 4 + 0] = conx; conic_op[i * 4 + 1] = cony; conic_op[i * 4 + 2] = conz; conic_op[i * 4 + 3] = op;
@@ -252,6 +259,27 @@ uint64_t orc_preprocess(int64_t n, const float *mean3d, const float *rotation, c
         total += cnt;
     }
     return total;
+}
+
+uint64_t orc_preprocess(int64_t n, const float *mean3d, const float *rotation, const float *logscale, const float *opacity_raw,
+                        const float *sh0, const float *sh1, const float *sh2, const float *sh3, int sh_degree,
+                        const orc_camera *cam, uint32_t *n_touched, uint32_t *bounds, float *mean2d, float *conic_op,
+                        float *color, float *depth_out)
+{
+    return orc_preprocess_impl(n, mean3d, rotation, logscale, opacity_raw, sh0, sh1, sh2, sh3, sh_degree, cam, n_touched,
+                               bounds, mean2d, conic_op, color, depth_out, NULL);
+}
+
+/* The same, also writing the screen radius of every visible (tile-touching) Gaussian: the value a
+ * TRAIN forward folds into gs_max_screen_radius (gsx-metal/kernels/render.metal:425-439; a visible
+ * Gaussian is also the one that raises gs_visible_counter).  Culled Gaussians keep screen_radius[i]. */
+uint64_t orc_preprocess_aux(int64_t n, const float *mean3d, const float *rotation, const float *logscale,
+                            const float *opacity_raw, const float *sh0, const float *sh1, const float *sh2, const float *sh3,
+                            int sh_degree, const orc_camera *cam, uint32_t *n_touched, uint32_t *bounds, float *mean2d,
+                            float *conic_op, float *color, float *depth_out, float *screen_radius)
+{
+    return orc_preprocess_impl(n, mean3d, rotation, logscale, opacity_raw, sh0, sh1, sh2, sh3, sh_degree, cam, n_touched,
+                               bounds, mean2d, conic_op, color, depth_out, screen_radius);
 }
 
 /* ---------------------------------------------------------------- instance emission + sort
@@ -392,10 +420,11 @@ void orc_blend_forward(int width, int height, const uint32_t *ranges, const uint
 static int orc_backward_consistent = 0;
 void orc_set_backward_consistent(int v) { orc_backward_consistent = v; }
 
-void orc_blend_backward(int width, int height, const uint32_t *ranges, const uint32_t *vals, const float *mean2d,
-                        const float *conic_op, const float *color, const float *image, const uint32_t *n_contrib,
-                        const uint32_t *tile_max, const float *grad_rgb, float *d_mean2d, float *d_conic,
-                        float *d_opacity_raw, float *d_color)
+static void orc_blend_backward_impl(int width, int height, const uint32_t *ranges, const uint32_t *vals,
+                                    const float *mean2d, const float *conic_op, const float *color, const float *image,
+                                    const uint32_t *n_contrib, const uint32_t *tile_max, const float *grad_rgb,
+                                    float *d_mean2d, float *d_conic, float *d_opacity_raw, float *d_color,
+                                    float *d_mean2d_abs)
 {
     const int gw = (width + ORC_TILE - 1) / ORC_TILE, gh = (height + ORC_TILE - 1) / ORC_TILE;
     const size_t P = (size_t)width * (size_t)height;
@@ -464,6 +493,11 @@ void orc_blend_backward(int width, int height, const uint32_t *ranges, const uin
                                 d_conic[p * 3 + 2] += -0.5f * part * (dy * dy);
                                 d_mean2d[p * 2 + 0] -= part * (cx * dx + cy * dy);
                                 d_mean2d[p * 2 + 1] -= part * (cy * dx + cz * dy);
+                                if(d_mean2d_abs) {
+                                    /* gsx-metal/kernels/render_backward.metal:361-366 */
+                                    d_mean2d_abs[p * 2 + 0] += fabsf(part * (cx * dx + cy * dy));
+                                    d_mean2d_abs[p * 2 + 1] += fabsf(part * (cy * dx + cz * dy));
+                                }
                                 d_opacity_raw[p] += part * (1.0f - op);
                                 bT *= oma;
                             }
@@ -488,6 +522,26 @@ void orc_blend_backward(int width, int height, const uint32_t *ranges, const uin
             }
         }
     }
+}
+
+void orc_blend_backward(int width, int height, const uint32_t *ranges, const uint32_t *vals, const float *mean2d,
+                        const float *conic_op, const float *color, const float *image, const uint32_t *n_contrib,
+                        const uint32_t *tile_max, const float *grad_rgb, float *d_mean2d, float *d_conic,
+                        float *d_opacity_raw, float *d_color)
+{
+    orc_blend_backward_impl(width, height, ranges, vals, mean2d, conic_op, color, image, n_contrib, tile_max, grad_rgb,
+                            d_mean2d, d_conic, d_opacity_raw, d_color, NULL);
+}
+
+/* The same, also accumulating the per-pixel absolute screen-space mean gradient per component
+ * (d_mean2d_abs[N*2], added to), the input of gs_absgrad_acc. */
+void orc_blend_backward_abs(int width, int height, const uint32_t *ranges, const uint32_t *vals, const float *mean2d,
+                            const float *conic_op, const float *color, const float *image, const uint32_t *n_contrib,
+                            const uint32_t *tile_max, const float *grad_rgb, float *d_mean2d, float *d_conic,
+                            float *d_opacity_raw, float *d_color, float *d_mean2d_abs)
+{
+    orc_blend_backward_impl(width, height, ranges, vals, mean2d, conic_op, color, image, n_contrib, tile_max, grad_rgb,
+                            d_mean2d, d_conic, d_opacity_raw, d_color, d_mean2d_abs);
 }
 
 /* ---------------------------------------------------------------- preprocess backward

@@ -50,6 +50,7 @@ def lib():
             build()
         L = ctypes.CDLL(_LIB)
         L.orc_preprocess.restype = ctypes.c_uint64
+        L.orc_preprocess_aux.restype = ctypes.c_uint64
         L.orc_ssim.restype = ctypes.c_int
         L.orc_sort_pairs.restype = ctypes.c_int
         _lib = L
@@ -102,9 +103,11 @@ def render_forward(g: dict, cam: Camera, sh_degree: int = 0, bg=(0.0, 0.0, 0.0))
     conic_op = np.zeros(n * 4, np.float32)
     color = np.zeros(n * 3, np.float32)
     depth = np.zeros(n, np.float32)
-    total = L.orc_preprocess(ctypes.c_int64(n), _p(mean3d), _p(rot), _p(logscale), _p(op), _p(sh0),
-                             _p(sh[0]), _p(sh[1]), _p(sh[2]), ctypes.c_int(sh_degree), ctypes.byref(c),
-                             _p(n_touched, U32P), _p(bounds, U32P), _p(mean2d), _p(conic_op), _p(color), _p(depth))
+    screen_radius = np.zeros(n, np.float32)
+    total = L.orc_preprocess_aux(ctypes.c_int64(n), _p(mean3d), _p(rot), _p(logscale), _p(op), _p(sh0),
+                                 _p(sh[0]), _p(sh[1]), _p(sh[2]), ctypes.c_int(sh_degree), ctypes.byref(c),
+                                 _p(n_touched, U32P), _p(bounds, U32P), _p(mean2d), _p(conic_op), _p(color), _p(depth),
+                                 _p(screen_radius))
     keys = np.zeros(max(total, 1), np.uint64)
     vals = np.zeros(max(total, 1), np.uint32)
     L.orc_emit(ctypes.c_int64(n), _p(n_touched, U32P), _p(bounds, U32P), _p(mean2d), _p(conic_op), _p(depth),
@@ -127,7 +130,7 @@ def render_forward(g: dict, cam: Camera, sh_degree: int = 0, bg=(0.0, 0.0, 0.0))
                         _p(mean2d), _p(conic_op), _p(color), _p(bgv), _p(out_rgb), _p(out_alpha),
                         _p(n_contrib, U32P), _p(tile_max, U32P))
     return dict(n_touched=n_touched, bounds=bounds.reshape(n, 4), mean2d=mean2d.reshape(n, 2),
-                conic_op=conic_op.reshape(n, 4), color=color.reshape(n, 3), depth=depth,
+                conic_op=conic_op.reshape(n, 4), color=color.reshape(n, 3), depth=depth, screen_radius=screen_radius,
                 n_instances=int(total), unsorted_keys=unsorted_keys, unsorted_vals=unsorted_vals,
                 keys=keys, vals=vals, ranges=ranges.reshape(n_tiles, 2),
                 rgb=out_rgb.reshape(3, cam.height, cam.width), alpha=out_alpha.reshape(cam.height, cam.width),
@@ -146,9 +149,11 @@ def render_backward(g: dict, cam: Camera, fwd: dict, grad_rgb, sh_degree: int = 
     d_conic = np.zeros(n * 3, np.float32)
     d_op = np.zeros(n, np.float32)
     d_color = np.zeros(n * 3, np.float32)
-    L.orc_blend_backward(ctypes.c_int(cam.width), ctypes.c_int(cam.height), _p(r["ranges"], U32P), _p(r["vals"], U32P),
+    d_mean2d_abs = np.zeros(n * 2, np.float32)
+    L.orc_blend_backward_abs(ctypes.c_int(cam.width), ctypes.c_int(cam.height), _p(r["ranges"], U32P), _p(r["vals"], U32P),
                          _p(r["mean2d"]), _p(r["conic_op"]), _p(r["color"]), _p(r["rgb"]), _p(r["n_contrib"], U32P),
-                         _p(r["tile_max"], U32P), _p(grad_rgb), _p(d_mean2d), _p(d_conic), _p(d_op), _p(d_color))
+                         _p(r["tile_max"], U32P), _p(grad_rgb), _p(d_mean2d), _p(d_conic), _p(d_op), _p(d_color),
+                         _p(d_mean2d_abs))
     c = cam.c_struct()
     mean3d, rot, logscale = (_f32(g[k]) for k in ("mean3d", "rotation", "logscale"))
     sh = [_f32(g[k]) if sh_degree >= i + 1 else None for i, k in enumerate(("sh1", "sh2", "sh3"))]
@@ -163,8 +168,28 @@ def render_backward(g: dict, cam: Camera, fwd: dict, grad_rgb, sh_degree: int = 
         if gsh[i] is not None:
             out[k] = gsh[i]
     out["_helpers"] = dict(mean2d=d_mean2d.reshape(n, 2), conic=d_conic.reshape(n, 3), opacity=d_op,
-                           color=d_color.reshape(n, 3))
+                           color=d_color.reshape(n, 3), mean2d_abs=d_mean2d_abs.reshape(n, 2))
     return out
+
+
+def aux_forward(fwd: dict, visible_counter, max_screen_radius):
+    """Fold one TRAIN forward into the density-control accumulators (in place, f32):
+    visible_counter += 1 and max_screen_radius = max(., radius) for every tile-touching Gaussian
+    (gsx-metal/kernels/render.metal:425-439)."""
+    vis = fwd["n_touched"] > 0
+    visible_counter[vis] += np.float32(1.0)
+    max_screen_radius[vis] = np.maximum(max_screen_radius[vis], fwd["screen_radius"][vis])
+
+
+def aux_backward(bwd: dict, cam: "Camera", grad_acc, absgrad_acc):
+    """Fold one backward into grad_acc / absgrad_acc (in place, f32): the norms of the screen-space
+    mean gradient and of the per-pixel absolute gradient, scaled by (W/2, H/2)
+    (gsx-metal/kernels/render_backward.metal:700-714)."""
+    scale = np.array([0.5 * cam.width, 0.5 * cam.height], np.float32)
+    g = bwd["_helpers"]["mean2d"].astype(np.float32) * scale
+    a = bwd["_helpers"]["mean2d_abs"].astype(np.float32) * scale
+    grad_acc += np.sqrt((g * g).sum(1)).astype(np.float32)
+    absgrad_acc += np.sqrt((a * a).sum(1)).astype(np.float32)
 
 
 def sort_pairs(keys, vals):
@@ -315,6 +340,14 @@ class RefSession:
         _ref_check(self.L, self.L.refdrv_session_step(self.h, ctypes.c_float(l1_weight), ctypes.c_float(ssim_weight),
                                                       ctypes.byref(sec)))
         return sec.value
+
+    def enable_aux(self, on=True):
+        """Bind the session's [N] density-control accumulators (zero at creation) on later calls."""
+        _ref_check(self.L, self.L.refdrv_session_enable_aux(self.h, 1 if on else 0))
+
+    def aux(self):
+        """(visible_counter, max_screen_radius, grad_acc, absgrad_acc) as numpy arrays."""
+        return tuple(self.download(11 + k, self.n) for k in range(4))
 
     def download(self, which: int, size: int):
         out = np.zeros(size, np.float32)

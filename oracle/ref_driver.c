@@ -87,6 +87,8 @@ typedef struct refdrv_session {
     gsx_optim_t optim;
     gsx_tensor_t params[8], grads[8];
     gsx_tensor_t out_rgb, target, loss_map, grad_rgb;
+    gsx_tensor_t aux[4]; /* visible_counter, max_screen_radius, grad_acc, absgrad_acc ([N] f32) */
+    int aux_on;
     gsx_camera_intrinsics intr;
     gsx_camera_pose pose;
     float near_plane, far_plane, bg[3];
@@ -106,7 +108,7 @@ int refdrv_session_create(refdrv_session **out, int64_t n, const float *mean3d, 
                           const float lr[8])
 {
     refdrv_session *s = (refdrv_session *)calloc(1, sizeof(refdrv_session));
-    gsx_size_t per_g = (3 + 4 + 3 + 1 + 3 + 9 + 15 + 21) * 2 * 4 + 64;
+    gsx_size_t per_g = (3 + 4 + 3 + 1 + 3 + 9 + 15 + 21) * 2 * 4 + 4 * 4 + 64;
     gsx_size_t bytes = (gsx_size_t)n * per_g + (gsx_size_t)width * height * 4 * 16 + (1u << 20);
     const float *pv[8] = { mean3d, logscale, rotation, opacity, sh0, sh1, sh2, sh3 };
     const int cols[8] = { 3, 3, 4, 1, 3, 9, 15, 21 };
@@ -148,6 +150,11 @@ int refdrv_session_create(refdrv_session **out, int64_t n, const float *mean3d, 
         if(refdrv_tensor(s->arena, &s->target, 3, img, target)) return 1;
         if(refdrv_tensor(s->arena, &s->loss_map, 3, img, NULL)) return 1;
         if(refdrv_tensor(s->arena, &s->grad_rgb, 3, img, NULL)) return 1;
+    }
+    for(int k = 0; k < 4; ++k) {
+        int shape[1] = { (int)n };
+        if(refdrv_tensor(s->arena, &s->aux[k], 1, shape, NULL)) return 1;
+        REF_CHECK(gsx_tensor_set_zero(s->aux[k]));
     }
     memset(&rd, 0, sizeof(rd));
     rd.width = width;
@@ -220,6 +227,17 @@ static void refdrv_fill_forward(refdrv_session *s, gsx_render_forward_request *r
     rq->gs_sh2 = s->sh_degree >= 2 ? s->params[6] : NULL;
     rq->gs_sh3 = s->sh_degree >= 3 ? s->params[7] : NULL;
     rq->out_rgb = s->out_rgb;
+    if(s->aux_on) {
+        rq->gs_visible_counter = s->aux[0];
+        rq->gs_max_screen_radius = s->aux[1];
+    }
+}
+
+/* Bind (on != 0) or unbind the four density-control accumulators on later renders and backwards. */
+int refdrv_session_enable_aux(refdrv_session *s, int on)
+{
+    s->aux_on = on;
+    return 0;
 }
 
 /* Forward INFERENCE render into out_rgb (host CHW). */
@@ -251,6 +269,10 @@ int refdrv_session_render_backward(refdrv_session *s, const float *grad_rgb, flo
     bq.grad_gs_sh1 = s->sh_degree >= 1 ? s->grads[5] : NULL;
     bq.grad_gs_sh2 = s->sh_degree >= 2 ? s->grads[6] : NULL;
     bq.grad_gs_sh3 = s->sh_degree >= 3 ? s->grads[7] : NULL;
+    if(s->aux_on) {
+        bq.gs_grad_acc = s->aux[2];
+        bq.gs_absgrad_acc = s->aux[3];
+    }
     REF_CHECK(gsx_renderer_backward(s->renderer, s->rctx, &bq));
     REF_CHECK(gsx_tensor_download(s->out_rgb, out_rgb, (gsx_size_t)3 * s->width * s->height * 4));
     for(int f = 0; f < s->n_fields; ++f) {
@@ -313,10 +335,12 @@ int refdrv_session_step(refdrv_session *s, float l1_weight, float ssim_weight, d
     return 0;
 }
 
-/* Download the current parameter, loss map or rendered image. which: 0..7 params, 8 out_rgb, 9 loss_map, 10 grad_rgb */
+/* Download the current parameter, loss map or rendered image. which: 0..7 params, 8 out_rgb, 9 loss_map, 10 grad_rgb,
+ * 11..14 visible_counter, max_screen_radius, grad_acc, absgrad_acc */
 int refdrv_session_download(refdrv_session *s, int which, float *dst)
 {
-    gsx_tensor_t t = which < 8 ? s->params[which] : (which == 8 ? s->out_rgb : (which == 9 ? s->loss_map : s->grad_rgb));
+    gsx_tensor_t t = which >= 11 ? s->aux[which - 11]
+                                 : which < 8 ? s->params[which] : (which == 8 ? s->out_rgb : (which == 9 ? s->loss_map : s->grad_rgb));
     gsx_size_t bytes = 0;
     REF_CHECK(gsx_tensor_get_size_bytes(t, &bytes));
     REF_CHECK(gsx_tensor_download(t, dst, bytes));
