@@ -46,7 +46,7 @@ def _ptr(t):
     if not t.is_contiguous():
         raise GsxError(INVALID_ARGUMENT, "tensor must be contiguous")
     import torch
-    if t.dtype not in (torch.float32, torch.bfloat16, torch.int64, torch.int32, torch.uint64, torch.uint32):
+    if t.dtype not in (torch.float32, torch.bfloat16, torch.uint8, torch.int64, torch.int32, torch.uint64, torch.uint32):
         raise GsxError(NOT_SUPPORTED, f"unsupported dtype {t.dtype}")
     return ctypes.c_void_p(t.data_ptr())
 
@@ -144,6 +144,25 @@ def _c_gaussians(gaussians: dict):
         t = gaussians.get(k)
         setattr(g, k, _ptr(t).value if t is not None else None)
     return g
+
+
+def hwc_to_chw(src, out=None, stream=None):
+    """Dataloader layout conversion: a [H, W, 3] (or [H, W]) u8/f32 CUDA image to a [3, H, W] (or
+    [1, H, W]) f32 tensor, values unchanged (gsx_b200_hwc_to_chw_f32)."""
+    import torch
+    if src.dim() not in (2, 3) or (src.dim() == 3 and src.shape[2] not in (1, 3)):
+        raise GsxError(INVALID_ARGUMENT, "src must be [H, W, 3], [H, W, 1] or [H, W]")
+    if src.dtype not in (torch.uint8, torch.float32):
+        raise GsxError(NOT_SUPPORTED, "src must be uint8 or float32")
+    c = 1 if src.dim() == 2 else int(src.shape[2])
+    H, W = int(src.shape[0]), int(src.shape[1])
+    if out is None:
+        out = torch.empty((c, H, W), dtype=torch.float32, device=src.device)
+    if tuple(out.shape) != (c, H, W) or out.dtype != torch.float32:
+        raise GsxError(INVALID_ARGUMENT, "out must be a [C, H, W] float32 tensor")
+    check(lib().gsx_b200_hwc_to_chw_f32(_ptr(src), 8 if src.dtype == torch.uint8 else 0, c, H * W, _ptr(out),
+                                        _stream_handle(stream)))
+    return out
 
 
 def band_rows(height: int, rank: int, world_size: int):

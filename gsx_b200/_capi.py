@@ -70,6 +70,8 @@ SIGNATURES = {
                                                     ctypes.c_int, ctypes.c_void_p]),
     "gsx_b200_render_bind_aux": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                 ctypes.c_void_p]),
+    "gsx_b200_hwc_to_chw_f32": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint64,
+                                               ctypes.c_void_p, ctypes.c_void_p]),
     "gsx_b200_render_backward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(GaussianGrads),
                                                 ctypes.c_void_p]),
     "gsx_b200_render_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64),

@@ -43,6 +43,9 @@ enum {
 
 enum { GSX_B200_FORWARD_INFERENCE = 0, GSX_B200_FORWARD_TRAIN = 1 };
 
+/* element types of gsx_b200_hwc_to_chw_f32's source (the values of gsx_data_type, gsx-core.h:9-11) */
+enum { GSX_B200_DATA_F32 = 0, GSX_B200_DATA_U8 = 8 };
+
 /* Pinhole camera: world->camera rotation (quaternion x, y, z, w) and translation, as
  * gsx_camera_pose (gsx-base.h:211-216) plus gsx_camera_intrinsics fx, fy, cx, cy, width, height. */
 typedef struct gsx_b200_camera {
@@ -260,6 +263,18 @@ GSX_B200_API int gsx_b200_sort_pairs_noalloc(uint64_t *keys, uint32_t *values, u
  */
 GSX_B200_API int gsx_b200_fill_pattern(void *dst, uint64_t size_bytes, const void *pattern, uint32_t pattern_bytes, void *stream);
 GSX_B200_API int gsx_b200_count_nonfinite_f32(const float *x, uint64_t n, uint32_t *device_count, void *stream);
+
+/*
+ * Dataloader layout conversion: an interleaved HWC image of pixel_count pixels (channels 3: RGB;
+ * channels 1: an alpha or inverse-depth plane), u8 or f32 (src_type GSX_B200_DATA_U8 / _F32), to a
+ * planar CHW f32 tensor [channels, H, W] at dst, values unchanged (no 1/255 scaling).  Replaces the
+ * CUDA async dataloader's layout kernels (gsx-cuda/async_dl.cu:45-160, called after the staging
+ * upload at :205-262); results equal the CPU packer gsx_dataloader_pack_hwc_to_chw /
+ * pack_hw_to_chw (gsx-data-impl.h:212-260) with f32 output, for every pixel count.  Device pointers;
+ * f32 buffers 4-byte aligned; 16-byte aligned buffers take the vector path.
+ */
+GSX_B200_API int gsx_b200_hwc_to_chw_f32(const void *src, int src_type, int channels, uint64_t pixel_count, float *dst,
+                                         void *stream);
 
 #ifdef __cplusplus
 }

@@ -353,3 +353,13 @@ class RefSession:
         out = np.zeros(size, np.float32)
         _ref_check(self.L, self.L.refdrv_session_download(self.h, which, _p(out)))
         return out
+
+
+def pack_hwc_to_chw(src):
+    """Dataloader packing to f32 CHW: gsx_dataloader_pack_hwc_to_chw / pack_hw_to_chw with f32 output
+    (gsx/src/gsx-data-impl.h:174-182 read_source_value, :212-240, :242-260): element (y, x, c) of the
+    HWC source goes to (c, y, x), u8 values converted exactly to float, f32 copied."""
+    a = np.asarray(src)
+    if a.ndim == 2:
+        a = a[:, :, None]
+    return np.ascontiguousarray(np.transpose(a, (2, 0, 1)).astype(np.float32))

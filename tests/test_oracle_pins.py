@@ -117,3 +117,13 @@ def test_oracle_sort_is_stable():
     np.testing.assert_array_equal(sk, k[order])
     np.testing.assert_array_equal(sv, v[order])
     assert not math.isnan(float(sk[0]))
+
+
+def test_pack_hwc_to_chw_pinned_to_reference_test():
+    """Known answer of the reference's DataRuntime.NextExProducesFixedCHWOutputAndPreservesMetadata
+    (tests/data_runtime.cpp:386-428): a 2x2 u8 RGB sample with alpha, packed to f32 CHW."""
+    rgb = np.array([0, 10, 20, 40, 50, 60, 80, 90, 100, 120, 130, 140], np.uint8).reshape(2, 2, 3)
+    alpha = np.array([10, 30, 50, 70], np.uint8).reshape(2, 2)
+    np.testing.assert_array_equal(po.pack_hwc_to_chw(rgb).ravel(),
+                                  np.array([0, 40, 80, 120, 10, 50, 90, 130, 20, 60, 100, 140], np.float32))
+    np.testing.assert_array_equal(po.pack_hwc_to_chw(alpha).ravel(), np.array([10, 30, 50, 70], np.float32))
