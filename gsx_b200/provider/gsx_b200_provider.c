@@ -8,13 +8,15 @@
  * compiled with GSX_HAS_CUDA=1 (gsx/src/gsx-backend.c:226), so a GSX build links this file plus
  * libgsx_b200.so in place of its gsx/src/gsx-cuda/ sources and no GSX source changes.
  *
- * Scope (the training hot path): device and pinned-host buffers with the buffer operations the GSX
- * core and front-ends issue on that path (upload/download, set/get/memset/copy/fill, finiteness);
- * the renderer (float32 RGB forward INFERENCE/TRAIN with borrowed or cloned train state, RGB
- * backward); L1/MSE/SSIM losses with MEAN/SUM gradient normalisation; Adam.  Everything else
- * returns GSX_ERROR_NOT_SUPPORTED, as the reference CUDA backend does for what it lacks
- * (gsx-cuda/render.c:766-800, 1583-1592): tensor math ops (unary/reduce/gather/clamp, random
- * fills, image conversion), ADC, the async dataloader, and the optimizer's structural ops.
+ * Scope (the training hot path and what density control needs around it): device and pinned-host
+ * buffers with the buffer operations the GSX core and front-ends issue on that path
+ * (upload/download, set/get/memset/copy/fill, finiteness, row gather, clamp); the renderer (float32
+ * RGB forward INFERENCE/TRAIN with borrowed or cloned train state, RGB backward, the density-control
+ * statistics of the requests); L1/MSE/SSIM losses with MEAN/SUM gradient normalisation; Adam with its
+ * structural ops (permute, gather, resize, reset); the default ADC.  Everything else returns
+ * GSX_ERROR_NOT_SUPPORTED, as the reference CUDA backend does for what it lacks
+ * (gsx-cuda/render.c:766-800, 1583-1592): unary/reduce tensor math, random fills, image conversion,
+ * the async dataloader and the MCMC ADC.
  *
  * Build: compiled against a GSX source tree's headers (gsx/include and gsx/src for gsx-impl.h), see
  * gsx_b200/provider/Makefile.  All work runs on the backend's major stream (gsx-base.h:94-109).
@@ -24,6 +26,7 @@
 #include "gsx_b200.h"
 
 #include <cuda_runtime.h>
+#include <float.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -113,6 +116,8 @@ static float *b200_tensor_f32(gsx_tensor_t t)
     if(t == NULL || t->backing_buffer == NULL || !b200_is_device(t->backing_buffer)) return NULL;
     return (float *)((unsigned char *)b200_buffer_of(t->backing_buffer)->ptr + (size_t)t->offset_bytes);
 }
+
+static int32_t *b200_tensor_i32(gsx_tensor_t t) { return (int32_t *)b200_tensor_f32(t); }
 
 static gsx_error b200_sync(b200_backend *be) { return b200_cuda_error(cudaStreamSynchronize(be->stream), "cudaStreamSynchronize failed"); }
 
@@ -288,12 +293,49 @@ static gsx_error b200_multinomial(gsx_backend_buffer_t b, const gsx_backend_tens
     (void)b, (void)o, (void)c, (void)s, (void)i;
     return B200_UNSUPPORTED("multinomial sampling");
 }
+/* rows of x gathered by an int32 index (gsx-impl.h:373-382; gsx-cuda/buffer.c:1120-1240): the
+ * density-control path's gsx_gs_gather.  An out-of-range index fails with OUT_OF_RANGE. */
 static gsx_error b200_gather(gsx_backend_buffer_t b, const gsx_backend_tensor_view *x, const gsx_backend_tensor_view *ix,
                              const gsx_backend_tensor_view *o, gsx_index_t xr, const gsx_index_t *xs, gsx_index_t orr,
                              const gsx_index_t *os)
 {
-    (void)b, (void)x, (void)ix, (void)o, (void)xr, (void)xs, (void)orr, (void)os;
-    return B200_UNSUPPORTED("tensor gather");
+    b200_backend *be = b200_backend_of_buffer(b);
+    uint32_t bad = 0;
+    gsx_size_t rows = 0, row_bytes = 0;
+    if(x == NULL || ix == NULL || o == NULL || xs == NULL || os == NULL || xr < 1 || orr < 1)
+        return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "gather views and shapes must be non-null");
+    if(ix->data_type != GSX_DATA_TYPE_I32) return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "gather index must be int32");
+    rows = (gsx_size_t)os[0];
+    if(rows == 0) return b200_ok();
+    if(o->size_bytes % rows != 0) return gsx_make_error(GSX_ERROR_INVALID_STATE, "gather output view byte size must be row-aligned");
+    row_bytes = o->size_bytes / rows;
+    if((gsx_size_t)xs[0] * row_bytes != x->size_bytes)
+        return gsx_make_error(GSX_ERROR_INVALID_STATE, "gather x view byte size is inconsistent with row metadata");
+    if(rows * sizeof(int32_t) != ix->size_bytes)
+        return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "index view byte size must match out leading dimension");
+    if(row_bytes == 0) return b200_ok();
+    B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    if(!b200_is_device(b) || !b200_is_device(x->buffer) || !b200_is_device(ix->buffer)) {
+        const unsigned char *src = b200_view_ptr(x);
+        const int32_t *idx = (const int32_t *)b200_view_ptr(ix);
+        unsigned char *dst = b200_view_ptr(o);
+        if(b200_is_device(b) || b200_is_device(x->buffer) || b200_is_device(ix->buffer))
+            return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gather across device and host buffers is not supported");
+        B200_TRY(b200_sync(be));
+        for(gsx_size_t r = 0; r < rows; ++r) {
+            if(idx[r] < 0 || (gsx_size_t)idx[r] >= (gsx_size_t)xs[0]) return gsx_make_error(GSX_ERROR_OUT_OF_RANGE, "gather index is out of range");
+            memcpy(dst + r * row_bytes, src + (gsx_size_t)idx[r] * row_bytes, (size_t)row_bytes);
+        }
+        return b200_ok();
+    }
+    B200_TRY(b200_cuda_error(cudaMemsetAsync(be->finite_word, 0, sizeof(uint32_t), be->stream), "cudaMemsetAsync failed"));
+    B200_TRY(b200_lib_error(gsx_b200_gather_rows(b200_view_ptr(x), (uint64_t)xs[0], row_bytes, (const int32_t *)b200_view_ptr(ix),
+                                                 rows, b200_view_ptr(o), be->finite_word, be->stream),
+                            "gsx_b200_gather_rows failed"));
+    B200_TRY(b200_cuda_error(cudaMemcpyAsync(&bad, be->finite_word, sizeof(bad), cudaMemcpyDeviceToHost, be->stream), "D2H failed"));
+    B200_TRY(b200_sync(be));
+    if(bad != 0) return gsx_make_error(GSX_ERROR_OUT_OF_RANGE, "gather index is out of range");
+    return b200_ok();
 }
 static gsx_error b200_unary(gsx_backend_buffer_t b, const gsx_backend_tensor_view *x, const gsx_backend_tensor_view *o,
                             gsx_index_t r, const gsx_index_t *s, gsx_impl_unary_op op)
@@ -321,10 +363,39 @@ static gsx_error b200_binary_reduce(gsx_backend_buffer_t b, const gsx_backend_te
     (void)b, (void)l, (void)r, (void)o, (void)w, (void)lr, (void)ls, (void)rr, (void)rs, (void)orr, (void)os, (void)a, (void)op;
     return B200_UNSUPPORTED("tensor reductions");
 }
+/* in-place clamp (gsx-cuda/buffer.c:1985-2060): density control's opacity reset */
 static gsx_error b200_clamp(gsx_backend_buffer_t b, const gsx_backend_tensor_view *v, const void *lo, const void *hi)
 {
-    (void)b, (void)v, (void)lo, (void)hi;
-    return B200_UNSUPPORTED("tensor clamp");
+    b200_backend *be = b200_backend_of_buffer(b);
+    gsx_size_t es = 0;
+    if(v == NULL || lo == NULL || hi == NULL) return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "clamp view and bounds must be non-null");
+    if(v->data_type == GSX_DATA_TYPE_F32 || v->data_type == GSX_DATA_TYPE_I32) es = 4;
+    else if(v->data_type == GSX_DATA_TYPE_U8) es = 1;
+    else return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "clamp supports float32, int32 and uint8");
+    if(v->size_bytes % es != 0) return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "tensor view byte size is not aligned to element size");
+    B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    if(!b200_is_device(b)) {
+        unsigned char *p = b200_view_ptr(v);
+        B200_TRY(b200_sync(be));
+        for(gsx_size_t i = 0; i < v->size_bytes / es; ++i) {
+            if(v->data_type == GSX_DATA_TYPE_F32) {
+                float *x = (float *)p + i;
+                if(*x < *(const float *)lo) *x = *(const float *)lo;
+                else if(*x > *(const float *)hi) *x = *(const float *)hi;
+            } else if(v->data_type == GSX_DATA_TYPE_I32) {
+                int32_t *x = (int32_t *)p + i;
+                if(*x < *(const int32_t *)lo) *x = *(const int32_t *)lo;
+                else if(*x > *(const int32_t *)hi) *x = *(const int32_t *)hi;
+            } else {
+                uint8_t *x = p + i;
+                if(*x < *(const uint8_t *)lo) *x = *(const uint8_t *)lo;
+                else if(*x > *(const uint8_t *)hi) *x = *(const uint8_t *)hi;
+            }
+        }
+        return b200_ok();
+    }
+    return b200_lib_error(gsx_b200_clamp_inplace(b200_view_ptr(v), (int)v->data_type, v->size_bytes / es, lo, hi, be->stream),
+                          "gsx_b200_clamp_inplace failed");
 }
 static gsx_error b200_img_colorspace(gsx_backend_buffer_t b, const gsx_backend_tensor_view *s, gsx_storage_format f,
                                      gsx_index_t r, const gsx_index_t *sh, gsx_image_colorspace sc,
@@ -760,6 +831,7 @@ typedef struct b200_optim {
     float **m1, **m2;     /* per group, device, parameter-sized */
     uint64_t *counts;     /* elements per group */
     uint64_t *steps;      /* Adam step counter per group (bias correction) */
+    uint64_t *rows;       /* leading extent (Gaussians) the moments currently hold, per group */
 } b200_optim;
 
 static gsx_error b200_optim_free_state(b200_optim *o)
@@ -772,6 +844,7 @@ static gsx_error b200_optim_free_state(b200_optim *o)
     free(o->m2);
     free(o->counts);
     free(o->steps);
+    free(o->rows);
     return b200_ok();
 }
 
@@ -844,20 +917,157 @@ static gsx_error b200_optim_reset_all(gsx_optim_t optim)
     return b200_ok();
 }
 
+/* ---- structural ops of density control (gsx-cuda/optim.c:846-1195): the moments follow the
+ * Gaussians when the set is permuted, gathered (grown / pruned) or resized.  New moment buffers are
+ * filled first and swapped in only when everything succeeded, so a failing call leaves the state. */
+
+/* leading extent of a parameter tensor (its Gaussian count) */
+static gsx_size_t b200_rows_of(gsx_tensor_t t) { return t != NULL && t->rank >= 1 ? (gsx_size_t)t->shape[0] : 0; }
+
+/* the common old / new Gaussian counts of all groups, with matching row widths */
+static gsx_error b200_optim_transition(b200_optim *o, gsx_size_t *old_rows, gsx_size_t *new_rows, const char *what)
+{
+    for(gsx_index_t i = 0; i < o->base.param_group_count; ++i) {
+        const gsx_tensor_t p = o->base.param_groups[i].parameter;
+        const gsx_size_t orow = o->rows[i], nrow = b200_rows_of(p);
+        const gsx_size_t elems = p->size_bytes / sizeof(float);
+        if(orow == 0 || nrow == 0 || o->counts[i] % orow != 0 || elems % nrow != 0 || o->counts[i] / orow != elems / nrow)
+            return gsx_make_error(GSX_ERROR_INVALID_STATE, "optimizer state and parameter row layouts do not match");
+        if(i == 0) {
+            *old_rows = orow;
+            *new_rows = nrow;
+        } else if(orow != *old_rows || nrow != *new_rows) {
+            return gsx_make_error(GSX_ERROR_INVALID_STATE, what);
+        }
+    }
+    return b200_ok();
+}
+
+/* rank-1 int32 device tensor of `count` entries, downloaded for validation */
+static gsx_error b200_optim_indices(b200_optim *o, gsx_tensor_t t, gsx_size_t count, int32_t **out, const char *msg)
+{
+    b200_backend *be = b200_backend_of(o->base.backend);
+    *out = NULL;
+    if(t->rank != 1 || t->data_type != GSX_DATA_TYPE_I32 || (gsx_size_t)t->shape[0] != count || b200_tensor_i32(t) == NULL)
+        return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, msg);
+    *out = (int32_t *)malloc((size_t)(count ? count : 1) * sizeof(int32_t));
+    if(*out == NULL) return gsx_make_error(GSX_ERROR_OUT_OF_MEMORY, "failed to allocate optimizer index validation storage");
+    B200_TRY(b200_cuda_error(cudaMemcpyAsync(*out, b200_tensor_i32(t), (size_t)count * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                             be->stream),
+                             "index download failed"));
+    return b200_sync(be);
+}
+
+/* new moments: rows gathered by `index` (device, new_rows entries), or (index == NULL) the first
+ * min(old, new) rows copied and the rest zero */
+static gsx_error b200_optim_rebuild(b200_optim *o, gsx_size_t old_rows, gsx_size_t new_rows, const int32_t *index)
+{
+    b200_backend *be = b200_backend_of(o->base.backend);
+    const gsx_index_t ng = o->base.param_group_count;
+    float **n1 = (float **)calloc((size_t)ng, sizeof(float *)), **n2 = (float **)calloc((size_t)ng, sizeof(float *));
+    gsx_error err = b200_ok();
+    if(n1 == NULL || n2 == NULL) {
+        free(n1);
+        free(n2);
+        return gsx_make_error(GSX_ERROR_OUT_OF_MEMORY, "failed to allocate optimizer state records");
+    }
+    for(gsx_index_t i = 0; i < ng && gsx_error_is_success(err); ++i) {
+        const gsx_size_t width = o->counts[i] / old_rows, bytes = new_rows * width * sizeof(float);
+        float *src[2] = { o->m1[i], o->m2[i] };
+        float **dst[2] = { &n1[i], &n2[i] };
+        for(int m = 0; m < 2 && gsx_error_is_success(err); ++m) {
+            err = b200_cuda_error(cudaMalloc((void **)dst[m], (size_t)(bytes ? bytes : sizeof(float))), "optimizer state allocation failed");
+            if(!gsx_error_is_success(err)) break;
+            if(index != NULL) {
+                err = b200_lib_error(gsx_b200_gather_rows(src[m], old_rows, width * sizeof(float), index, new_rows, *dst[m], NULL,
+                                                          be->stream),
+                                     "gsx_b200_gather_rows failed");
+            } else {
+                const gsx_size_t keep = (old_rows < new_rows ? old_rows : new_rows) * width * sizeof(float);
+                err = b200_cuda_error(cudaMemsetAsync(*dst[m], 0, (size_t)bytes, be->stream), "cudaMemsetAsync failed");
+                if(gsx_error_is_success(err) && keep)
+                    err = b200_cuda_error(cudaMemcpyAsync(*dst[m], src[m], (size_t)keep, cudaMemcpyDeviceToDevice, be->stream),
+                                          "cudaMemcpyAsync failed");
+            }
+        }
+    }
+    if(gsx_error_is_success(err)) err = b200_sync(be);
+    for(gsx_index_t i = 0; i < ng; ++i) {
+        if(gsx_error_is_success(err)) {
+            cudaFree(o->m1[i]);
+            cudaFree(o->m2[i]);
+            o->m1[i] = n1[i];
+            o->m2[i] = n2[i];
+            o->counts[i] = new_rows * (o->counts[i] / old_rows);
+            o->rows[i] = new_rows;
+        } else {
+            if(n1[i]) cudaFree(n1[i]);
+            if(n2[i]) cudaFree(n2[i]);
+        }
+    }
+    free(n1);
+    free(n2);
+    return err;
+}
+
 static gsx_error b200_optim_permute(gsx_optim_t optim, gsx_tensor_t permutation)
 {
-    (void)optim, (void)permutation;
-    return B200_UNSUPPORTED("optimizer state permutation (density control)");
+    b200_optim *o = (b200_optim *)optim;
+    b200_backend *be = b200_backend_of(optim->backend);
+    gsx_size_t old_rows = 0, new_rows = 0;
+    int32_t *idx = NULL;
+    bool *seen = NULL;
+    gsx_error err;
+    if(optim->param_group_count == 0) return b200_ok();
+    B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    B200_TRY(b200_optim_transition(o, &old_rows, &new_rows, "optimizer param groups must share the same leading extent for permutation"));
+    if(old_rows != new_rows) return gsx_make_error(GSX_ERROR_INVALID_STATE, "optimizer permutation requires an unchanged leading extent");
+    err = b200_optim_indices(o, permutation, old_rows, &idx, "optimizer permutation tensor must be rank-1 int32");
+    if(gsx_error_is_success(err)) {
+        seen = (bool *)calloc((size_t)old_rows, sizeof(bool));
+        if(seen == NULL) err = gsx_make_error(GSX_ERROR_OUT_OF_MEMORY, "failed to allocate optimizer permutation validation storage");
+    }
+    for(gsx_size_t r = 0; r < old_rows && gsx_error_is_success(err); ++r) {
+        if(idx[r] < 0) err = gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "optimizer permutation entries must be non-negative");
+        else if((gsx_size_t)idx[r] >= old_rows) err = gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "optimizer permutation entries must be in range");
+        else if(seen[idx[r]]) err = gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "optimizer permutation entries must be unique");
+        else seen[idx[r]] = true;
+    }
+    free(seen);
+    free(idx);
+    if(!gsx_error_is_success(err)) return err;
+    return b200_optim_rebuild(o, old_rows, new_rows, b200_tensor_i32(permutation));
 }
+
 static gsx_error b200_optim_gather(gsx_optim_t optim, gsx_tensor_t indices)
 {
-    (void)optim, (void)indices;
-    return B200_UNSUPPORTED("optimizer state gather (density control)");
+    b200_optim *o = (b200_optim *)optim;
+    b200_backend *be = b200_backend_of(optim->backend);
+    gsx_size_t old_rows = 0, new_rows = 0;
+    int32_t *idx = NULL;
+    gsx_error err;
+    if(optim->param_group_count == 0) return b200_ok();
+    B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    B200_TRY(b200_optim_transition(o, &old_rows, &new_rows, "optimizer param groups must share the same leading extents for gather"));
+    err = b200_optim_indices(o, indices, new_rows, &idx, "optimizer indices tensor must be rank-1 int32");
+    for(gsx_size_t r = 0; r < new_rows && gsx_error_is_success(err); ++r)
+        if(idx[r] < 0 || (gsx_size_t)idx[r] >= old_rows) err = gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "optimizer gather indices must be in range");
+    free(idx);
+    if(!gsx_error_is_success(err)) return err;
+    return b200_optim_rebuild(o, old_rows, new_rows, b200_tensor_i32(indices));
 }
+
 static gsx_error b200_optim_resize(gsx_optim_t optim, gsx_size_t count)
 {
-    (void)optim, (void)count;
-    return B200_UNSUPPORTED("optimizer state resize (density control)");
+    b200_optim *o = (b200_optim *)optim;
+    b200_backend *be = b200_backend_of(optim->backend);
+    gsx_size_t old_rows = 0, new_rows = 0;
+    if(optim->param_group_count == 0) return b200_ok();
+    B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    B200_TRY(b200_optim_transition(o, &old_rows, &new_rows, "optimizer param groups must share the same leading extents for resize"));
+    if(new_rows != count)
+        return gsx_make_error(GSX_ERROR_INVALID_STATE, "optimizer resize expects parameter tensors to already expose the target leading extent");
+    return b200_optim_rebuild(o, old_rows, new_rows, NULL);
 }
 
 static const gsx_optim_i b200_optim_iface = { b200_optim_destroy,   b200_optim_step_selected, b200_optim_permute,
@@ -883,7 +1093,8 @@ static gsx_error b200_create_optim(gsx_backend_t backend, const gsx_optim_desc *
     o->m2 = (float **)calloc((size_t)ng, sizeof(float *));
     o->counts = (uint64_t *)calloc((size_t)ng, sizeof(uint64_t));
     o->steps = (uint64_t *)calloc((size_t)ng, sizeof(uint64_t));
-    if(o->m1 == NULL || o->m2 == NULL || o->counts == NULL || o->steps == NULL) {
+    o->rows = (uint64_t *)calloc((size_t)ng, sizeof(uint64_t));
+    if(o->m1 == NULL || o->m2 == NULL || o->counts == NULL || o->steps == NULL || o->rows == NULL) {
         b200_optim_free_state(o);
         gsx_optim_base_deinit(&o->base);
         free(o);
@@ -899,6 +1110,7 @@ static gsx_error b200_create_optim(gsx_backend_t backend, const gsx_optim_desc *
             return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gsx-b200 Adam requires float32 device parameters");
         }
         o->counts[i] = pg->parameter->size_bytes / sizeof(float);
+        o->rows[i] = b200_rows_of(pg->parameter);
         const size_t bytes = (size_t)(o->counts[i] ? o->counts[i] : 1) * sizeof(float);
         ce = cudaMalloc((void **)&o->m1[i], bytes);
         if(ce == cudaSuccess) ce = cudaMalloc((void **)&o->m2[i], bytes);
@@ -1007,11 +1219,305 @@ static gsx_error b200_backend_binary_ws(gsx_backend_t b, gsx_backend_buffer_type
     return B200_UNSUPPORTED("tensor reductions");
 }
 
+/* ------------------------------------------------------------------------------------------ */
+/* density control: GSX's default ADC (gsx-cuda/adc.cu:948-1040) with the device stages of
+ * libgsx_b200 (gsx_b200_adc_*) and GSX's own gsx_gs_gather / gsx_optim_gather for the structural
+ * changes, so the Gaussian set, its auxiliary statistics and the optimizer moments move together. */
+
+typedef struct b200_adc {
+    struct gsx_adc base;
+} b200_adc;
+
+typedef struct b200_adc_fields {
+    float *mean3d, *logscale, *opacity, *rotation, *grad_acc, *visible_counter, *max_screen_radius;
+} b200_adc_fields;
+
+static gsx_size_t b200_nonneg(gsx_index_t v) { return v <= 0 ? 0 : (gsx_size_t)v; }
+
+/* refine / reset windows of gsx-cuda/adc.cu:78-110 */
+static bool b200_adc_refine_window(const gsx_adc_desc *d, gsx_size_t step)
+{
+    if(d->refine_every == 0 || step % (gsx_size_t)d->refine_every != 0) return false;
+    return step >= b200_nonneg(d->start_refine) && step <= b200_nonneg(d->end_refine);
+}
+
+static bool b200_adc_reset_window(const gsx_adc_desc *d, gsx_size_t step)
+{
+    if(d->reset_every == 0 || step % (gsx_size_t)d->reset_every != 0) return false;
+    return step >= b200_nonneg(d->start_refine) && step < b200_nonneg(d->end_refine);
+}
+
+static bool b200_adc_optim_enabled(const gsx_adc_request *r) { return r->optim != NULL && r->optim->iface != NULL; }
+
+static gsx_error b200_adc_count(gsx_gs_t gs, gsx_size_t *out)
+{
+    gsx_gs_info info;
+    memset(&info, 0, sizeof(info));
+    B200_TRY(gsx_gs_get_info(gs, &info));
+    *out = info.count;
+    return b200_ok();
+}
+
+static gsx_error b200_adc_field(gsx_gs_t gs, gsx_gs_field field, gsx_size_t count, gsx_size_t dim1, bool optional,
+                                const char *missing, float **out)
+{
+    gsx_tensor_t t = NULL;
+    *out = NULL;
+    if(!gsx_error_is_success(gsx_gs_get_field(gs, field, &t)))
+        return optional ? b200_ok() : gsx_make_error(GSX_ERROR_NOT_SUPPORTED, missing);
+    if(t->data_type != GSX_DATA_TYPE_F32)
+        return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gsx-b200 default adc supports only float32 gs fields");
+    B200_TRY(gsx_adc_validate_gs_field_shape(t, count, dim1));
+    *out = b200_tensor_f32(t);
+    if(*out == NULL) return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gsx-b200 default adc requires device-backed gs fields");
+    return b200_ok();
+}
+
+/* the fields the refine pass reads (gsx-cuda/adc.cu:187-277, same requirements and messages) */
+static gsx_error b200_adc_load(gsx_gs_t gs, gsx_size_t n, b200_adc_fields *f)
+{
+    float *unused = NULL;
+    memset(f, 0, sizeof(*f));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_MEAN3D, n, 3, false, "cuda default adc refine requires GSX_GS_FIELD_MEAN3D access", &f->mean3d));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_GRAD_ACC, n, 1, true, NULL, &f->grad_acc));
+    if(f->grad_acc == NULL)
+        return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "cuda default adc refine requires GSX_GS_FIELD_GRAD_ACC auxiliary field");
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_VISIBLE_COUNTER, n, 1, true, NULL, &f->visible_counter));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_LOGSCALE, n, 3, false, "cuda default adc refine requires GSX_GS_FIELD_LOGSCALE access", &f->logscale));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_OPACITY, n, 1, false, "cuda default adc refine requires GSX_GS_FIELD_OPACITY access", &f->opacity));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_ROTATION, n, 4, false, "cuda default adc refine requires GSX_GS_FIELD_ROTATION access", &f->rotation));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_SH0, n, 3, false, "cuda default adc refine requires GSX_GS_FIELD_SH0 access", &unused));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_SH1, n, 9, true, NULL, &unused));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_SH2, n, 15, true, NULL, &unused));
+    B200_TRY(b200_adc_field(gs, GSX_GS_FIELD_SH3, n, 21, true, NULL, &unused));
+    return b200_adc_field(gs, GSX_GS_FIELD_MAX_SCREEN_RADIUS, n, 1, true, NULL, &f->max_screen_radius);
+}
+
+/* a rank-1 int32 index tensor over a fresh buffer of the Gaussian set's buffer type */
+static gsx_error b200_adc_index_tensor(gsx_gs_t gs, gsx_size_t count, gsx_backend_buffer_t *buf, struct gsx_tensor *t)
+{
+    gsx_tensor_t mean3d = NULL;
+    gsx_backend_buffer_desc bd;
+    if(count == 0 || count > (gsx_size_t)INT32_MAX) return gsx_make_error(GSX_ERROR_OUT_OF_RANGE, "index count exceeds supported int32 range");
+    B200_TRY(gsx_gs_get_field(gs, GSX_GS_FIELD_MEAN3D, &mean3d));
+    memset(&bd, 0, sizeof(bd));
+    bd.buffer_type = mean3d->backing_buffer->buffer_type;
+    bd.size_bytes = count * sizeof(int32_t);
+    bd.alignment_bytes = sizeof(int32_t);
+    B200_TRY(gsx_backend_buffer_init(buf, &bd));
+    memset(t, 0, sizeof(*t));
+    t->arena = mean3d->arena;
+    t->backing_buffer = *buf;
+    t->size_bytes = bd.size_bytes;
+    t->alloc_span_bytes = bd.size_bytes;
+    t->requested_alignment_bytes = sizeof(int32_t);
+    t->effective_alignment_bytes = sizeof(int32_t);
+    t->alloc_end_bytes = bd.size_bytes;
+    t->rank = 1;
+    t->shape[0] = (gsx_index_t)count;
+    t->data_type = GSX_DATA_TYPE_I32;
+    t->storage_format = GSX_STORAGE_FORMAT_CHW;
+    return b200_ok();
+}
+
+/* the Gaussian set and the optimizer state gathered by one index tensor (adc.cu:398-421) */
+static gsx_error b200_adc_gather(const gsx_adc_request *r, gsx_tensor_t index)
+{
+    B200_TRY(gsx_gs_gather(r->gs, index));
+    if(b200_adc_optim_enabled(r)) {
+        B200_TRY(gsx_optim_rebind_param_groups_from_gs(r->optim, r->gs));
+        B200_TRY(gsx_optim_gather(r->optim, index));
+    }
+    return b200_ok();
+}
+
+typedef struct b200_adc_scratch {
+    uint8_t *flags;
+    int32_t *list;
+    uint32_t *words;
+    uint32_t *counts;
+} b200_adc_scratch;
+
+static void b200_adc_scratch_free(b200_adc_scratch *s)
+{
+    if(s->flags) cudaFree(s->flags);
+    if(s->list) cudaFree(s->list);
+    if(s->words) cudaFree(s->words);
+    if(s->counts) cudaFree(s->counts);
+    memset(s, 0, sizeof(*s));
+}
+
+static gsx_error b200_adc_scratch_alloc(b200_adc_scratch *s, gsx_size_t n)
+{
+    memset(s, 0, sizeof(*s));
+    cudaError_t e = cudaMalloc((void **)&s->flags, (size_t)n);
+    if(e == cudaSuccess) e = cudaMalloc((void **)&s->list, (size_t)n * sizeof(int32_t));
+    if(e == cudaSuccess) e = cudaMalloc((void **)&s->words, (size_t)gsx_b200_adc_scratch_words(n) * sizeof(uint32_t));
+    if(e == cudaSuccess) e = cudaMalloc((void **)&s->counts, 2 * sizeof(uint32_t));
+    if(e != cudaSuccess) b200_adc_scratch_free(s);
+    return b200_cuda_error(e, "adc scratch allocation failed");
+}
+
+/* growth (duplicate / split) then prune, gsx-cuda/adc.cu:707-946 */
+static gsx_error b200_adc_refine_inner(const gsx_adc_desc *d, b200_backend *be, const gsx_adc_request *r, gsx_adc_result *res,
+                                       b200_adc_scratch *sc, gsx_backend_buffer_t *ibuf)
+{
+    b200_adc_fields f;
+    struct gsx_tensor itensor;
+    gsx_size_t n0 = 0, n1 = 0, budget = 0, max_cap = b200_nonneg(d->max_num_gaussians);
+    uint32_t counts[2] = { 0, 0 };
+    B200_TRY(b200_adc_count(r->gs, &n0));
+    if(n0 == 0) return b200_ok();
+    B200_TRY(b200_adc_load(r->gs, n0, &f));
+    budget = max_cap > n0 ? max_cap - n0 : 0;
+    if(budget > 0) {
+        gsx_size_t grow = 0, split = 0;
+        B200_TRY(b200_adc_scratch_alloc(sc, n0));
+        B200_TRY(b200_lib_error(gsx_b200_adc_select_growth(n0, f.grad_acc, f.visible_counter, f.logscale, d->duplicate_grad_threshold,
+                                                           d->duplicate_scale_threshold, r->scene_scale, budget, sc->flags, sc->list,
+                                                           sc->words, sc->counts, be->stream),
+                                "gsx_b200_adc_select_growth failed"));
+        B200_TRY(b200_cuda_error(cudaMemcpyAsync(counts, sc->counts, sizeof(counts), cudaMemcpyDeviceToHost, be->stream), "D2H failed"));
+        B200_TRY(b200_sync(be));
+        grow = counts[0] < budget ? counts[0] : budget;
+        split = counts[1];
+        if(grow > 0) {
+            int32_t *ix = NULL;
+            B200_TRY(b200_adc_index_tensor(r->gs, n0 + grow, ibuf, &itensor));
+            ix = b200_tensor_i32(&itensor);
+            if(ix == NULL) return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gsx-b200 default adc requires device-backed gs fields");
+            B200_TRY(b200_lib_error(gsx_b200_iota_i32(ix, n0, be->stream), "gsx_b200_iota_i32 failed"));
+            B200_TRY(b200_cuda_error(cudaMemcpyAsync(ix + n0, sc->list, (size_t)grow * sizeof(int32_t), cudaMemcpyDeviceToDevice, be->stream),
+                                     "cudaMemcpyAsync failed"));
+            B200_TRY(b200_adc_gather(r, &itensor));
+            B200_TRY(gsx_backend_buffer_free(*ibuf));
+            *ibuf = NULL;
+            B200_TRY(b200_adc_count(r->gs, &n1));
+            if(n1 != n0 + grow) return gsx_make_error(GSX_ERROR_INVALID_STATE, "cuda default adc growth produced unexpected gaussian count");
+            if(b200_adc_optim_enabled(r)) B200_TRY(gsx_optim_resize(r->optim, n1));
+            B200_TRY(b200_adc_load(r->gs, n1, &f));
+            B200_TRY(b200_lib_error(gsx_b200_adc_apply_split(grow, sc->list, sc->flags, n0, d->seed, r->global_step, f.mean3d, f.logscale,
+                                                             f.opacity, f.rotation, be->stream),
+                                    "gsx_b200_adc_apply_split failed"));
+            res->duplicated_count += grow - split;
+            res->grown_count += split;
+            res->mutated = true;
+        }
+        B200_TRY(b200_sync(be));
+        b200_adc_scratch_free(sc);
+    }
+    B200_TRY(b200_adc_count(r->gs, &n1));
+    if(n1 == 0) return b200_ok();
+    B200_TRY(b200_adc_load(r->gs, n1, &f));
+    B200_TRY(b200_adc_scratch_alloc(sc, n1));
+    B200_TRY(b200_lib_error(gsx_b200_adc_select_keep(n1, f.opacity, f.logscale, f.rotation, f.max_screen_radius, n0,
+                                                     r->global_step > b200_nonneg(d->reset_every) ? 1 : 0,
+                                                     d->pruning_opacity_threshold, d->max_world_scale, d->max_screen_scale,
+                                                     r->scene_scale, sc->flags, sc->list, sc->words, sc->counts, be->stream),
+                            "gsx_b200_adc_select_keep failed"));
+    B200_TRY(b200_cuda_error(cudaMemcpyAsync(counts, sc->counts, sizeof(uint32_t), cudaMemcpyDeviceToHost, be->stream), "D2H failed"));
+    B200_TRY(b200_sync(be));
+    {
+        const gsx_size_t keep = counts[0] == 0 ? 1 : counts[0];
+        if(keep < n1) {
+            int32_t *ix = NULL;
+            B200_TRY(b200_adc_index_tensor(r->gs, keep, ibuf, &itensor));
+            ix = b200_tensor_i32(&itensor);
+            if(ix == NULL) return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "gsx-b200 default adc requires device-backed gs fields");
+            /* nothing kept: the reference keeps row 0 */
+            if(counts[0] == 0) B200_TRY(b200_cuda_error(cudaMemsetAsync(ix, 0, sizeof(int32_t), be->stream), "cudaMemsetAsync failed"));
+            else B200_TRY(b200_cuda_error(cudaMemcpyAsync(ix, sc->list, (size_t)keep * sizeof(int32_t), cudaMemcpyDeviceToDevice, be->stream),
+                                          "cudaMemcpyAsync failed"));
+            B200_TRY(b200_adc_gather(r, &itensor));
+            res->pruned_count += n1 - keep;
+            res->mutated = true;
+        }
+    }
+    return gsx_gs_zero_aux_tensors(r->gs, GSX_GS_AUX_GRAD_ACC | GSX_GS_AUX_VISIBLE_COUNTER | GSX_GS_AUX_MAX_SCREEN_RADIUS);
+}
+
+static gsx_error b200_adc_refine(const gsx_adc_desc *d, b200_backend *be, const gsx_adc_request *r, gsx_adc_result *res)
+{
+    b200_adc_scratch sc;
+    gsx_backend_buffer_t ibuf = NULL;
+    gsx_error e;
+    memset(&sc, 0, sizeof(sc));
+    e = b200_adc_refine_inner(d, be, r, res, &sc, &ibuf);
+    if(ibuf != NULL) (void)gsx_backend_buffer_free(ibuf);
+    cudaStreamSynchronize(be->stream);
+    b200_adc_scratch_free(&sc);
+    return e;
+}
+
+/* opacity clamp to logit(clamp value) and optimizer reset (gsx-cuda/adc.cu:279-331) */
+static gsx_error b200_adc_reset(const gsx_adc_desc *d, const gsx_adc_request *r)
+{
+    gsx_tensor_t opacity = NULL;
+    float lo = -FLT_MAX, hi, p = d->opacity_clamp_value;
+    if(!gsx_error_is_success(gsx_gs_get_field(r->gs, GSX_GS_FIELD_OPACITY, &opacity)))
+        return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "cuda default adc reset requires gs opacity access");
+    if(opacity->data_type != GSX_DATA_TYPE_F32) return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "cuda default adc reset supports only float32 opacity");
+    if(p > 1.0f) p = 1.0f;
+    if(p < 1e-6f) p = 1e-6f;
+    if(p <= 1e-6f) p = 1e-6f;
+    if(p >= 1.0f - 1e-6f) p = 1.0f - 1e-6f;
+    hi = logf(p / (1.0f - p));
+    B200_TRY(gsx_tensor_clamp_inplace(opacity, &lo, &hi));
+    if(b200_adc_optim_enabled(r)) B200_TRY(gsx_optim_reset(r->optim));
+    return b200_ok();
+}
+
+static gsx_error b200_adc_step(gsx_adc_t adc, const gsx_adc_request *request, gsx_adc_result *out)
+{
+    b200_backend *be = b200_backend_of(adc->backend);
+    gsx_size_t before = 0, after = 0;
+    if(request == NULL || out == NULL) return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "out_result must be non-null");
+    memset(out, 0, sizeof(*out));
+    if(!gsx_error_is_success(b200_adc_count(request->gs, &before)))
+        return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "cuda default adc requires gs info/query support");
+    out->gaussians_before = before;
+    out->gaussians_after = before;
+    B200_TRY(b200_cuda_error(cudaSetDevice(be->ordinal), "cudaSetDevice failed"));
+    if(b200_adc_refine_window(&adc->desc, request->global_step)) B200_TRY(b200_adc_refine(&adc->desc, be, request, out));
+    if(b200_adc_reset_window(&adc->desc, request->global_step)) {
+        B200_TRY(b200_adc_reset(&adc->desc, request));
+        out->reset_count = 1;
+        out->mutated = true;
+    }
+    if(!gsx_error_is_success(b200_adc_count(request->gs, &after)))
+        return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "cuda default adc requires gs info/query support");
+    out->gaussians_after = after;
+    if(after != before) out->mutated = true;
+    return b200_ok();
+}
+
+static gsx_error b200_adc_destroy(gsx_adc_t adc)
+{
+    if(adc == NULL) return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "adc must be non-null");
+    gsx_adc_base_deinit(adc);
+    free(adc);
+    return b200_ok();
+}
+
+static const gsx_adc_i b200_adc_iface = { b200_adc_destroy, b200_adc_step };
+
 static gsx_error b200_create_adc(gsx_backend_t backend, const gsx_adc_desc *desc, gsx_adc_t *out)
 {
-    (void)backend, (void)desc;
-    if(out) *out = NULL;
-    return B200_UNSUPPORTED("adaptive density control");
+    b200_adc *a = NULL;
+    gsx_error e;
+    if(out == NULL || desc == NULL) return gsx_make_error(GSX_ERROR_INVALID_ARGUMENT, "out_adc and desc must be non-null");
+    *out = NULL;
+    if(desc->algorithm != GSX_ADC_ALGORITHM_DEFAULT)
+        return gsx_make_error(GSX_ERROR_NOT_SUPPORTED, "cuda adc currently supports only GSX_ADC_ALGORITHM_DEFAULT");
+    a = (b200_adc *)calloc(1, sizeof(*a));
+    if(a == NULL) return gsx_make_error(GSX_ERROR_OUT_OF_MEMORY, "failed to allocate the adc");
+    e = gsx_adc_base_init(&a->base, &b200_adc_iface, backend, desc);
+    if(!gsx_error_is_success(e)) {
+        free(a);
+        return e;
+    }
+    *out = &a->base;
+    return b200_ok();
 }
 
 static gsx_error b200_create_async_dl(gsx_backend_t backend, const gsx_async_dl_desc *desc, gsx_async_dl_t *out)

@@ -43,8 +43,8 @@ enum {
 
 enum { GSX_B200_FORWARD_INFERENCE = 0, GSX_B200_FORWARD_TRAIN = 1 };
 
-/* element types of gsx_b200_hwc_to_chw_f32's source (the values of gsx_data_type, gsx-core.h:9-11) */
-enum { GSX_B200_DATA_F32 = 0, GSX_B200_DATA_U8 = 8 };
+/* element types (the values of gsx_data_type, gsx-core.h:8-14) */
+enum { GSX_B200_DATA_F32 = 0, GSX_B200_DATA_U8 = 8, GSX_B200_DATA_I32 = 12 };
 
 /* Pinhole camera: world->camera rotation (quaternion x, y, z, w) and translation, as
  * gsx_camera_pose (gsx-base.h:211-216) plus gsx_camera_intrinsics fx, fy, cx, cy, width, height. */
@@ -275,6 +275,47 @@ GSX_B200_API int gsx_b200_count_nonfinite_f32(const float *x, uint64_t n, uint32
  */
 GSX_B200_API int gsx_b200_hwc_to_chw_f32(const void *src, int src_type, int channels, uint64_t pixel_count, float *dst,
                                          void *stream);
+
+/*
+ * Structural operations of density control (device pointers, on `stream`).
+ * gsx_b200_gather_rows: dst row r = src row index[r] (rows of row_bytes bytes, out_rows rows, src has
+ * src_rows rows); an index outside [0, src_rows) sets *device_out_of_range to 1 (when non-NULL) and
+ * leaves that row of dst untouched.  Replaces gsx_cuda_gather_rows_kernel_launch
+ * (gsx-cuda/gsx-cuda-kernels.cu:642-675), behind gather_tensor and the optimizer's permute/gather.
+ * gsx_b200_clamp_inplace: x[i] = lo if x[i] < lo, hi if x[i] > hi (NaN kept) for f32, i32 or u8
+ * (gsx-cuda/buffer.c:1985-2060).  gsx_b200_iota_i32: dst[i] = i.
+ */
+GSX_B200_API int gsx_b200_gather_rows(const void *src, uint64_t src_rows, uint64_t row_bytes, const int32_t *index,
+                                      uint64_t out_rows, void *dst, uint32_t *device_out_of_range, void *stream);
+GSX_B200_API int gsx_b200_clamp_inplace(void *x, int data_type, uint64_t n, const void *min_value, const void *max_value,
+                                        void *stream);
+GSX_B200_API int gsx_b200_iota_i32(int32_t *dst, uint64_t n, void *stream);
+
+/*
+ * The refine pass of GSX's default density control (gsx-cuda/adc.cu:707-946), as device stages the
+ * host sequences around gsx_gs_gather / gsx_optim_gather.  scratch holds
+ * gsx_b200_adc_scratch_words(n) words.
+ * gsx_b200_adc_select_growth: modes[i] (0 none, 1 duplicate, 2 split; adc.cu:428-476) for n
+ * Gaussians and the ordered list of candidates (mode != 0) in candidates[]; device_counts[0] = the
+ * candidate count, device_counts[1] = the splits among the first `budget` candidates.
+ * gsx_b200_adc_apply_split: the split mutation (adc.cu:541-705) of grown rows count_before + g for
+ * the first grow_count candidates whose mode is split (modes indexed by source row).
+ * gsx_b200_adc_select_keep: the ordered list of rows the prune pass keeps (adc.cu:499-539) in keep[],
+ * its length in *device_count; flags[n] is scratch.
+ */
+GSX_B200_API uint64_t gsx_b200_adc_scratch_words(uint64_t n);
+GSX_B200_API int gsx_b200_adc_select_growth(uint64_t n, const float *grad_acc, const float *visible_counter,
+                                            const float *logscale, float grad_threshold, float scale_threshold,
+                                            float scene_scale, uint64_t budget, uint8_t *modes, int32_t *candidates,
+                                            uint32_t *scratch, uint32_t *device_counts, void *stream);
+GSX_B200_API int gsx_b200_adc_apply_split(uint64_t grow_count, const int32_t *sources, const uint8_t *modes,
+                                          uint64_t count_before, uint64_t seed, uint64_t global_step, float *mean3d,
+                                          float *logscale, float *opacity, const float *rotation, void *stream);
+GSX_B200_API int gsx_b200_adc_select_keep(uint64_t n, const float *opacity, const float *logscale, const float *rotation,
+                                          const float *max_screen_radius, uint64_t count_before_growth, int prune_large,
+                                          float opacity_threshold, float max_world_scale, float max_screen_scale,
+                                          float scene_scale, uint8_t *flags, int32_t *keep, uint32_t *scratch,
+                                          uint32_t *device_count, void *stream);
 
 #ifdef __cplusplus
 }

@@ -363,3 +363,160 @@ def pack_hwc_to_chw(src):
     if a.ndim == 2:
         a = a[:, :, None]
     return np.ascontiguousarray(np.transpose(a, (2, 0, 1)).astype(np.float32))
+
+
+ADC_FIELDS = ("mean3d", "logscale", "rotation", "opacity", "sh0")
+_ADC_COLS = (3, 3, 4, 1, 3)
+
+
+def ref_adc_run(kind: str, g: dict, aux: dict, grads: dict, fparams, iparams, cap: int = None):
+    """One density-control step of the reference GSX library (oracle/ref_driver.c refdrv_adc_run) on
+    backend `kind`: returns (result dict, fields after ADC, fields after the following Adam step,
+    statistics after ADC)."""
+    L = ref(kind)
+    n = int(g["mean3d"].shape[0])
+    cap = cap or 2 * n + 1
+    keep = [_f32(g[k]) for k in ADC_FIELDS] + [_f32(aux[k]) for k in ("grad_acc", "visible_counter", "max_screen_radius")]
+    gr = [_f32(grads[k]) for k in ADC_FIELDS]
+    fp = np.asarray(fparams, np.float32)
+    ip = np.asarray(iparams, np.int64)
+    res = np.zeros(7, np.int64)
+    after = [np.zeros(cap * c, np.float32) for c in _ADC_COLS]
+    final = [np.zeros(cap * c, np.float32) for c in _ADC_COLS]
+    aux_out = [np.zeros(cap, np.float32) for _ in range(3)]
+    arr = lambda xs: (F32P * len(xs))(*[_p(x) for x in xs])
+    L.refdrv_adc_run.argtypes = None
+    _ref_check(L, L.refdrv_adc_run(ctypes.c_int64(n), *[_p(x) for x in keep], arr(gr), _p(fp),
+                                   ip.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                   res.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), ctypes.c_int64(cap),
+                                   arr(after), arr(final), arr(aux_out)))
+    m = int(res[1])
+    r = dict(zip(("before", "after", "pruned", "duplicated", "grown", "reset", "mutated"), (int(v) for v in res)))
+    shape = lambda c: (m, c) if c > 1 else (m,)
+    fa = {k: after[i][:m * c].reshape(shape(c)) for i, (k, c) in enumerate(zip(ADC_FIELDS, _ADC_COLS))}
+    ff = {k: final[i][:m * c].reshape(shape(c)) for i, (k, c) in enumerate(zip(ADC_FIELDS, _ADC_COLS))}
+    fx = {k: aux_out[i][:m] for i, k in enumerate(("grad_acc", "visible_counter", "max_screen_radius"))}
+    return r, fa, ff, fx
+
+
+def _adc_variate(seed, step, grow_index, lane):
+    """The split offset variate of gsx-cuda/adc.cu:582-599: a hashed uniform (u32 arithmetic) mapped
+    through the logistic quantile, in float32."""
+    M = 0xFFFFFFFF
+    key = (int(seed) ^ ((int(step) * 0x9E3779B97F4A7C15) & 0xFFFFFFFFFFFFFFFF)) & M
+    x = (key ^ (int(grow_index) & M) ^ ((lane * 0x9E3779B9 + 0x85EBCA6B) & M)) & M
+    x ^= x >> 16
+    x = (x * 0x7FEB352D) & M
+    x ^= x >> 15
+    x = (x * 0x846CA68B) & M
+    x ^= x >> 16
+    u = (np.float32(x) + np.float32(1.0)) / np.float32(4294967297.0)
+    u = min(max(u, np.float32(1e-6)), np.float32(1.0) - np.float32(1e-6))
+    return np.float32(np.log(np.float32(u / (np.float32(1.0) - u))))
+
+
+def adc_step(g: dict, aux: dict, fparams, iparams, grads=None):
+    """Restatement of GSX's CUDA default density control step (gsx-cuda/adc.cu:990-1040 with the refine
+    pass :707-946 and the reset :292-331), float32 numpy.  g: mean3d/logscale/rotation/opacity/sh0;
+    aux: grad_acc/visible_counter/max_screen_radius.  Returns (result dict, new fields, new aux, the
+    row index each output row was gathered from (-1 for none: gathering composes), split rows)."""
+    f32 = np.float32
+    (op_thr, clamp_v, max_ws, max_ss, dup_thr, dup_scale, scene) = [f32(v) for v in fparams]
+    refine_every, start, end, max_n, reset_every, seed, step = (int(v) for v in iparams)
+    g = {k: np.array(v, np.float32, copy=True) for k, v in g.items()}
+    aux = {k: np.array(v, np.float32, copy=True) for k, v in aux.items()}
+    n0 = g["mean3d"].shape[0]
+    origin = np.arange(n0)
+    split_flag = np.zeros(n0, bool)
+    res = dict(before=n0, after=n0, pruned=0, duplicated=0, grown=0, reset=0, mutated=0)
+    nn = lambda v: max(v, 0)
+    refine = refine_every != 0 and step % refine_every == 0 and nn(start) <= step <= nn(end)
+    reset = reset_every != 0 and step % reset_every == 0 and nn(start) <= step < nn(end)
+
+    def gather(idx):
+        nonlocal origin, split_flag
+        for d in (g, aux):
+            for k in d:
+                d[k] = d[k][idx]
+        origin = origin[idx]
+        split_flag = split_flag[idx]
+
+    def max_scale(ls):
+        return np.exp(ls).max(axis=1)
+
+    if refine and n0 > 0:
+        budget = max(nn(max_n) - n0, 0)
+        if budget > 0:
+            counter = aux["visible_counter"] if "visible_counter" in aux else np.ones(n0, f32)
+            grad = aux["grad_acc"] / np.maximum(counter, f32(1.0))
+            grow_on = (counter > 0) & (grad > dup_thr)
+            split_on = grow_on & (max_scale(g["logscale"]) > f32(dup_scale * scene))
+            modes = np.where(split_on, 2, np.where(grow_on, 1, 0))
+            cand = np.nonzero(modes)[0]
+            grow = min(len(cand), budget)
+            if grow > 0:
+                cand = cand[:grow]
+                nsplit = int((modes[cand] == 2).sum())
+                gather(np.concatenate([np.arange(n0), cand]))
+                for gi, src in enumerate(cand):
+                    if modes[src] != 2:
+                        continue
+                    dst = n0 + gi
+                    s = np.exp(g["logscale"][src]).astype(f32)
+                    so = f32(1.0) / (f32(1.0) + np.exp(-g["opacity"][src]))
+                    r = [_adc_variate(seed, step, gi, l) for l in range(6)]
+                    q = g["rotation"][src].astype(f32)
+                    qn = np.sqrt(np.sum(q * q, dtype=f32))
+                    if qn > f32(1e-8):
+                        q = q * (f32(1.0) / qn)
+                    qx, qy, qz, qw = q
+                    R = np.array([[1 - 2 * (qy * qy + qz * qz), 2 * (qx * qy - qw * qz), 2 * (qx * qz + qw * qy)],
+                                  [2 * (qx * qy + qw * qz), 1 - 2 * (qx * qx + qz * qz), 2 * (qy * qz - qw * qx)],
+                                  [2 * (qx * qz - qw * qy), 2 * (qy * qz + qw * qx), 1 - 2 * (qx * qx + qy * qy)]], f32)
+                    t1 = np.array(r[:3], f32) * (s + f32(1e-5))
+                    t2 = np.array(r[3:], f32) * (s + f32(1e-5))
+                    so = min(max(so, f32(0.0)), f32(1.0) - f32(1e-6))
+                    sp = f32(1.0) - np.sqrt(f32(1.0) - so)
+                    sp = min(max(sp, f32(1e-6)), f32(1.0) - f32(1e-6))
+                    nl = np.log(s / f32(1.6)).astype(f32)
+                    nop = f32(np.log(f32(sp / (f32(1.0) - sp))))
+                    m = g["mean3d"][src].copy()
+                    g["mean3d"][dst] = m + R @ t1
+                    g["mean3d"][src] = m + R @ t2
+                    g["logscale"][dst] = nl
+                    g["logscale"][src] = nl
+                    g["opacity"][dst] = nop
+                    g["opacity"][src] = nop
+                    split_flag[src] = split_flag[dst] = True
+                res["duplicated"] += grow - nsplit
+                res["grown"] += nsplit
+                res["mutated"] = 1
+        n1 = g["mean3d"].shape[0]
+        op = f32(1.0) / (f32(1.0) + np.exp(-g["opacity"]))
+        keep = (op > op_thr) & (np.abs(g["rotation"]).sum(1, dtype=f32) > np.finfo(np.float32).eps)
+        if step > nn(reset_every):
+            if max_ws > 0:
+                keep &= max_scale(g["logscale"]) < f32(max_ws * scene)
+            if max_ss > 0 and "max_screen_radius" in aux:
+                keep &= ~((np.arange(n1) < n0) & ~(aux["max_screen_radius"] < max_ss))
+        kept = np.nonzero(keep)[0]
+        if len(kept) == 0:
+            kept = np.array([0])
+        if len(kept) < n1:
+            gather(kept)
+            res["pruned"] += n1 - len(kept)
+            res["mutated"] = 1
+        for k in ("grad_acc", "visible_counter", "max_screen_radius"):
+            if k in aux:
+                aux[k][:] = 0.0
+    if reset:
+        p = min(max(f32(clamp_v), f32(1e-6)), f32(1.0))
+        p = min(max(p, f32(1e-6)), f32(1.0) - f32(1e-6))
+        hi = f32(np.log(f32(p / (f32(1.0) - p))))
+        g["opacity"] = np.where(g["opacity"] > hi, hi, g["opacity"]).astype(f32)
+        res["reset"] = 1
+        res["mutated"] = 1
+    res["after"] = g["mean3d"].shape[0]
+    if res["after"] != res["before"]:
+        res["mutated"] = 1
+    return res, g, aux, origin, np.nonzero(split_flag)[0]

@@ -436,3 +436,194 @@ int refdrv_adam(int64_t n, float *param, const float *grad, int steps, float lr,
     gsx_arena_free(arena);
     return 0;
 }
+
+/* a one-sample 4x4 u8 dataset: the ADC request needs a dataloader and a renderer handle */
+static const uint8_t refdrv_tiny_rgb[4 * 4 * 3] = { 0 };
+static gsx_error refdrv_ok(void)
+{
+    gsx_error e;
+    e.code = GSX_ERROR_SUCCESS;
+    e.message = NULL;
+    return e;
+}
+static gsx_error refdrv_tiny_length(void *o, gsx_size_t *n)
+{
+    (void)o;
+    *n = 1;
+    return refdrv_ok();
+}
+static gsx_error refdrv_tiny_sample(void *o, gsx_size_t i, gsx_dataset_cpu_sample *s)
+{
+    (void)o, (void)i;
+    memset(s, 0, sizeof(*s));
+    s->intrinsics.fx = s->intrinsics.fy = 4.0f;
+    s->intrinsics.cx = s->intrinsics.cy = 2.0f;
+    s->intrinsics.width = s->intrinsics.height = 4;
+    s->pose.rot.w = 1.0f;
+    s->rgb_data = refdrv_tiny_rgb;
+    return refdrv_ok();
+}
+static void refdrv_tiny_release(void *o, gsx_dataset_cpu_sample *s) { (void)o, (void)s; }
+
+/* ---------------------------------------------------------------- density control
+ * One GSX density-control step through the public API, as the runtime drives it
+ * (gsx-runtime.c ADC stage): a gsx_gs holding `n` Gaussians (mean3d, logscale, rotation, opacity,
+ * sh0 and the grad_acc / visible_counter / max_screen_radius statistics), an Adam optimizer bound to
+ * its fields and stepped once with the given gradients (so the moments are non-trivial), then
+ * gsx_adc_step with the default algorithm, then one more Adam step with every gradient = 1 (so the
+ * gathered moments show in the parameters).
+ *   fparams: pruning_opacity_threshold, opacity_clamp_value, max_world_scale, max_screen_scale,
+ *            duplicate_grad_threshold, duplicate_scale_threshold, scene_scale
+ *   iparams: refine_every, start_refine, end_refine, max_num_gaussians, reset_every, seed, global_step
+ *   grads:   gradients of mean3d, logscale, rotation, opacity, sh0 for the first Adam step
+ *   result:  gaussians_before, gaussians_after, pruned, duplicated, grown, reset_count, mutated
+ *   out_after_adc / out_final: the five fields (same layout as the inputs, `cap` Gaussians of room),
+ *   after the ADC step and after the final Adam step; out_aux: the three statistics after ADC. */
+int refdrv_adc_run(int64_t n, const float *mean3d, const float *logscale, const float *rotation, const float *opacity,
+                   const float *sh0, const float *grad_acc, const float *visible_counter, const float *max_screen_radius,
+                   const float *const *grads, const float *fparams, const int64_t *iparams, int64_t *result, int64_t cap,
+                   float *const *out_after_adc, float *const *out_final, float *const *out_aux)
+{
+    static const int cols[5] = { 3, 3, 4, 1, 3 };
+    const float *in[5] = { mean3d, logscale, rotation, opacity, sh0 };
+    const float *aux_in[3] = { grad_acc, visible_counter, max_screen_radius };
+    const gsx_gs_field aux_field[3] = { GSX_GS_FIELD_GRAD_ACC, GSX_GS_FIELD_VISIBLE_COUNTER, GSX_GS_FIELD_MAX_SCREEN_RADIUS };
+    gsx_gs_t gs = NULL;
+    gsx_gs_desc gd;
+    gsx_optim_t optim = NULL;
+    gsx_optim_param_group_desc groups[5];
+    gsx_optim_desc od;
+    gsx_optim_step_request oq;
+    gsx_adc_t adc = NULL;
+    gsx_adc_desc ad;
+    gsx_adc_request rq;
+    gsx_adc_result res;
+    gsx_gs_info info;
+    float *ones = NULL;
+    gsx_dataset_t ds = NULL;
+    gsx_dataset_desc dsd;
+    gsx_dataloader_t dl = NULL;
+    gsx_dataloader_desc dld;
+    gsx_renderer_t ren = NULL;
+    gsx_renderer_desc rd;
+    memset(&dsd, 0, sizeof(dsd));
+    dsd.image_data_type = GSX_DATA_TYPE_U8;
+    dsd.width = dsd.height = 4;
+    dsd.has_rgb = true;
+    dsd.get_length = refdrv_tiny_length;
+    dsd.get_sample = refdrv_tiny_sample;
+    dsd.release_sample = refdrv_tiny_release;
+    REF_CHECK(gsx_dataset_init(&ds, &dsd));
+    memset(&dld, 0, sizeof(dld));
+    dld.image_data_type = GSX_DATA_TYPE_F32;
+    REF_CHECK(gsx_dataloader_init(&dl, refdrv_backend, ds, &dld));
+    memset(&rd, 0, sizeof(rd));
+    rd.width = rd.height = 4;
+    rd.output_data_type = GSX_DATA_TYPE_F32;
+    REF_CHECK(gsx_renderer_init(&ren, refdrv_backend, &rd));
+    memset(&gd, 0, sizeof(gd));
+    gd.buffer_type = refdrv_device_type;
+    gd.count = (gsx_size_t)n;
+    gd.aux_flags = GSX_GS_AUX_GRAD_ACC | GSX_GS_AUX_VISIBLE_COUNTER | GSX_GS_AUX_MAX_SCREEN_RADIUS;
+    REF_CHECK(gsx_gs_init(&gs, &gd));
+    for(int f = 0; f < 5; ++f) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &t));
+        REF_CHECK(gsx_tensor_upload(t, in[f], (gsx_size_t)n * cols[f] * sizeof(float)));
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)(GSX_GS_FIELD_GRAD_MEAN3D + f), &t));
+        REF_CHECK(gsx_tensor_upload(t, grads[f], (gsx_size_t)n * cols[f] * sizeof(float)));
+    }
+    for(int k = 0; k < 3; ++k) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, aux_field[k], &t));
+        REF_CHECK(gsx_tensor_upload(t, aux_in[k], (gsx_size_t)n * sizeof(float)));
+    }
+    memset(groups, 0, sizeof(groups));
+    for(int f = 0; f < 5; ++f) {
+        groups[f].role = (gsx_optim_param_role)f;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &groups[f].parameter));
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)(GSX_GS_FIELD_GRAD_MEAN3D + f), &groups[f].gradient));
+        groups[f].learning_rate = f == 0 ? 1e-3f : 1e-2f;
+        groups[f].beta1 = 0.9f;
+        groups[f].beta2 = 0.999f;
+        groups[f].epsilon = 1e-8f;
+    }
+    memset(&od, 0, sizeof(od));
+    od.algorithm = GSX_OPTIM_ALGORITHM_ADAM;
+    od.param_groups = groups;
+    od.param_group_count = 5;
+    REF_CHECK(gsx_optim_init(&optim, refdrv_backend, &od));
+    memset(&oq, 0, sizeof(oq));
+    oq.force_all = true;
+    REF_CHECK(gsx_optim_step(optim, &oq));
+
+    memset(&ad, 0, sizeof(ad));
+    ad.algorithm = GSX_ADC_ALGORITHM_DEFAULT;
+    ad.pruning_opacity_threshold = fparams[0];
+    ad.opacity_clamp_value = fparams[1];
+    ad.max_world_scale = fparams[2];
+    ad.max_screen_scale = fparams[3];
+    ad.duplicate_grad_threshold = fparams[4];
+    ad.duplicate_scale_threshold = fparams[5];
+    ad.refine_every = (gsx_index_t)iparams[0];
+    ad.start_refine = (gsx_index_t)iparams[1];
+    ad.end_refine = (gsx_index_t)iparams[2];
+    ad.max_num_gaussians = (gsx_index_t)iparams[3];
+    ad.reset_every = (gsx_index_t)iparams[4];
+    ad.seed = (gsx_size_t)iparams[5];
+    REF_CHECK(gsx_adc_init(&adc, refdrv_backend, &ad));
+    memset(&rq, 0, sizeof(rq));
+    rq.gs = gs;
+    rq.optim = optim;
+    rq.dataloader = dl;
+    rq.renderer = ren;
+    rq.global_step = (gsx_size_t)iparams[6];
+    rq.scene_scale = fparams[6];
+    memset(&res, 0, sizeof(res));
+    REF_CHECK(gsx_adc_step(adc, &rq, &res));
+    result[0] = (int64_t)res.gaussians_before;
+    result[1] = (int64_t)res.gaussians_after;
+    result[2] = (int64_t)res.pruned_count;
+    result[3] = (int64_t)res.duplicated_count;
+    result[4] = (int64_t)res.grown_count;
+    result[5] = (int64_t)res.reset_count;
+    result[6] = res.mutated ? 1 : 0;
+    memset(&info, 0, sizeof(info));
+    REF_CHECK(gsx_gs_get_info(gs, &info));
+    if((int64_t)info.count > cap) return 254;
+    for(int f = 0; f < 5; ++f) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &t));
+        REF_CHECK(gsx_tensor_download(t, out_after_adc[f], (gsx_size_t)info.count * cols[f] * sizeof(float)));
+    }
+    for(int k = 0; k < 3; ++k) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, aux_field[k], &t));
+        REF_CHECK(gsx_tensor_download(t, out_aux[k], (gsx_size_t)info.count * sizeof(float)));
+    }
+    /* one more Adam step with unit gradients: the moments the ADC step carried show in the parameters */
+    ones = (float *)malloc((size_t)(info.count ? info.count : 1) * 4 * sizeof(float));
+    if(ones == NULL) return 253;
+    for(gsx_size_t i = 0; i < info.count * 4; ++i) ones[i] = 1.0f;
+    for(int f = 0; f < 5; ++f) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)(GSX_GS_FIELD_GRAD_MEAN3D + f), &t));
+        REF_CHECK(gsx_tensor_upload(t, ones, (gsx_size_t)info.count * cols[f] * sizeof(float)));
+    }
+    free(ones);
+    REF_CHECK(gsx_optim_rebind_param_groups_from_gs(optim, gs));
+    REF_CHECK(gsx_optim_step(optim, &oq));
+    for(int f = 0; f < 5; ++f) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &t));
+        REF_CHECK(gsx_tensor_download(t, out_final[f], (gsx_size_t)info.count * cols[f] * sizeof(float)));
+    }
+    REF_CHECK(gsx_backend_major_stream_sync(refdrv_backend));
+    REF_CHECK(gsx_adc_free(adc));
+    REF_CHECK(gsx_optim_free(optim));
+    REF_CHECK(gsx_gs_free(gs));
+    REF_CHECK(gsx_renderer_free(ren));
+    REF_CHECK(gsx_dataloader_free(dl));
+    REF_CHECK(gsx_dataset_free(ds));
+    return 0;
+}
