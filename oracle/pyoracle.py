@@ -520,3 +520,29 @@ def adc_step(g: dict, aux: dict, fparams, iparams, grads=None):
     if res["after"] != res["before"]:
         res["mutated"] = 1
     return res, g, aux, origin, np.nonzero(split_flag)[0]
+
+
+def ref_session_fit(kind: str, g: dict, target_chw, cam: "Camera", fparams, iparams, steps: int, cap: int = None):
+    """GSX's runtime session (gsx_session_step with L1 0.8 + SSIM 0.2, Adam, default ADC) on backend
+    `kind` over a one-image dataset (oracle/ref_driver.c refdrv_session_fit).  Returns (mean loss
+    per step, Gaussian count per step, final fields)."""
+    L = ref(kind)
+    n = int(g["mean3d"].shape[0])
+    cap = cap or 8 * n
+    keep = [_f32(g[k]) for k in ADC_FIELDS]
+    hwc = np.ascontiguousarray(np.transpose(_f32(target_chw), (1, 2, 0)))
+    c = np.array([cam.fx, cam.fy, cam.cx, cam.cy, *cam.q, *cam.t], np.float32)
+    fp = np.asarray(fparams, np.float32)
+    ip = np.asarray(iparams, np.int64)
+    loss = np.zeros(steps, np.float32)
+    count = np.zeros(steps, np.int64)
+    out = [np.zeros(cap * k, np.float32) for k in _ADC_COLS]
+    L.refdrv_session_fit.argtypes = None
+    _ref_check(L, L.refdrv_session_fit(ctypes.c_int64(n), *[_p(x) for x in keep], _p(hwc), ctypes.c_int(cam.width),
+                                       ctypes.c_int(cam.height), _p(c), _p(fp),
+                                       ip.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), ctypes.c_int64(steps), _p(loss),
+                                       count.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), ctypes.c_int64(cap),
+                                       (F32P * 5)(*[_p(x) for x in out])))
+    m = int(count[-1])
+    fields = {k: out[i][:m * cc].reshape((m, cc) if cc > 1 else (m,)) for i, (k, cc) in enumerate(zip(ADC_FIELDS, _ADC_COLS))}
+    return loss, count, fields

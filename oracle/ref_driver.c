@@ -627,3 +627,216 @@ int refdrv_adc_run(int64_t n, const float *mean3d, const float *logscale, const 
     REF_CHECK(gsx_dataset_free(ds));
     return 0;
 }
+
+/* ---------------------------------------------------------------- runtime session
+ * GSX's own training loop (gsx_session_step: dataloader -> render TRAIN -> L1 + SSIM -> backward ->
+ * Adam -> ADC) over a one-image dataset, `steps` steps.  Inputs as refdrv_adc_run plus the target
+ * image (f32 HWC [H,W,3]) and its camera.  Per step: the summed loss map and the Gaussian count;
+ * at the end the five fields (`cap` Gaussians of room). */
+typedef struct refdrv_fit_data {
+    const float *rgb;
+    int width, height;
+    float fx, fy, cx, cy, q[4], t[3];
+} refdrv_fit_data;
+
+static gsx_error refdrv_fit_sample(void *o, gsx_size_t i, gsx_dataset_cpu_sample *s)
+{
+    const refdrv_fit_data *d = (const refdrv_fit_data *)o;
+    (void)i;
+    memset(s, 0, sizeof(*s));
+    s->intrinsics.fx = d->fx;
+    s->intrinsics.fy = d->fy;
+    s->intrinsics.cx = d->cx;
+    s->intrinsics.cy = d->cy;
+    s->intrinsics.width = d->width;
+    s->intrinsics.height = d->height;
+    s->pose.rot.x = d->q[0];
+    s->pose.rot.y = d->q[1];
+    s->pose.rot.z = d->q[2];
+    s->pose.rot.w = d->q[3];
+    s->pose.transl.x = d->t[0];
+    s->pose.transl.y = d->t[1];
+    s->pose.transl.z = d->t[2];
+    s->rgb_data = d->rgb;
+    return refdrv_ok();
+}
+
+int refdrv_session_fit(int64_t n, const float *mean3d, const float *logscale, const float *rotation, const float *opacity,
+                       const float *sh0, const float *target_hwc, int width, int height, const float *cam /* fx fy cx cy q4 t3 */,
+                       const float *fparams, const int64_t *iparams, int64_t steps, float *loss_out, int64_t *count_out,
+                       int64_t cap, float *const *out_fields)
+{
+    static const int cols[5] = { 3, 3, 4, 1, 3 };
+    const float *in[5] = { mean3d, logscale, rotation, opacity, sh0 };
+    refdrv_fit_data data;
+    gsx_dataset_t ds = NULL;
+    gsx_dataset_desc dsd;
+    gsx_dataloader_t dl = NULL;
+    gsx_dataloader_desc dld;
+    gsx_renderer_t ren = NULL;
+    gsx_renderer_desc rd;
+    gsx_gs_t gs = NULL;
+    gsx_gs_desc gd;
+    gsx_optim_t optim = NULL;
+    gsx_optim_param_group_desc groups[5];
+    gsx_optim_desc od;
+    gsx_adc_t adc = NULL;
+    gsx_adc_desc ad;
+    gsx_gs_aux_flags aux_flags = 0;
+    gsx_loss_t l1 = NULL, ssim = NULL;
+    gsx_loss_context_t l1c = NULL, ssimc = NULL;
+    gsx_loss_desc ld;
+    gsx_loss_item items[2];
+    gsx_session_t session = NULL;
+    gsx_session_desc sd;
+    float *host = (float *)malloc((size_t)width * height * 3 * sizeof(float));
+    if(host == NULL) return 253;
+    data.rgb = target_hwc;
+    data.width = width;
+    data.height = height;
+    data.fx = cam[0];
+    data.fy = cam[1];
+    data.cx = cam[2];
+    data.cy = cam[3];
+    memcpy(data.q, cam + 4, sizeof(data.q));
+    memcpy(data.t, cam + 8, sizeof(data.t));
+    memset(&dsd, 0, sizeof(dsd));
+    dsd.object = &data;
+    dsd.image_data_type = GSX_DATA_TYPE_F32;
+    dsd.width = width;
+    dsd.height = height;
+    dsd.has_rgb = true;
+    dsd.get_length = refdrv_tiny_length;
+    dsd.get_sample = refdrv_fit_sample;
+    dsd.release_sample = refdrv_tiny_release;
+    REF_CHECK(gsx_dataset_init(&ds, &dsd));
+    memset(&dld, 0, sizeof(dld));
+    dld.image_data_type = GSX_DATA_TYPE_F32;
+    REF_CHECK(gsx_dataloader_init(&dl, refdrv_backend, ds, &dld));
+    memset(&rd, 0, sizeof(rd));
+    rd.width = width;
+    rd.height = height;
+    rd.output_data_type = GSX_DATA_TYPE_F32;
+    REF_CHECK(gsx_renderer_init(&ren, refdrv_backend, &rd));
+
+    memset(&ad, 0, sizeof(ad));
+    ad.algorithm = GSX_ADC_ALGORITHM_DEFAULT;
+    ad.pruning_opacity_threshold = fparams[0];
+    ad.opacity_clamp_value = fparams[1];
+    ad.max_world_scale = fparams[2];
+    ad.max_screen_scale = fparams[3];
+    ad.duplicate_grad_threshold = fparams[4];
+    ad.duplicate_scale_threshold = fparams[5];
+    ad.refine_every = (gsx_index_t)iparams[0];
+    ad.start_refine = (gsx_index_t)iparams[1];
+    ad.end_refine = (gsx_index_t)iparams[2];
+    ad.max_num_gaussians = (gsx_index_t)iparams[3];
+    ad.reset_every = (gsx_index_t)iparams[4];
+    ad.seed = (gsx_size_t)iparams[5];
+    REF_CHECK(gsx_adc_init(&adc, refdrv_backend, &ad));
+    REF_CHECK(gsx_adc_get_gs_aux_fields(adc, &aux_flags));
+
+    memset(&gd, 0, sizeof(gd));
+    gd.buffer_type = refdrv_device_type;
+    gd.count = (gsx_size_t)n;
+    gd.aux_flags = aux_flags;
+    REF_CHECK(gsx_gs_init(&gs, &gd));
+    for(int f = 0; f < 5; ++f) {
+        gsx_tensor_t t = NULL;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &t));
+        REF_CHECK(gsx_tensor_upload(t, in[f], (gsx_size_t)n * cols[f] * sizeof(float)));
+    }
+    REF_CHECK(gsx_gs_zero_aux_tensors(gs, aux_flags));
+    memset(groups, 0, sizeof(groups));
+    for(int f = 0; f < 5; ++f) {
+        groups[f].role = (gsx_optim_param_role)f;
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &groups[f].parameter));
+        REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)(GSX_GS_FIELD_GRAD_MEAN3D + f), &groups[f].gradient));
+        groups[f].learning_rate = f == 0 ? 1.6e-4f : (f == 3 ? 5e-2f : (f == 4 ? 2.5e-3f : (f == 1 ? 5e-3f : 1e-3f)));
+        groups[f].beta1 = 0.9f;
+        groups[f].beta2 = 0.999f;
+        groups[f].epsilon = 1e-15f;
+    }
+    memset(&od, 0, sizeof(od));
+    od.algorithm = GSX_OPTIM_ALGORITHM_ADAM;
+    od.param_groups = groups;
+    od.param_group_count = 5;
+    REF_CHECK(gsx_optim_init(&optim, refdrv_backend, &od));
+
+    memset(&ld, 0, sizeof(ld));
+    ld.algorithm = GSX_LOSS_ALGORITHM_L1;
+    ld.grad_normalization = GSX_LOSS_GRAD_NORMALIZATION_TYPE_MEAN;
+    REF_CHECK(gsx_loss_init(&l1, refdrv_backend, &ld));
+    ld.algorithm = GSX_LOSS_ALGORITHM_SSIM;
+    REF_CHECK(gsx_loss_init(&ssim, refdrv_backend, &ld));
+    REF_CHECK(gsx_loss_context_init(&l1c, l1));
+    REF_CHECK(gsx_loss_context_init(&ssimc, ssim));
+    items[0].loss = l1;
+    items[0].context = l1c;
+    items[0].scale = 0.8f;
+    items[1].loss = ssim;
+    items[1].context = ssimc;
+    items[1].scale = 0.2f;
+
+    memset(&sd, 0, sizeof(sd));
+    sd.backend = refdrv_backend;
+    sd.gs = gs;
+    sd.optim = optim;
+    sd.renderer = ren;
+    sd.train_dataloader = dl;
+    sd.adc = adc;
+    sd.loss_count = 2;
+    sd.loss_items = items;
+    sd.render.near_plane = 0.01f;
+    sd.render.far_plane = 100.0f;
+    sd.render.precision = GSX_RENDER_PRECISION_FLOAT32;
+    sd.render.sh_degree_mode = GSX_SESSION_SH_DEGREE_MODE_EXPLICIT;
+    sd.render.sh_degree = 0;
+    sd.optim_step.force_all = true;
+    sd.adc_step.enabled = true;
+    sd.adc_step.scene_scale = fparams[6];
+    sd.workspace.buffer_type_class = GSX_BACKEND_BUFFER_TYPE_DEVICE;
+    sd.workspace.auto_plan = true;
+    sd.reporting.retain_loss_map = true;
+    REF_CHECK(gsx_session_init(&session, &sd));
+    for(int64_t k = 0; k < steps; ++k) {
+        gsx_session_outputs outs;
+        gsx_gs_info info;
+        double sum = 0.0;
+        REF_CHECK(gsx_session_step(session));
+        memset(&outs, 0, sizeof(outs));
+        REF_CHECK(gsx_session_get_last_outputs(session, &outs));
+        if(outs.loss_map == NULL) return 252;
+        REF_CHECK(gsx_tensor_download(outs.loss_map, host, (gsx_size_t)width * height * 3 * sizeof(float)));
+        for(int64_t i = 0; i < (int64_t)width * height * 3; ++i) sum += host[i];
+        loss_out[k] = (float)(sum / ((double)width * height * 3));
+        memset(&info, 0, sizeof(info));
+        REF_CHECK(gsx_gs_get_info(gs, &info));
+        count_out[k] = (int64_t)info.count;
+    }
+    {
+        gsx_gs_info info;
+        memset(&info, 0, sizeof(info));
+        REF_CHECK(gsx_gs_get_info(gs, &info));
+        if((int64_t)info.count > cap) return 254;
+        for(int f = 0; f < 5; ++f) {
+            gsx_tensor_t t = NULL;
+            REF_CHECK(gsx_gs_get_field(gs, (gsx_gs_field)f, &t));
+            REF_CHECK(gsx_tensor_download(t, out_fields[f], (gsx_size_t)info.count * cols[f] * sizeof(float)));
+        }
+    }
+    free(host);
+    REF_CHECK(gsx_backend_major_stream_sync(refdrv_backend));
+    REF_CHECK(gsx_session_free(session));
+    REF_CHECK(gsx_loss_context_free(l1c));
+    REF_CHECK(gsx_loss_context_free(ssimc));
+    REF_CHECK(gsx_loss_free(l1));
+    REF_CHECK(gsx_loss_free(ssim));
+    REF_CHECK(gsx_optim_free(optim));
+    REF_CHECK(gsx_adc_free(adc));
+    REF_CHECK(gsx_gs_free(gs));
+    REF_CHECK(gsx_renderer_free(ren));
+    REF_CHECK(gsx_dataloader_free(dl));
+    REF_CHECK(gsx_dataset_free(ds));
+    return 0;
+}
