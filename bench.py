@@ -267,6 +267,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
+                    help="multi-GPU gradient exchange: fused NVLink reduce+Adam+gather kernel, or NCCL all-reduce + Adam")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -300,7 +302,7 @@ def main():
     del teacher
     model = GaussianModel(scene, dev)
     W, H = cams[0].width, cams[0].height
-    trainer = Trainer(model, W, H, group=group, device=dev)
+    trainer = Trainer(model, W, H, group=group, device=dev, exchange=args.exchange)
 
     def view(step):
         return (rank + step * world) % len(cams)
@@ -317,6 +319,8 @@ def main():
     ae = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     trainer.ctx.set_profiling(True)
     trainer.ctx.read_profile()
+    if trainer.sharded is not None:
+        trainer.sharded.kernel_events = []
     launches0 = trainer.ctx.launch_count()
     if world > 1:
         dist.barrier()
@@ -333,6 +337,18 @@ def main():
     timed_launches = trainer.ctx.launch_count() - launches0 + 2 * args.steps
     prof = trainer.ctx.read_profile()
     ms = e0.elapsed_time(e1)
+    exchange = None
+    if trainer.sharded is not None:
+        kms = sum(a.elapsed_time(b) for a, b in trainer.sharded.kernel_events) / len(trainer.sharded.kernel_events)
+        trainer.sharded.kernel_events = None
+        kt = torch.tensor([kms], device=dev)
+        dist.all_reduce(kt, op=dist.ReduceOp.MAX)
+        nb = trainer.sharded.nvlink_bytes()
+        exchange = {"kernel": "gsx_b200_dp_reduce_adam_gather", "avg_ms_max_over_ranks": float(kt.item()),
+                    "nvlink_bytes_per_rank": nb, "achieved_gbs_per_rank": nb / (float(kt.item()) / 1000.0) / 1e9,
+                    "peer_copy_gbs_reference": 770.0,
+                    "note": "bytes = the shard's gradients read from the other ranks + the updated shard written "
+                            "to them; the NVLink reference is the measured 770 GB/s per direction peer copy"}
     loss_ms = sum(a.elapsed_time(b) for a, b in le) / args.steps
     adam_ms = sum(a.elapsed_time(b) for a, b in ae) / args.steps
     t = torch.tensor([ms], device=dev)
@@ -366,6 +382,7 @@ def main():
     e2e_value = world * args.steps / (float(t2.item()) / 1000.0)
     h2d = dev_target.numel() * 4
     trainer.ctx.check()
+    trainer.close()
 
     fwd = forward_inference(args, dev, rank, world, local)
     big = large_frame(args, dev, rank, world, local)
@@ -424,7 +441,10 @@ def main():
             "config": {"workload": "config 3 training step: 3M Gaussians (2M volume + 1M z-slab), 1245x825, "
                                    "one view per GPU per step, L1(0.8)+SSIM(0.2), per-role Adam",
                        "gaussians": n, "width": W, "height": H, "views_per_step": world,
-                       "parallelism": f"dp{world} (views), NCCL all-reduce of 14 f32/Gaussian",
+                       "parallelism": (f"dp{world} (views), " + (
+                           "fused NVLink gradient average + sharded Adam + parameter all-gather (one kernel per rank)"
+                           if args.exchange == "fused" else "NCCL all-reduce AVG of 14 f32/Gaussian + Adam on every rank")
+                           if world > 1 else "dp1 (views)"),
                        "l2": "inputs larger than L2 (params+grads+moments = 672 MB)",
                        "visible": V, "instances": I, "buckets": B},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
@@ -436,6 +456,7 @@ def main():
             "forward": fwd,
             "large_frame": big,
             "input_conversion": conv,
+            "exchange": exchange,
             "cpu_baseline": cpu_baseline,
             "clocks": clocks.summary(),
         }

@@ -1,0 +1,160 @@
+"""Data-parallel training over NVLink with the fused gradient exchange + sharded Adam.
+
+One process per GPU.  The flat parameter and gradient buffers of every rank are mapped into every
+other rank's process (CUDA IPC over the NVSwitch fabric); each rank owns one contiguous shard of the
+flat parameter space and runs gsx_b200_dp_reduce_adam_gather on it: peer loads of the shard's
+gradients from all ranks, the average, Adam with shard-local moments, peer stores of the updated
+shard into all ranks' parameters.  Two collectives order it on the stream: one before (every rank's
+backward has finished writing its gradients) and one after (every rank's shard has landed in every
+parameter buffer before anyone renders again).
+
+The same arithmetic as an average all-reduce (sum in rank order, times 1/world) followed by Adam on
+every rank, so the replicas stay identical; the moments are sharded (1/world of them per rank).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+from ._capi import GsxError, INVALID_ARGUMENT, check, lib
+
+ALIGN = 4  # elements: shard and segment bounds stay 16-byte aligned
+
+
+class _CudaArray:
+    """A raw device pointer presented to torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, numel: int):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+def shard_bounds(numel: int, world: int, rank: int):
+    """[begin, end) of rank's shard of `numel` flat elements: contiguous, multiples of 4 elements,
+    sizes as even as the alignment allows (earlier ranks take the remainder)."""
+    if world < 1 or not 0 <= rank < world or numel % ALIGN:
+        raise GsxError(INVALID_ARGUMENT, "shard_bounds: numel a multiple of 4, 0 <= rank < world")
+    units = numel // ALIGN
+    base, extra = divmod(units, world)
+    b = rank * base + min(rank, extra)
+    e = b + base + (1 if rank < extra else 0)
+    return b * ALIGN, e * ALIGN
+
+
+def shard_segments(field_ranges: dict, begin: int, end: int):
+    """The runs of one field inside [begin, end): [(field, run_begin, run_end)] in flat order."""
+    out = []
+    for f, (a, b) in field_ranges.items():
+        lo, hi = max(a, begin), min(b, end)
+        if lo < hi:
+            out.append((f, lo, hi))
+    return sorted(out, key=lambda s: s[1])
+
+
+class PeerBuffers:
+    """One flat f32 device buffer of `numel` elements per rank, every rank's buffer mapped into this
+    process.  `local` is this rank's buffer as a torch tensor; `ptrs[r]` is rank r's buffer here."""
+
+    def __init__(self, numel: int, group, device):
+        import torch
+        import torch.distributed as dist
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        raw = ctypes.c_void_p()
+        check(lib().gsx_b200_device_alloc(numel * 4, ctypes.byref(raw)))
+        self._own = raw.value
+        self.local = torch.as_tensor(_CudaArray(self._own, numel), device=device)
+        self.local.zero_()
+        h = (ctypes.c_ubyte * 64)()
+        check(lib().gsx_b200_ipc_handle(ctypes.c_void_p(self._own), h))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(h), group=group)
+        self.ptrs, self._opened = [], []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            check(lib().gsx_b200_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(hb), ctypes.byref(p)))
+            self.ptrs.append(p.value)
+            self._opened.append(p.value)
+
+    def close_peers(self):
+        """Unmap the other ranks' buffers (call on every rank before any rank frees its own)."""
+        for p in self._opened:
+            lib().gsx_b200_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+
+    def free(self):
+        if self._own:
+            self.local = None
+            lib().gsx_b200_device_free(ctypes.c_void_p(self._own))
+            self._own = None
+
+
+class Segment(ctypes.Structure):
+    _fields_ = [("begin", ctypes.c_uint64), ("end", ctypes.c_uint64), ("learning_rate", ctypes.c_float),
+                ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("epsilon", ctypes.c_float),
+                ("weight_decay", ctypes.c_float), ("max_grad", ctypes.c_float),
+                ("inv_bias_correction1", ctypes.c_double), ("inv_bias_correction2", ctypes.c_double)]
+
+
+class ShardedAdam:
+    """Adam over this rank's shard, fused with the gradient average and the parameter all-gather.
+    `field_ranges` maps each role to its [begin, end) in the flat buffers; `lr` maps role -> rate."""
+
+    def __init__(self, params: PeerBuffers, grads: PeerBuffers, field_ranges: dict, lr: dict, group, device,
+                 beta1=0.9, beta2=0.999, epsilon=1e-8):
+        import torch
+        self.params, self.grads, self.group = params, grads, group
+        self.world, self.rank = params.world, params.rank
+        numel = params.local.numel()
+        self.begin, self.end = shard_bounds(numel, self.world, self.rank)
+        self.runs = shard_segments(field_ranges, self.begin, self.end)
+        n = self.end - self.begin
+        self.m1 = torch.zeros(max(n, ALIGN), dtype=torch.float32, device=device)
+        self.m2 = torch.zeros(max(n, ALIGN), dtype=torch.float32, device=device)
+        self.lr = dict(lr)
+        self.beta1, self.beta2, self.epsilon = beta1, beta2, epsilon
+        self.steps = 0
+        self.token = torch.zeros(1, dtype=torch.float32, device=device)
+        self.kernel_events = None  # optional list receiving (start, end) CUDA events around each launch
+        P = ctypes.c_void_p * self.world
+        self._params = P(*self.params.ptrs)
+        self._grads = P(*self.grads.ptrs)
+
+    def _barrier(self):
+        import torch.distributed as dist
+        dist.all_reduce(self.token, group=self.group)
+
+    def step(self, stream=None):
+        from . import _stream_handle
+        self.steps += 1
+        b1 = float(ctypes.c_float(self.beta1).value)
+        b2 = float(ctypes.c_float(self.beta2).value)
+        segs = (Segment * max(len(self.runs), 1))()
+        for k, (f, a, b) in enumerate(self.runs):
+            s = segs[k]
+            s.begin, s.end = a, b
+            s.learning_rate, s.beta1, s.beta2, s.epsilon = self.lr[f], self.beta1, self.beta2, self.epsilon
+            s.weight_decay, s.max_grad = 0.0, 0.0
+            s.inv_bias_correction1 = 1.0 / (1.0 - math.pow(b1, self.steps))
+            s.inv_bias_correction2 = 1.0 / (1.0 - math.pow(b2, self.steps))
+        self._barrier()
+        ev = None
+        if self.kernel_events is not None:
+            import torch
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        check(lib().gsx_b200_dp_reduce_adam_gather(self.world, self.rank, self._params, self._grads,
+                                                   ctypes.c_void_p(self.m1.data_ptr()),
+                                                   ctypes.c_void_p(self.m2.data_ptr()), self.begin, self.end, segs,
+                                                   len(self.runs), _stream_handle(stream)))
+        if ev is not None:
+            ev[1].record()
+            self.kernel_events.append(ev)
+        self._barrier()
+
+    def nvlink_bytes(self) -> int:
+        """Bytes this rank moves over NVLink per step: its shard's gradients read from the other ranks
+        and its updated shard written to them."""
+        return 2 * (self.world - 1) * (self.end - self.begin) * 4

@@ -34,23 +34,37 @@ class GaussianModel:
             offs[f] = (o, cnt)
             o += (cnt + 3) // 4 * 4
         self.numel = o
-        self.flat_param = torch.zeros(o, dtype=torch.float32, device=device)
-        self.flat_grad = torch.zeros(o, dtype=torch.float32, device=device)
+        self.offsets = offs
+        # each field's padded [begin, end) in the flat buffers (16-byte aligned on both ends)
+        self.field_ranges = {f: (a, a + (c + 3) // 4 * 4) for f, (a, c) in offs.items()}
+        self._bind(torch.zeros(o, dtype=torch.float32, device=device), torch.zeros(o, dtype=torch.float32, device=device))
+        for f in self.fields:
+            src = np.ascontiguousarray(arrays[f], dtype=np.float32).reshape(self.params[f].shape)
+            self.params[f].copy_(torch.from_numpy(src))
+
+    def _bind(self, flat_param, flat_grad):
+        self.flat_param, self.flat_grad = flat_param, flat_grad
         self.params, self.grads = {}, {}
         for f in self.fields:
-            a, c = offs[f]
+            a, c = self.offsets[f]
             shape = (self.n,) + FIELD_COLS[f]
             self.params[f] = self.flat_param[a:a + c].view(shape)
             self.grads[f] = self.flat_grad[a:a + c].view(shape)
-            src = np.ascontiguousarray(arrays[f], dtype=np.float32).reshape(shape)
-            self.params[f].copy_(torch.from_numpy(src))
+
+    def rebind(self, flat_param, flat_grad):
+        """Move the parameters into other flat buffers (e.g. ones mapped into the peer ranks)."""
+        flat_param.copy_(self.flat_param)
+        flat_grad.zero_()
+        self._bind(flat_param, flat_grad)
 
 
 class Trainer:
     """One view per call of step(); `group` is a torch.distributed process group (None = 1 GPU)."""
 
     def __init__(self, model: GaussianModel, width: int, height: int, lr: dict | None = None, l1_weight=0.8,
-                 ssim_weight=0.2, background=(0.0, 0.0, 0.0), group=None, device="cuda:0"):
+                 ssim_weight=0.2, background=(0.0, 0.0, 0.0), group=None, device="cuda:0", exchange="fused"):
+        """exchange (with a group): "fused" = gsx_b200.dp.ShardedAdam (gradient average + sharded Adam +
+        parameter all-gather in one NVLink kernel per rank); "nccl" = all-reduce AVG then Adam everywhere."""
         self.model = model
         self.renderer = Renderer(width, height)
         self.ctx = RenderContext(torch.device(device).index or 0)
@@ -62,7 +76,15 @@ class Trainer:
         self.background = background
         self.group = group
         lr = dict(DEFAULT_LR, **(lr or {}))
-        self.optim = Adam([ParamGroup(f, model.params[f], model.grads[f], lr[f]) for f in model.fields])
+        self.sharded = None
+        if group is not None and exchange == "fused":
+            from .dp import PeerBuffers, ShardedAdam
+            self._peer = (PeerBuffers(model.numel, group, device), PeerBuffers(model.numel, group, device))
+            model.rebind(self._peer[0].local, self._peer[1].local)
+            self.sharded = ShardedAdam(self._peer[0], self._peer[1], model.field_ranges, lr, group, device)
+            self.optim = None
+        else:
+            self.optim = Adam([ParamGroup(f, model.params[f], model.grads[f], lr[f]) for f in model.fields])
 
     def step(self, camera: Camera, target, events=None):
         """One training iteration on `camera` against `target` ([3,H,W] on the device).
@@ -79,6 +101,13 @@ class Trainer:
         if events:
             events[0][1].record()
         self.renderer.backward(self.ctx, self.grad_rgb, m.grads)
+        if self.sharded is not None:
+            if events:
+                events[1][0].record()
+            self.sharded.step()
+            if events:
+                events[1][1].record()
+            return self.loss_sum
         if self.group is not None:
             allreduce_mean(m.flat_grad, self.group)
         if events:
@@ -87,6 +116,19 @@ class Trainer:
         if events:
             events[1][1].record()
         return self.loss_sum
+
+    def close(self):
+        """Release the peer mappings: every rank unmaps, a barrier, then every rank frees its own."""
+        if self.sharded is not None:
+            import torch
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            for b in self._peer:
+                b.close_peers()
+            dist.barrier(group=self.group)
+            for b in self._peer:
+                b.free()
+            self.sharded = None
 
 
 def allreduce_mean(flat, group):

@@ -303,6 +303,39 @@ GSX_B200_API int gsx_b200_iota_i32(int32_t *dst, uint64_t n, void *stream);
  * gsx_b200_adc_select_keep: the ordered list of rows the prune pass keeps (adc.cu:499-539) in keep[],
  * its length in *device_count; flags[n] is scratch.
  */
+/*
+ * Data-parallel training over NVLink: the gradient all-reduce and Adam fused into one kernel per rank
+ * (no counterpart in the reference, which runs one view per process and no exchange; it replaces the
+ * ncclAllReduce + full Adam that the data-parallel extension of gsx-runtime.c:1413-1536 would issue).
+ * Rank `rank` of `world` owns the flat elements [shard_begin, shard_end): it averages them over
+ * grads[0..world-1] (sum in rank order, times 1/world), applies Adam with the shard-local moments
+ * (first/second_moment[k] belongs to element shard_begin + k) and stores the updated values into
+ * params[0..world-1].  params[r] / grads[r] are rank r's flat buffers mapped into this process
+ * (gsx_b200_ipc_open; this rank's own buffers for r == rank), 16-byte aligned.  segments cut the shard
+ * into runs of one parameter role (Adam hyper-parameters per run), bounds multiples of 4 elements.
+ * The kernel never waits: all ranks' gradients must be complete before it runs, and no rank may read
+ * its parameters until every rank's call has finished (the host orders both with collectives).
+ */
+#define GSX_B200_DP_MAX_RANKS 8
+#define GSX_B200_DP_MAX_SEGMENTS 8
+#define GSX_B200_IPC_HANDLE_BYTES 64
+typedef struct gsx_b200_dp_segment {
+    uint64_t begin, end;
+    float learning_rate, beta1, beta2, epsilon, weight_decay, max_grad;
+    double inv_bias_correction1, inv_bias_correction2;
+} gsx_b200_dp_segment;
+GSX_B200_API int gsx_b200_dp_reduce_adam_gather(int world, int rank, float *const *params, const float *const *grads,
+                                                float *first_moment, float *second_moment, uint64_t shard_begin,
+                                                uint64_t shard_end, const gsx_b200_dp_segment *segments, int n_segments,
+                                                void *stream);
+/* Device buffers that other processes can map: cudaMalloc / cudaFree, the 64-byte CUDA IPC handle of a
+ * buffer from gsx_b200_device_alloc, and mapping / unmapping another process's buffer by its handle. */
+GSX_B200_API int gsx_b200_device_alloc(uint64_t bytes, void **out);
+GSX_B200_API int gsx_b200_device_free(void *ptr);
+GSX_B200_API int gsx_b200_ipc_handle(void *base, void *out_handle);
+GSX_B200_API int gsx_b200_ipc_open(const void *handle, void **out);
+GSX_B200_API int gsx_b200_ipc_close(void *ptr);
+
 GSX_B200_API uint64_t gsx_b200_adc_scratch_words(uint64_t n);
 GSX_B200_API int gsx_b200_adc_select_growth(uint64_t n, const float *grad_acc, const float *visible_counter,
                                             const float *logscale, float grad_threshold, float scale_threshold,

@@ -143,3 +143,22 @@ def test_band_rows_partition_the_frame(height, world):
     assert pos == height
     tiles = [(b1 - b0 + 15) // 16 for b0, b1 in bands if b1 > b0]
     assert max(tiles) - min(tiles) <= 1
+
+
+@pytest.mark.parametrize("numel,world", [(4, 1), (400, 3), (12348, 8), (16, 8), (1_000_000, 4)])
+def test_shards_cover_the_flat_space(numel, world):
+    from gsx_b200.dp import shard_bounds, shard_segments
+    bounds = [shard_bounds(numel, world, r) for r in range(world)]
+    pos = 0
+    for b, e in bounds:
+        assert b == pos and e >= b and b % 4 == 0 and e % 4 == 0
+        pos = e
+    assert pos == numel
+    ranges = {"a": (0, numel // 2 // 4 * 4), "b": (numel // 2 // 4 * 4, numel)}
+    covered = 0
+    for b, e in bounds:
+        runs = shard_segments(ranges, b, e)
+        for f, lo, hi in runs:
+            assert ranges[f][0] <= lo < hi <= ranges[f][1] and b <= lo and hi <= e
+            covered += hi - lo
+    assert covered == numel
