@@ -15,8 +15,9 @@
  * replies to the other ranks' loads of its gradients), like a ring all-reduce, and runs Adam on
  * 1/world of the parameters instead of all of them.  Measured on two B200s: 168 MB per direction in
  * 0.255 ms, 660 GB/s per direction, at the link rate of a plain peer copy; issuing the stores through
- * the copy engines in pipelined chunks instead was slower (0.31-0.43 ms).  No waits inside the kernel: the host orders it
- * between two collectives (all ranks' backward done before; every rank's parameters complete after).
+ * the copy engines in pipelined chunks instead was slower (0.31-0.43 ms).  No waits inside the
+ * kernel: the host orders it between two collectives (all ranks' backward done before; every rank's
+ * parameters complete after).
  * The element update is gsx_adam_one, the same arithmetic as the single-GPU Adam kernel.
  */
 #include "../../include/gsx_b200.h"
