@@ -360,27 +360,37 @@ def main():
     value = world * args.steps / (ms_max / 1000.0)
 
     # ---- end to end through the public API: H2D target + D2H loss every step ----
+    # (gsx_b200.train.HostFeed: each step's pinned target uploads on a copy stream while the previous
+    #  step computes, and each step's loss is read back into pinned memory one step later)
+    from gsx_b200.train import HostFeed
     host_targets = [tt.cpu().pin_memory() for tt in targets]
-    dev_target = torch.empty_like(targets[0])
-    loss_host = torch.zeros(1, dtype=torch.float32).pin_memory()
+    feed = HostFeed(targets[0].shape, dev)
+    losses = []
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
+    feed.upload(host_targets[view(args.warmup + args.steps)], 0)
     for s in range(args.steps):
         v = view(args.warmup + args.steps + s)
-        dev_target.copy_(host_targets[v], non_blocking=True)
-        loss = trainer.step(cams[v], dev_target)
-        loss_host.copy_(loss, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        slot = s % 2
+        target = feed.target(slot)
+        if s + 1 < args.steps:
+            feed.upload(host_targets[view(args.warmup + args.steps + s + 1)], 1 - slot)
+        loss = trainer.step(cams[v], target)
+        feed.finish(slot, loss)
+        if s >= 1:
+            losses.append(feed.read_loss(1 - slot))
+    losses.append(feed.read_loss((args.steps - 1) % 2))
     f1.record(stream)
     torch.cuda.synchronize()
+    assert len(losses) == args.steps and all(np.isfinite(losses))
     t2 = torch.tensor([f0.elapsed_time(f1)], device=dev)
     if world > 1:
         dist.all_reduce(t2, op=dist.ReduceOp.MAX)
     e2e_value = world * args.steps / (float(t2.item()) / 1000.0)
-    h2d = dev_target.numel() * 4
+    h2d = targets[0].numel() * 4
     trainer.ctx.check()
     trainer.close()
 

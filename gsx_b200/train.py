@@ -141,3 +141,54 @@ def allreduce_mean(flat, group):
     else:
         dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
         flat.div_(dist.get_world_size(group))
+
+
+class HostFeed:
+    """Per-step host I/O of a training loop: each step's target image goes from pinned host memory to
+    the device on a copy stream, double-buffered, so the upload of step s+1 overlaps step s; each
+    step's loss comes back into pinned host memory and is read one step later (no per-step stall of
+    the compute stream).  Every step still moves its full target in and its loss out."""
+
+    def __init__(self, shape, device):
+        import torch
+        self.device = torch.device(device)
+        self.copy_stream = torch.cuda.Stream(self.device)
+        self.buf = [torch.empty(shape, dtype=torch.float32, device=self.device) for _ in range(2)]
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.free = [None, None]
+        self.loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
+        self.loss_ev = [torch.cuda.Event() for _ in range(2)]
+        self.pending = [False, False]
+
+    def upload(self, host_tensor, slot: int):
+        """Queue the copy of `host_tensor` (pinned) into buffer `slot` once its previous user is done."""
+        import torch
+        with torch.cuda.stream(self.copy_stream):
+            if self.free[slot] is not None:
+                self.copy_stream.wait_event(self.free[slot])
+            self.buf[slot].copy_(host_tensor, non_blocking=True)
+            self.ready[slot].record(self.copy_stream)
+
+    def target(self, slot: int):
+        """Buffer `slot` for the compute stream (ordered after its upload)."""
+        import torch
+        torch.cuda.current_stream(self.device).wait_event(self.ready[slot])
+        return self.buf[slot]
+
+    def finish(self, slot: int, loss):
+        """The step that used buffer `slot` is queued: release the buffer and queue its loss read."""
+        import torch
+        ev = torch.cuda.Event()
+        ev.record()
+        self.free[slot] = ev
+        self.loss_host[slot:slot + 1].copy_(loss, non_blocking=True)
+        self.loss_ev[slot].record()
+        self.pending[slot] = True
+
+    def read_loss(self, slot: int) -> float:
+        """The loss of the step that used buffer `slot` (waits only for that step)."""
+        if not self.pending[slot]:
+            return float("nan")
+        self.loss_ev[slot].synchronize()
+        self.pending[slot] = False
+        return float(self.loss_host[slot])
