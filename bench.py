@@ -414,10 +414,11 @@ def main():
             "preprocess": 56 * n + 52 * V + 4 * n,
             # emission: PrimRec + count + mask per visible Gaussian in, key + value + tile-count add out
             "emit": 48 * V + 8 * n + 16 * I,
-            # binning (key + value in, 8-byte sort key out) + per-tile sort (sort key in, key + value out)
-            "sort": 40 * I,
-            # tile scan: 8 sub-counters read twice, ranges + bucket prefix + end positions + class list written
-            "ranges": 112 * ((W + 15) // 16) * ((H + 15) // 16),
+            # per-tile sort: 8-byte sort key in, key + value out
+            "sort": 20 * I,
+            # tile scan (32 sub-counters read twice, ranges + bucket prefix + end positions + class list
+            # written) + binning (key + value in, 8-byte sort key out)
+            "ranges": 112 * ((W + 15) // 16) * ((H + 15) // 16) + 20 * I,
             "blend_forward": 4 * I + 48 * I + 28 * P + 16 * 256 * B,
             "blend_backward": 4 * I + 48 * I + 28 * P + 16 * 256 * B + 48 * I,
             "preprocess_backward": 56 * n + 48 * V * 2 + 44 * n,

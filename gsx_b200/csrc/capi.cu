@@ -146,6 +146,9 @@ struct gsx_b200_context {
     cudaStream_t side[GSX_SORT_CLASSES - 1] = {};
     cudaEvent_t side_ev[GSX_SORT_CLASSES] = {};
     bool side_created = false;
+    /* recorded after the forward's read-back copies: the host waits on it, not on the stream, so the
+     * kernels queued behind the copies keep the GPU busy meanwhile */
+    cudaEvent_t readback_ev = nullptr;
     uint64_t launches = 0; /* kernels launched by this context (host-side count) */
     /* retained forward state */
     bool has_train = false;
@@ -245,6 +248,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
                 cudaEventDestroy(ctx->ev[s][k][0]);
                 cudaEventDestroy(ctx->ev[s][k][1]);
             }
+    if(ctx->readback_ev) cudaEventDestroy(ctx->readback_ev);
     if(ctx->side_created) {
         for(int k = 0; k < GSX_SORT_CLASSES - 1; ++k) cudaStreamDestroy(ctx->side[k]);
         for(int k = 0; k < GSX_SORT_CLASSES; ++k) cudaEventDestroy(ctx->side_ev[k]);
@@ -312,16 +316,20 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
     uint32_t *block_sums = (uint32_t *)ctx->block_sums.ptr;
 
     /* preprocess -> block-total scan -> emission into the current instance capacity (each instance
-     * takes its rank in its tile) -> tile scan (ranges, bucket prefix, total, largest tile) -> ONE host
-     * synchronisation; if the capacity was too small the emission is repeated into grown buffers (rare:
-     * capacity keeps 25% headroom).  Then the tile binning + per-tile depth sort, or, when a tile holds
-     * more instances than shared memory sorts, the global radix sort of the tile|depth keys. */
+     * takes its rank in its tile) -> tile scan (ranges, bucket prefix, total, largest tile) -> ONE
+     * read-back (instance total, largest tile, size-class counts), behind which the binning is already
+     * queued (it reads the total on the device), so the GPU bins while the host waits; if the
+     * capacity was too small the emission is repeated into grown buffers (rare: capacity keeps 25%
+     * headroom).  Then the per-tile depth sort, or, when a tile holds more instances than shared memory
+     * sorts, the global radix sort of the tile|depth keys (the binning's output is then unused). */
     int tile_bits = 0;
     while((1 << tile_bits) < n_tiles) ++tile_bits;
     const int end_bit = 32 + tile_bits;
     if(int rc = ensure(ctx->tile_count, sizeof(uint32_t) * GSX_TILE_SUBCOUNTERS * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->class_tiles, sizeof(uint32_t) * (size_t)n_tiles)) return rc;
     if(int rc = ensure(ctx->tile_aux, sizeof(uint32_t) * gsx_tile_scan_aux_words(n_tiles))) return rc;
+    if(ctx->readback_ev == nullptr)
+        GSX_CUDA_TRY(cudaEventCreateWithFlags(&ctx->readback_ev, cudaEventDisableTiming), "cudaEventCreate");
     uint32_t *tile_count = (uint32_t *)ctx->tile_count.ptr;
     uint32_t *class_tiles = (uint32_t *)ctx->class_tiles.ptr;
     uint64_t total = 0;
@@ -352,6 +360,25 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
                                           (uint32_t *)ctx->tile_aux.ptr, words + 2, stream),
                      "tile scan launch");
         ctx->launches += n_tiles > 0 ? 3 : 0;
+        if(n > 0)
+            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
+                         "D2H");
+        else
+            ctx->host_words[0] = 0;
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (1 + GSX_SORT_CLASSES) * sizeof(uint32_t),
+                                     cudaMemcpyDeviceToHost, stream),
+                     "D2H");
+        GSX_CUDA_TRY(cudaEventRecord(ctx->readback_ev, stream), "cudaEventRecord");
+        /* binning for the per-tile sort: keys/values of the emission -> (depth, primitive) keys in the
+         * second half of the key buffer, count read on the device (words[2], the tile scan's total) */
+        {
+            const uint64_t kc = ctx->keys.bytes / (2 * sizeof(unsigned long long));
+            unsigned long long *ka = (unsigned long long *)ctx->keys.ptr;
+            GSX_CUDA_TRY(gsx_launch_tile_bin(ka, (const uint32_t *)ctx->vals.ptr, words + 2, ctx->inst_cap, tile_count, ka + kc,
+                                             stream),
+                         "tile bin launch");
+            ctx->launches += 1;
+        }
         return 0;
     };
     if(n > 0) {
@@ -365,24 +392,17 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
             ctx->launches += 2;
         }
         if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
-        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
-                     "D2H");
-        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (1 + GSX_SORT_CLASSES) * sizeof(uint32_t),
-                                     cudaMemcpyDeviceToHost, stream),
-                     "D2H");
-        GSX_CUDA_TRY(cudaStreamSynchronize(stream), "forward");
+        GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
         total = ctx->host_words[0];
         if(total > ctx->inst_cap) {
             if(int rc = emit_into_capacity(total + total / 4 + 1024)) return rc;
-            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (1 + GSX_SORT_CLASSES) * sizeof(uint32_t),
-                                         cudaMemcpyDeviceToHost, stream),
-                         "D2H");
-            GSX_CUDA_TRY(cudaStreamSynchronize(stream), "forward");
+            GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
         }
         max_tile = ctx->host_words[2];
     } else {
         GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
         if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
+        GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
     }
     ctx->n_instances = total;
     const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
@@ -408,11 +428,9 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
                     GSX_CUDA_TRY(cudaEventCreateWithFlags(&ctx->side_ev[k], cudaEventDisableTiming), "cudaEventCreate");
                 ctx->side_created = true;
             }
-            GSX_CUDA_TRY(gsx_launch_tile_sort(keys_a, vals_a, total, n_tiles, (const uint2 *)ctx->ranges.ptr, tile_count,
-                                              class_tiles, ctx->host_words + 3, keys_b, keys_a, vals_a, stream, ctx->side,
-                                              ctx->side_ev),
+            GSX_CUDA_TRY(gsx_launch_tile_sort(total, n_tiles, (const uint2 *)ctx->ranges.ptr, class_tiles, ctx->host_words + 3,
+                                              keys_b, keys_a, vals_a, stream, ctx->side, ctx->side_ev),
                          "tile sort launch");
-            ctx->launches += 1;
             for(int c = 0; c < GSX_SORT_CLASSES; ++c) ctx->launches += ctx->host_words[3 + c] ? 1 : 0;
         } else {
             /* a tile too large for shared memory: stable global radix sort of the tile|depth keys

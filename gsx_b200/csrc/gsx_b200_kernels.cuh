@@ -154,10 +154,12 @@ size_t gsx_tile_scan_aux_words(int n_tiles);
 cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
                                  uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream);
 /* side: GSX_SORT_CLASSES - 1 streams; ev: GSX_SORT_CLASSES events (fork and join) */
-cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t *vals, uint64_t n, int n_tiles,
-                                 const uint2 *ranges, uint32_t *tile_end, const uint32_t *class_tiles,
-                                 const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
-                                 uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev);
+cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *vals, const uint32_t *d_total,
+                                uint64_t max_n, uint32_t *tile_end, unsigned long long *sort_keys, cudaStream_t stream);
+cudaError_t gsx_launch_tile_sort(uint64_t n, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
+                                 const uint32_t *class_counts, const unsigned long long *sort_keys,
+                                 unsigned long long *keys_out, uint32_t *vals_out, cudaStream_t stream,
+                                 cudaStream_t const *side, cudaEvent_t const *ev);
 /* out_rgb: [3, height, width] f32, or bf16 (round to nearest even) when out_bf16; row0 = first pixel
  * row of the band in the full frame (a multiple of 16, 0 for a full frame) */
 cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,

@@ -15,6 +15,8 @@
  *      per-class tile lists, and every sub-counter into the absolute end of its slice of the range;
  *   3. bin_kernel moves every instance into a slot of its tile's range (taken by counting its
  *      sub-counter's end back down: arbitrary order) as a 64-bit sort key depth_bits << 32 | primitive;
+ *      it reads the instance count from the device, so the host launches it before waiting for the
+ *      forward's one read-back and the GPU bins while the host decides the sort;
  *   4. segsort_kernel (one CTA per tile) radix-sorts the tile's (depth, primitive) keys in shared
  *      memory and writes the final tile|depth keys and primitive values: the order is fully
  *      determined.  Five size classes (up to 512, 1024, 2048, 4096 and 16384 instances), each launched
@@ -220,13 +222,17 @@ __global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__re
 
 /* each instance takes a slot of its tile by counting its sub-counter's end position back down (the
  * scan turned the counts into end positions) */
+/* the instance count comes from the device (the tile scan's total), so the launch needs no host
+ * round trip: the grid covers the emission capacity and the CTAs past the total exit at once */
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(const unsigned long long *__restrict__ keys,
-                                                          const uint32_t *__restrict__ vals, uint64_t n,
+                                                          const uint32_t *__restrict__ vals,
+                                                          const uint32_t *__restrict__ d_total, uint64_t max_n,
                                                           uint32_t *__restrict__ tile_end,
                                                           unsigned long long *__restrict__ sort_keys)
 {
     const uint64_t i = (uint64_t)blockIdx.x * kBinThreads + threadIdx.x;
-    if(i >= n) return;
+    const uint64_t n = *d_total;
+    if(i >= n || i >= max_n) return;
     const unsigned long long k = keys[i];
     const uint32_t tile = (uint32_t)(k >> 32);
     const uint32_t slot = atomicSub(&tile_end[tile * GSX_TILE_SUBCOUNTERS + (uint32_t)(i & (GSX_TILE_SUBCOUNTERS - 1))], 1u) - 1u;
@@ -402,20 +408,25 @@ cudaError_t launch_class(const uint2 *ranges, const uint32_t *list, uint32_t cou
 
 } // namespace
 
-cudaError_t gsx_launch_tile_sort(const unsigned long long *keys, const uint32_t *vals, uint64_t n, int n_tiles,
-                                 const uint2 *ranges, uint32_t *tile_end, const uint32_t *class_tiles,
-                                 const uint32_t *class_counts, unsigned long long *sort_keys, unsigned long long *keys_out,
-                                 uint32_t *vals_out, cudaStream_t stream, cudaStream_t const *side, cudaEvent_t const *ev)
+cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *vals, const uint32_t *d_total,
+                                uint64_t max_n, uint32_t *tile_end, unsigned long long *sort_keys, cudaStream_t stream)
+{
+    if(max_n == 0) return cudaSuccess;
+    bin_kernel<<<(unsigned)((max_n + kBinThreads - 1) / kBinThreads), kBinThreads, 0, stream>>>(keys, vals, d_total, max_n,
+                                                                                              tile_end, sort_keys);
+    return cudaGetLastError();
+}
+
+cudaError_t gsx_launch_tile_sort(uint64_t n, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
+                                 const uint32_t *class_counts, const unsigned long long *sort_keys,
+                                 unsigned long long *keys_out, uint32_t *vals_out, cudaStream_t stream,
+                                 cudaStream_t const *side, cudaEvent_t const *ev)
 {
     static_assert(kClassMax[kClasses - 1] == GSX_SEG_MAX, "the largest class covers up to GSX_SEG_MAX");
     static_assert(kClasses == GSX_SORT_CLASSES, "class count");
     if(n == 0 || n_tiles <= 0) return cudaSuccess;
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
-    if(err != cudaSuccess) return err;
-    bin_kernel<<<(unsigned)((n + kBinThreads - 1) / kBinThreads), kBinThreads, 0, stream>>>(keys, vals, n, tile_end,
-                                                                                          sort_keys);
-    err = cudaGetLastError();
     if(err != cudaSuccess) return err;
     /* fork: class c > 0 runs on side[c - 1] after the binning, class 0 on the caller's stream; join */
     err = cudaEventRecord(ev[0], stream);
