@@ -349,7 +349,7 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         {
             StageTimer st(ctx, 1, stream);
             GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets,
-                                         cam.grid_w, cam.trow0, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
+                                         cam.grid_w, cam.trow0, n_tiles, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
                                          ctx->inst_cap, words, nullptr, 0, tile_count, stream),
                          "emit launch");
             ctx->launches += n > 0 ? 1 : 0;
@@ -374,7 +374,7 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         {
             const uint64_t kc = ctx->keys.bytes / (2 * sizeof(unsigned long long));
             unsigned long long *ka = (unsigned long long *)ctx->keys.ptr;
-            GSX_CUDA_TRY(gsx_launch_tile_bin(ka, (const uint32_t *)ctx->vals.ptr, words + 2, ctx->inst_cap, tile_count, ka + kc,
+            GSX_CUDA_TRY(gsx_launch_tile_bin(ka, (const uint32_t *)ctx->vals.ptr, words + 2, ctx->inst_cap, n_tiles, tile_count, ka + kc,
                                              stream),
                          "tile bin launch");
             ctx->launches += 1;

@@ -138,7 +138,8 @@ cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, co
                                   float *max_screen_radius, cudaStream_t stream);
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
-                            uint32_t *offsets, int grid_w, int trow0, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
+                            uint32_t *offsets, int grid_w, int trow0, int n_tiles, unsigned long long *keys, uint32_t *vals,
+                            uint64_t capacity,
                             uint32_t *flags, uint32_t *hist, int n_digits, uint32_t *tile_count, cudaStream_t stream);
 cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a, unsigned long long *keys_b,
                                    uint32_t *vals_b, uint64_t count, const int *positions, const int *shifts,
@@ -150,12 +151,16 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
                                   size_t scratch_bytes, uint32_t *flags, int *out_result_in_b, cudaStream_t stream);
 #define GSX_SORT_CLASSES 5 /* per-tile sort size classes of k_tilesort.cu */
 #define GSX_TILE_SUBCOUNTERS 32 /* instance counters per tile (emission, binning); a multiple of 4 */
+/* sub-counter s of tile t, sub-counter-major: one tile's counters sit n_tiles words apart (different
+ * cache lines and L2 slices, so the atomics of a crowded tile spread), and a warp's 32 tiles read one
+ * counter index with one coalesced access */
+#define GSX_SUBCOUNTER(t, s, n_tiles) ((size_t)(s) * (size_t)(n_tiles) + (size_t)(t))
 size_t gsx_tile_scan_aux_words(int n_tiles);
 cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
                                  uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream);
 /* side: GSX_SORT_CLASSES - 1 streams; ev: GSX_SORT_CLASSES events (fork and join) */
 cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *vals, const uint32_t *d_total,
-                                uint64_t max_n, uint32_t *tile_end, unsigned long long *sort_keys, cudaStream_t stream);
+                                uint64_t max_n, int n_tiles, uint32_t *tile_end, unsigned long long *sort_keys, cudaStream_t stream);
 cudaError_t gsx_launch_tile_sort(uint64_t n, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
                                  const uint32_t *class_counts, const unsigned long long *sort_keys,
                                  unsigned long long *keys_out, uint32_t *vals_out, cudaStream_t stream,

@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                                                         const uint32_t *__restrict__ counts,
                                                         const uint32_t *__restrict__ tile_masks,
                                                         const uint32_t *__restrict__ block_offsets,
-                                                        uint32_t *__restrict__ offsets, unsigned grid_w, unsigned trow0,
+                                                        uint32_t *__restrict__ offsets, unsigned grid_w, unsigned trow0, unsigned n_tiles,
                                                         unsigned long long *__restrict__ keys, uint32_t *__restrict__ vals,
                                                         uint64_t capacity, uint32_t *__restrict__ flags,
                                                         uint32_t *__restrict__ hist, int n_digits,
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
-            if(tile_count) atomicAdd(&tile_count[t * GSX_TILE_SUBCOUNTERS + (wpos & (GSX_TILE_SUBCOUNTERS - 1))], 1u);
+            if(tile_count) atomicAdd(&tile_count[GSX_SUBCOUNTER(t, wpos & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u);
             ++wpos;
             for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
             const unsigned long long key = ((unsigned long long)t << 32) | dbits;
             keys[wpos] = key;
             vals[wpos] = (uint32_t)i;
-            if(tile_count) atomicAdd(&tile_count[t * GSX_TILE_SUBCOUNTERS + (wpos & (GSX_TILE_SUBCOUNTERS - 1))], 1u);
+            if(tile_count) atomicAdd(&tile_count[GSX_SUBCOUNTER(t, wpos & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u);
             ++wpos;
             for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
         }
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                 const unsigned long long key = ((unsigned long long)t << 32) | ldb;
                 keys[p] = key;
                 vals[p] = lidx;
-                if(tile_count) atomicAdd(&tile_count[t * GSX_TILE_SUBCOUNTERS + (p & (GSX_TILE_SUBCOUNTERS - 1))], 1u);
+                if(tile_count) atomicAdd(&tile_count[GSX_SUBCOUNTER(t, p & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u);
                 for(int q = 0; q < n_digits; ++q) atomicAdd(&s_hist[q][(uint32_t)(key >> (8 * q)) & 0xffu], 1u);
             }
             lpos += (uint32_t)__popc(ballot);
@@ -150,12 +150,13 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
-                            uint32_t *offsets, int grid_w, int trow0, unsigned long long *keys, uint32_t *vals, uint64_t capacity,
+                            uint32_t *offsets, int grid_w, int trow0, int n_tiles, unsigned long long *keys, uint32_t *vals,
+                            uint64_t capacity,
                             uint32_t *flags, uint32_t *hist, int n_digits, uint32_t *tile_count, cudaStream_t stream)
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
-    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, (unsigned)trow0, keys,
+    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, (unsigned)trow0, (unsigned)n_tiles, keys,
                                                             vals, capacity, flags, hist, n_digits, tile_count);
     return cudaGetLastError();
 }

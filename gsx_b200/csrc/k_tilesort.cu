@@ -54,14 +54,11 @@ __device__ __forceinline__ int size_class(uint32_t n)
 constexpr int kTileThreads = 256;
 constexpr int kAux = 2 + kClasses + 1; /* instances, buckets, per-class tiles, max */
 
-__device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub, int t, uint32_t part[GSX_TILE_SUBCOUNTERS])
+__device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub, int t, int n_tiles,
+                                               uint32_t part[GSX_TILE_SUBCOUNTERS])
 {
-    const uint4 *p = reinterpret_cast<const uint4 *>(sub + (size_t)t * GSX_TILE_SUBCOUNTERS);
 #pragma unroll
-    for(int q = 0; q < GSX_TILE_SUBCOUNTERS / 4; ++q) {
-        const uint4 v = p[q];
-        part[4 * q] = v.x, part[4 * q + 1] = v.y, part[4 * q + 2] = v.z, part[4 * q + 3] = v.w;
-    }
+    for(int q = 0; q < GSX_TILE_SUBCOUNTERS; ++q) part[q] = sub[GSX_SUBCOUNTER(t, q, n_tiles)];
     uint32_t c = 0;
 #pragma unroll
     for(int k = 0; k < GSX_TILE_SUBCOUNTERS; ++k) c += part[k];
@@ -71,7 +68,6 @@ __device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub,
 __global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_t *__restrict__ sub, int n_tiles,
                                                                    uint32_t *__restrict__ block_aux)
 {
-    static_assert(GSX_TILE_SUBCOUNTERS % 4 == 0, "16-byte loads of the sub-counters");
     __shared__ uint32_t s[kTileThreads / 32][kAux];
     const int t = blockIdx.x * kTileThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -80,7 +76,7 @@ __global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_
     for(int q = 0; q < kAux; ++q) v[q] = 0u;
     if(t < n_tiles) {
         uint32_t part[GSX_TILE_SUBCOUNTERS];
-        const uint32_t c = tile_total(sub, t, part);
+        const uint32_t c = tile_total(sub, t, n_tiles, part);
         v[0] = c;
         v[1] = (c + 31u) / 32u;
         if(c) v[2 + size_class(c)] = 1u;
@@ -168,7 +164,7 @@ __global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__re
     const unsigned lt = (1u << lane) - 1u;
     uint32_t part[GSX_TILE_SUBCOUNTERS];
     uint32_t c = 0;
-    if(t < n_tiles) c = tile_total(sub, t, part);
+    if(t < n_tiles) c = tile_total(sub, t, n_tiles, part);
     const int cls = c ? size_class(c) : -1;
     /* in-warp exclusive prefixes: instances and buckets by shuffles, class memberships by ballots */
     uint32_t vi = c, vb = (c + 31u) / 32u;
@@ -203,15 +199,10 @@ __global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__re
     ranges[t] = c ? make_uint2(start, start + c) : make_uint2(0u, 0u);
     bucket_offsets[t] = ob + ib;
     uint32_t run = start;
-    uint4 *ends = reinterpret_cast<uint4 *>(sub + (size_t)t * GSX_TILE_SUBCOUNTERS);
 #pragma unroll
-    for(int q = 0; q < GSX_TILE_SUBCOUNTERS / 4; ++q) {
-        uint4 e;
-        e.x = run += part[4 * q];
-        e.y = run += part[4 * q + 1];
-        e.z = run += part[4 * q + 2];
-        e.w = run += part[4 * q + 3];
-        ends[q] = e;
+    for(int q = 0; q < GSX_TILE_SUBCOUNTERS; ++q) {
+        run += part[q];
+        sub[GSX_SUBCOUNTER(t, q, n_tiles)] = run;
     }
     if(cls >= 0) {
         uint32_t pos = block_aux[(size_t)blockIdx.x * kAux + 2 + cls] + cpos;
@@ -227,7 +218,7 @@ __global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__re
 __global__ void __launch_bounds__(kBinThreads) bin_kernel(const unsigned long long *__restrict__ keys,
                                                           const uint32_t *__restrict__ vals,
                                                           const uint32_t *__restrict__ d_total, uint64_t max_n,
-                                                          uint32_t *__restrict__ tile_end,
+                                                          int n_tiles, uint32_t *__restrict__ tile_end,
                                                           unsigned long long *__restrict__ sort_keys)
 {
     const uint64_t i = (uint64_t)blockIdx.x * kBinThreads + threadIdx.x;
@@ -235,7 +226,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const unsigned long lo
     if(i >= n || i >= max_n) return;
     const unsigned long long k = keys[i];
     const uint32_t tile = (uint32_t)(k >> 32);
-    const uint32_t slot = atomicSub(&tile_end[tile * GSX_TILE_SUBCOUNTERS + (uint32_t)(i & (GSX_TILE_SUBCOUNTERS - 1))], 1u) - 1u;
+    const uint32_t slot = atomicSub(&tile_end[GSX_SUBCOUNTER(tile, i & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u) - 1u;
     sort_keys[slot] = (k << 32) | (unsigned long long)vals[i];
 }
 
@@ -409,11 +400,12 @@ cudaError_t launch_class(const uint2 *ranges, const uint32_t *list, uint32_t cou
 } // namespace
 
 cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *vals, const uint32_t *d_total,
-                                uint64_t max_n, uint32_t *tile_end, unsigned long long *sort_keys, cudaStream_t stream)
+                                uint64_t max_n, int n_tiles, uint32_t *tile_end, unsigned long long *sort_keys,
+                                cudaStream_t stream)
 {
-    if(max_n == 0) return cudaSuccess;
+    if(max_n == 0 || n_tiles <= 0) return cudaSuccess;
     bin_kernel<<<(unsigned)((max_n + kBinThreads - 1) / kBinThreads), kBinThreads, 0, stream>>>(keys, vals, d_total, max_n,
-                                                                                              tile_end, sort_keys);
+                                                                                              n_tiles, tile_end, sort_keys);
     return cudaGetLastError();
 }
 
