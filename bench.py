@@ -454,7 +454,7 @@ def main():
                        "gaussians": n, "width": W, "height": H, "views_per_step": world,
                        "parallelism": (f"dp{world} (views), " + (
                            "fused NVLink gradient average + sharded Adam + parameter all-gather (one kernel per rank)"
-                           if args.exchange == "fused" else "NCCL all-reduce AVG of 14 f32/Gaussian + Adam on every rank")
+                           if trainer.exchange == "fused" else "NCCL all-reduce AVG of 14 f32/Gaussian + Adam on every rank")
                            if world > 1 else "dp1 (views)"),
                        "l2": "inputs larger than L2 (params+grads+moments = 672 MB)",
                        "visible": V, "instances": I, "buckets": B},

@@ -77,14 +77,41 @@ class Trainer:
         self.group = group
         lr = dict(DEFAULT_LR, **(lr or {}))
         self.sharded = None
+        self.exchange = "nccl" if group is not None else None
         if group is not None and exchange == "fused":
-            from .dp import PeerBuffers, ShardedAdam
-            self._peer = (PeerBuffers(model.numel, group, device), PeerBuffers(model.numel, group, device))
-            model.rebind(self._peer[0].local, self._peer[1].local)
-            self.sharded = ShardedAdam(self._peer[0], self._peer[1], model.field_ranges, lr, group, device)
-            self.optim = None
-        else:
+            self._setup_fused(model, group, device, lr)
+        if self.sharded is None:
             self.optim = Adam([ParamGroup(f, model.params[f], model.grads[f], lr[f]) for f in model.fields])
+
+    def _setup_fused(self, model, group, device, lr):
+        """Peer-map the flat buffers and build the sharded optimizer.  Every rank reports whether its
+        setup worked (one all-reduce); if any rank failed (e.g. no peer access between two GPUs),
+        all ranks keep the NCCL exchange, so the ranks never disagree about the protocol."""
+        import torch
+        import torch.distributed as dist
+        from .dp import PeerBuffers, ShardedAdam
+        peer, err = None, None
+        try:
+            peer = (PeerBuffers(model.numel, group, device), PeerBuffers(model.numel, group, device))
+        except Exception as e:  # noqa: BLE001 - reported below, every rank falls back together
+            err = e
+        ok = torch.tensor([0.0 if err is not None else 1.0], device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if float(ok.item()) < 1.0:
+            if peer is not None:
+                for b in peer:
+                    b.close_peers()
+                dist.barrier(group=group)
+                for b in peer:
+                    b.free()
+            import warnings
+            warnings.warn(f"fused NVLink exchange unavailable ({err or 'failed on another rank'}); using NCCL")
+            return
+        self._peer = peer
+        model.rebind(peer[0].local, peer[1].local)
+        self.sharded = ShardedAdam(peer[0], peer[1], model.field_ranges, lr, group, device)
+        self.optim = None
+        self.exchange = "fused"
 
     def step(self, camera: Camera, target, events=None):
         """One training iteration on `camera` against `target` ([3,H,W] on the device).
