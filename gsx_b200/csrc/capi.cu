@@ -121,6 +121,8 @@ CameraParams make_camera(const gsx_b200_camera &c, int row_begin, int row_end)
     p.clip_r = (1.15f * p.width_f - p.cx) / p.fx;
     p.clip_t = (-0.15f * p.height_f - p.cy) / p.fy;
     p.clip_b = (1.15f * p.height_f - p.cy) / p.fy;
+    p.cull_jx = 1.0f + fmaxf(p.clip_l * p.clip_l, p.clip_r * p.clip_r);
+    p.cull_jy = 1.0f + fmaxf(p.clip_t * p.clip_t, p.clip_b * p.clip_b);
     return p;
 }
 

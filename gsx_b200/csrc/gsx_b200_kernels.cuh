@@ -54,6 +54,10 @@ struct CameraParams {
      * height_f; every projection, tile test and pixel position uses full-frame coordinates, only
      * the tile rows kept (grid_h from trow0) and the output rows are the band's.  0 = full frame. */
     int trow0;
+    /* 1 + the largest squared clamped normalised coordinate (x: max(clip_l^2, clip_r^2), y likewise):
+     * bounds the squared row norm of the EWA Jacobian over (fx or fy / depth)^2, for the preprocess's
+     * conservative screen cull */
+    float cull_jx, cull_jy;
 };
 
 /* Decoupled-lookback status word: 2-bit flag in the top bits, 30-bit count below. */
