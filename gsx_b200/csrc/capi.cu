@@ -139,7 +139,7 @@ struct gsx_b200_context {
     uint32_t *host_hist = nullptr; /* pinned copy of hist */
     /* per tile / pixel / bucket */
     DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap, tile_count, class_tiles, tile_aux;
-    /* small device words: [0] flags; from the tile scan: [2] instance total, [3] largest tile,
+    /* small device words: [0] sticky flags, [1] the emission's overflow bit; from the tile scan: [2] instance total, [3] largest tile,
      * [4..8] tiles per per-tile-sort size class */
     DevBuf words;
     uint32_t *host_words = nullptr; /* pinned: [0] instance total, [1] flags, [2] largest tile, [3..7] class sizes */
@@ -345,14 +345,17 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         ctx->inst_cap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
         const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
         if(vcap < ctx->inst_cap) ctx->inst_cap = vcap;
-        GSX_CUDA_TRY(cudaMemsetAsync(words, 0, sizeof(uint32_t), stream), "memset");
+        /* the emission's capacity-overflow bit lives in its own word (words[1]), cleared per pass: an
+         * overflow is expected on the pass before a capacity retry.  words[0] keeps the sticky flags
+         * (lookback timeouts) until gsx_b200_context_check reads them. */
+        GSX_CUDA_TRY(cudaMemsetAsync(words + 1, 0, sizeof(uint32_t), stream), "memset");
         GSX_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * GSX_TILE_SUBCOUNTERS * (size_t)n_tiles, stream),
                      "memset");
         {
             StageTimer st(ctx, 1, stream);
             GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets,
                                          cam.grid_w, cam.trow0, n_tiles, (unsigned long long *)ctx->keys.ptr, (uint32_t *)ctx->vals.ptr,
-                                         ctx->inst_cap, words, nullptr, 0, tile_count, stream),
+                                         ctx->inst_cap, words + 1, nullptr, 0, tile_count, stream),
                          "emit launch");
             ctx->launches += n > 0 ? 1 : 0;
         }

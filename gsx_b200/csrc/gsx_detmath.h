@@ -55,7 +55,7 @@ GSX_HD uint32_t gsx_float_to_bits(float f)
  *   P(r) = sum_{k=0..7} r^k/k!  (truncation error below 1e-8 relative on |r| <= 0.347).
  * ln2 is split into a 16-bit head (so n*head is exact for |n| <= 256) and a tail.
  * Results below 2^-126 (x < -87.33) are returned as 0; x > 88.72 returns +inf.
- * Measured against libm to within 2 ulp over the whole normal range (tests/test_oracle_math.py).
+ * Measured against libm to within 2 ulp over the whole normal range (tests/test_oracle_pins.py, test_detmath_exp_log_within_two_ulp).
  */
 GSX_HD float gsx_expf_inrange(float x);
 

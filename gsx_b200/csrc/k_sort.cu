@@ -312,12 +312,15 @@ cudaError_t gsx_launch_sort_passes(unsigned long long *keys_a, uint32_t *vals_a,
  * Allocation-free variant (gsx_b200_sort_pairs_noalloc, include/gsx_b200.h).
  *
  * Some callers must not allocate device memory on their own: a host that hands every buffer out of
- * its own arenas and accounts for all device memory (GSX's backend model), or code that runs while
- * a CUDA graph is being captured.  For them the sort's scratch (the alternate key/value buffers,
- * the digit histograms and the lookback table) lives in one file-scope device array sized for
- * GSX_B200_NOALLOC_SORT_MAX_PAIRS pairs.  Every GPU that loads this library holds the array until
- * the process exits.  All calls share it: calls that overlap on the GPU (different streams, or
- * different host threads on the same device) race and must be serialised by the caller.
+ * its own arenas and accounts for all device memory (GSX's backend model), or a plugin host with a
+ * fixed GPU memory budget that forbids hidden cudaMalloc calls.  For them the sort's scratch (the
+ * alternate key/value buffers, the digit histograms, the lookback table and one status word) lives
+ * in one file-scope device array sized for GSX_B200_NOALLOC_SORT_MAX_PAIRS pairs.  Every GPU that
+ * loads this library holds the array until the process exits.  All calls share it: calls that
+ * overlap on the GPU (different streams, or different host threads on the same device) race and
+ * must be serialised by the caller.  Each call clears the status word first and reads it back after
+ * the sort (so the call waits for its stream), returning GSX_B200_UNKNOWN if the bounded lookback
+ * wait gave up.
  */
 #include "../../include/gsx_b200.h"
 
@@ -375,14 +378,24 @@ extern "C" int gsx_b200_sort_pairs_noalloc(uint64_t *keys, uint32_t *values, uin
     void *scratch = base + kNoAllocKeysBytes + kNoAllocValsBytes;
     uint32_t *flags = reinterpret_cast<uint32_t *>(base + kNoAllocKeysBytes + kNoAllocValsBytes + kNoAllocSortBytes);
     int in_b = 0;
-    /* the launcher clears the histograms, tile counters and lookback table before use */
-    err = gsx_launch_sort_pairs(reinterpret_cast<unsigned long long *>(keys), values, keys_b, vals_b, count, begin_bit,
-                                end_bit, scratch, kNoAllocSortBytes, flags, &in_b, stream);
+    /* the status word keeps the previous call's value: clear it.  The launcher clears the
+     * histograms, tile counters and lookback table itself. */
+    err = cudaMemsetAsync(flags, 0, sizeof(uint32_t), stream);
+    if(err == cudaSuccess)
+        err = gsx_launch_sort_pairs(reinterpret_cast<unsigned long long *>(keys), values, keys_b, vals_b, count,
+                                    begin_bit, end_bit, scratch, kNoAllocSortBytes, flags, &in_b, stream);
     if(err == cudaSuccess && in_b) {
         err = cudaMemcpyAsync(keys, keys_b, sizeof(uint64_t) * count, cudaMemcpyDeviceToDevice, stream);
         if(err == cudaSuccess)
             err = cudaMemcpyAsync(values, vals_b, sizeof(uint32_t) * count, cudaMemcpyDeviceToDevice, stream);
     }
+    /* read the status word back (a copy into pageable host memory: returns once the sort is done) */
+    uint32_t status = 0;
+    if(err == cudaSuccess) err = cudaMemcpyAsync(&status, flags, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream);
+    if(err == cudaSuccess) err = cudaStreamSynchronize(stream);
     if(err != cudaSuccess) return gsx_internal_fail(GSX_B200_UNKNOWN, cudaGetErrorString(err));
+    if(status & GSX_FLAG_LOOKBACK_TIMEOUT)
+        return gsx_internal_fail(GSX_B200_UNKNOWN,
+                                 "gsx_b200_sort_pairs_noalloc: a decoupled-lookback wait timed out; the output order is invalid");
     return GSX_B200_SUCCESS;
 }

@@ -50,45 +50,111 @@ def shard_segments(field_ranges: dict, begin: int, end: int):
     return sorted(out, key=lambda s: s[1])
 
 
+class DeviceIpc:
+    """The device-memory and CUDA IPC calls the peer mapping needs (the C ABI).  A stand-in with the
+    same methods lets the host-side protocol run on CPU ranks (tests)."""
+
+    def alloc(self, nbytes: int) -> int:
+        raw = ctypes.c_void_p()
+        check(lib().gsx_b200_device_alloc(nbytes, ctypes.byref(raw)))
+        return raw.value
+
+    def handle(self, ptr: int) -> bytes:
+        h = (ctypes.c_ubyte * 64)()
+        check(lib().gsx_b200_ipc_handle(ctypes.c_void_p(ptr), h))
+        return bytes(h)
+
+    def open(self, handle: bytes) -> int:
+        p = ctypes.c_void_p()
+        check(lib().gsx_b200_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(handle), ctypes.byref(p)))
+        return p.value
+
+    def close(self, ptr: int) -> None:
+        lib().gsx_b200_ipc_close(ctypes.c_void_p(ptr))
+
+    def free(self, ptr: int) -> None:
+        lib().gsx_b200_device_free(ctypes.c_void_p(ptr))
+
+    def tensor(self, ptr: int, numel: int, device):
+        import torch
+        return torch.as_tensor(_CudaArray(ptr, numel), device=device)
+
+
 class PeerBuffers:
     """One flat f32 device buffer of `numel` elements per rank, every rank's buffer mapped into this
-    process.  `local` is this rank's buffer as a torch tensor; `ptrs[r]` is rank r's buffer here."""
+    process.  `local` is this rank's buffer as a torch tensor; `ptrs[r]` is rank r's buffer here.
+    Built by open_peer_buffers, which keeps every rank in step when a rank fails."""
 
-    def __init__(self, numel: int, group, device):
-        import torch
-        import torch.distributed as dist
-        self.world = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
-        raw = ctypes.c_void_p()
-        check(lib().gsx_b200_device_alloc(numel * 4, ctypes.byref(raw)))
-        self._own = raw.value
-        self.local = torch.as_tensor(_CudaArray(self._own, numel), device=device)
-        self.local.zero_()
-        h = (ctypes.c_ubyte * 64)()
-        check(lib().gsx_b200_ipc_handle(ctypes.c_void_p(self._own), h))
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(h), group=group)
-        self.ptrs, self._opened = [], []
-        for r, hb in enumerate(handles):
-            if r == self.rank:
-                self.ptrs.append(self._own)
-                continue
-            p = ctypes.c_void_p()
-            check(lib().gsx_b200_ipc_open((ctypes.c_ubyte * 64).from_buffer_copy(hb), ctypes.byref(p)))
-            self.ptrs.append(p.value)
-            self._opened.append(p.value)
+    def __init__(self, api, world: int, rank: int, own: int, local):
+        self.api, self.world, self.rank = api, world, rank
+        self._own, self.local = own, local
+        self.ptrs = [own if r == rank else None for r in range(world)]
+        self._opened = []
 
     def close_peers(self):
         """Unmap the other ranks' buffers (call on every rank before any rank frees its own)."""
         for p in self._opened:
-            lib().gsx_b200_ipc_close(ctypes.c_void_p(p))
+            self.api.close(p)
         self._opened = []
 
     def free(self):
         if self._own:
             self.local = None
-            lib().gsx_b200_device_free(ctypes.c_void_p(self._own))
+            self.api.free(self._own)
             self._own = None
+
+
+def _agree(ok: bool, group) -> bool:
+    """Every rank learns whether all ranks succeeded (one object all-gather; works on NCCL and gloo)."""
+    import torch.distributed as dist
+    flags = [None] * dist.get_world_size(group)
+    dist.all_gather_object(flags, bool(ok), group=group)
+    return all(flags)
+
+
+def open_peer_buffers(numel: int, group, device, count: int = 2, api=None):
+    """`count` PeerBuffers of `numel` f32 each, or (None, reason) on EVERY rank if any rank failed.
+
+    Every rank runs the same collectives in the same order whatever happens locally: stage 1 allocates
+    and exports IPC handles (a failed rank contributes None to the handle all-gather), stage 2 maps the
+    peers and agrees on the result.  On failure every rank unmaps what it opened, meets a barrier (so no
+    buffer is freed while a peer still maps it) and frees what it allocated."""
+    import torch.distributed as dist
+    api = api or DeviceIpc()
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    bufs, err = [], None
+    handles_mine = None
+    try:
+        for _ in range(count):
+            own = api.alloc(numel * 4)
+            bufs.append(PeerBuffers(api, world, rank, own, None))
+            bufs[-1].local = api.tensor(own, numel, device)
+            bufs[-1].local.zero_()
+        handles_mine = [api.handle(b._own) for b in bufs]
+    except Exception as e:  # noqa: BLE001 - reported through the all-gather below
+        err, handles_mine = e, None
+    every = [None] * world
+    dist.all_gather_object(every, handles_mine, group=group)
+    ok = all(h is not None for h in every)
+    if ok:
+        try:
+            for k, b in enumerate(bufs):
+                for r in range(world):
+                    if r != rank:
+                        p = api.open(every[r][k])
+                        b.ptrs[r] = p
+                        b._opened.append(p)
+        except Exception as e:  # noqa: BLE001 - agreed on below
+            err = e
+    ok = _agree(ok and err is None, group)
+    if ok:
+        return tuple(bufs), None
+    for b in bufs:
+        b.close_peers()
+    dist.barrier(group=group)
+    for b in bufs:
+        b.free()
+    return None, (str(err) if err is not None else "failed on another rank")
 
 
 class Segment(ctypes.Structure):

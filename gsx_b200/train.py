@@ -84,28 +84,14 @@ class Trainer:
             self.optim = Adam([ParamGroup(f, model.params[f], model.grads[f], lr[f]) for f in model.fields])
 
     def _setup_fused(self, model, group, device, lr):
-        """Peer-map the flat buffers and build the sharded optimizer.  Every rank reports whether its
-        setup worked (one all-reduce); if any rank failed (e.g. no peer access between two GPUs),
-        all ranks keep the NCCL exchange, so the ranks never disagree about the protocol."""
-        import torch
-        import torch.distributed as dist
-        from .dp import PeerBuffers, ShardedAdam
-        peer, err = None, None
-        try:
-            peer = (PeerBuffers(model.numel, group, device), PeerBuffers(model.numel, group, device))
-        except Exception as e:  # noqa: BLE001 - reported below, every rank falls back together
-            err = e
-        ok = torch.tensor([0.0 if err is not None else 1.0], device=device)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
-        if float(ok.item()) < 1.0:
-            if peer is not None:
-                for b in peer:
-                    b.close_peers()
-                dist.barrier(group=group)
-                for b in peer:
-                    b.free()
+        """Peer-map the flat buffers and build the sharded optimizer.  open_peer_buffers agrees on the
+        outcome across ranks (every rank runs the same collectives even when one fails locally), so if
+        any rank failed (e.g. no peer access between two GPUs) all ranks keep the NCCL exchange."""
+        from .dp import ShardedAdam, open_peer_buffers
+        peer, err = open_peer_buffers(model.numel, group, device, count=2)
+        if peer is None:
             import warnings
-            warnings.warn(f"fused NVLink exchange unavailable ({err or 'failed on another rank'}); using NCCL")
+            warnings.warn(f"fused NVLink exchange unavailable ({err}); using NCCL")
             return
         self._peer = peer
         model.rebind(peer[0].local, peer[1].local)

@@ -239,14 +239,15 @@ GSX_B200_API int gsx_b200_sort_pairs(gsx_b200_context *ctx, uint64_t *keys, uint
  * The same stable sort, for callers that cannot allocate device memory.  It has no counterpart in
  * the reference: it exists because some hosts own every device allocation themselves (GSX hands all
  * memory out of caller-owned arenas, and a plugin host that budgets GPU memory forbids hidden
- * cudaMalloc calls), and because cudaMalloc cannot be called while a CUDA graph is being captured.
- * keys/values are sorted in place; nothing is allocated: the scratch (alternate buffers, digit
- * histograms, lookback table) is one file-scope device array of about 14 MiB that every GPU which
- * loads this library keeps until the process exits.  count above GSX_B200_NOALLOC_SORT_MAX_PAIRS
- * is rejected with GSX_B200_OUT_OF_RANGE.  The first call on a device looks up the array's device
- * address (once per device, with that device current), so make that first call before starting any
- * stream capture.  All calls share the one array: calls that overlap on the GPU (other streams or
- * other host threads on the same device) race, so serialise them.
+ * cudaMalloc calls).  keys/values are sorted in place; nothing is allocated: the scratch (alternate
+ * buffers, digit histograms, lookback table, one status word) is one file-scope device array of
+ * about 14 MiB that every GPU which loads this library keeps until the process exits.  count above
+ * GSX_B200_NOALLOC_SORT_MAX_PAIRS is rejected with GSX_B200_OUT_OF_RANGE.  The first call on a
+ * device looks up the array's device address (once per device, with that device current).  Each
+ * call clears the status word, sorts, and reads the status word back, so it returns only once the
+ * sort has finished on `stream`; a timed-out lookback wait returns GSX_B200_UNKNOWN.  All calls
+ * share the one array: calls that overlap on the GPU (other streams or other host threads on the
+ * same device) race, so serialise them.
  */
 #define GSX_B200_NOALLOC_SORT_MAX_PAIRS (1u << 20)
 GSX_B200_API int gsx_b200_sort_pairs_noalloc(uint64_t *keys, uint32_t *values, uint64_t count, int32_t begin_bit,

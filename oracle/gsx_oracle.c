@@ -13,7 +13,7 @@
  * sources (oracle/Makefile.ref); the render path against the reference's own known answers
  * (tests/test_oracle_pins.py) and, on the GPU box, against the reference CUDA backend.
  *
- * Deliberate deviation (documented in DESIGN.md): depth ties between different Gaussians are
+ * Deliberate deviation: depth ties between different Gaussians are
  * broken by primitive index.  The reference breaks them by atomic compaction order
  * (kernels_forward.cuh:433-436), which is nondeterministic.
  */

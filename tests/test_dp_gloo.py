@@ -162,3 +162,83 @@ def test_shards_cover_the_flat_space(numel, world):
             assert ranges[f][0] <= lo < hi <= ranges[f][1] and b <= lo and hi <= e
             covered += hi - lo
     assert covered == numel
+
+
+class _FakeIpc:
+    """Host stand-in for the device/IPC calls of gsx_b200.dp.open_peer_buffers: CPU tensors as
+    'device buffers', integer ids as pointers and handles.  `fail` = (stage, rank) makes that call
+    raise on that rank only."""
+
+    def __init__(self, rank, fail):
+        self.rank, self.fail = rank, fail
+        self.live, self.opened, self.next = {}, set(), 1000 * (rank + 1)
+
+    def _maybe_fail(self, stage):
+        if self.fail == (stage, self.rank):
+            raise RuntimeError(f"injected {stage} failure on rank {self.rank}")
+
+    def alloc(self, nbytes):
+        self._maybe_fail("alloc")
+        self.next += 1
+        self.live[self.next] = torch.zeros(nbytes // 4)
+        return self.next
+
+    def handle(self, ptr):
+        return int(ptr).to_bytes(8, "little")
+
+    def open(self, handle):
+        self._maybe_fail("open")
+        p = int.from_bytes(handle, "little") + 10**6
+        self.opened.add(p)
+        return p
+
+    def close(self, ptr):
+        self.opened.remove(ptr)
+
+    def free(self, ptr):
+        del self.live[ptr]
+
+    def tensor(self, ptr, numel, device):
+        return self.live[ptr][:numel]
+
+
+def _peer_worker(rank, world, port, fail, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        from gsx_b200.dp import open_peer_buffers
+        api = _FakeIpc(rank, fail)
+        bufs, err = open_peer_buffers(64, dist.group.WORLD, "cpu", count=2, api=api)
+        # a collective after the setup: every rank must still be in step
+        t = torch.ones(1)
+        dist.all_reduce(t)
+        ptrs = [list(b.ptrs) for b in bufs] if bufs else None
+        out.put((rank, bufs is not None, err, len(api.live), len(api.opened), float(t.item()), ptrs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail", [None, ("alloc", 1), ("open", 1), ("open", 0)])
+def test_peer_mapping_failure_on_one_rank_falls_back_on_every_rank(fail):
+    """A failure of the allocation or of a peer mapping on ONE rank: every rank still runs the same
+    collectives, every rank returns no buffers (NCCL fallback), releases what it mapped and allocated,
+    and the next collective completes (no mismatched collectives, no hang)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, fail, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok, err, live, opened, total, ptrs in res:
+        assert total == world
+        if fail is None:
+            assert ok and err is None and live == 2 and opened == 2 * (world - 1)
+            assert all(None not in p for p in ptrs)
+        else:
+            assert not ok and err and live == 0 and opened == 0, (rank, err, live, opened)

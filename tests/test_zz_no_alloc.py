@@ -1,8 +1,8 @@
 """The allocation-free sort entry point, checked against the regular one through the C ABI.
 
 gsx_b200_sort_pairs_noalloc is for callers that must not allocate device memory themselves: a host
-that hands out every device buffer from its own arenas (GSX's model), or code running while a CUDA
-graph is being captured, where cudaMalloc cannot be called.  Its scratch is one static device array,
+that hands out every device buffer from its own arenas (GSX's model), or a plugin host with a fixed
+GPU memory budget that forbids hidden cudaMalloc calls.  Its scratch is one static device array,
 so it sorts at most GSX_B200_NOALLOC_SORT_MAX_PAIRS pairs per call.  This file is named to be
 collected last: it must pass alone in a fresh process and after every other test.
 """
