@@ -113,6 +113,17 @@ class RenderContext:
         check(lib().gsx_b200_render_bind_aux(self.handle, _ptr(visible_counter), _ptr(max_screen_radius),
                                              _ptr(grad_acc), _ptr(absgrad_acc)))
 
+    def set_train_state(self, borrowed: bool):
+        """False (default): the TRAIN forward's state is retained and the caller must not change the
+        Gaussians before the backward.  True: GSX's borrowed train state; the backward re-renders if the
+        Gaussians changed since the forward (gsx_b200_context_set_train_state)."""
+        check(lib().gsx_b200_context_set_train_state(self.handle, 1 if borrowed else 0))
+
+    def train_refreshes(self) -> int:
+        c = ctypes.c_uint64()
+        check(lib().gsx_b200_context_train_refreshes(self.handle, ctypes.byref(c)))
+        return int(c.value)
+
     def launch_count(self) -> int:
         """Kernels this context has launched since it was created (host-side count)."""
         c = ctypes.c_uint64()

@@ -154,6 +154,14 @@ struct gsx_b200_context {
     uint64_t launches = 0; /* kernels launched by this context (host-side count) */
     /* retained forward state */
     bool has_train = false;
+    /* borrowed train state (gsx_b200_context_set_train_state): what a refresh needs to re-render, and
+     * the inputs' fingerprints at the forward ([0]) and at the backward ([1]) */
+    int train_state = GSX_B200_TRAIN_STATE_RETAINED;
+    gsx_b200_camera saved_camera{};
+    int saved_rows[2] = { 0, 0 };
+    float saved_bg[3] = { 0.0f, 0.0f, 0.0f };
+    DevBuf fingerprint, refresh_rgb;
+    uint64_t refreshes = 0;
     /* bound ADC auxiliary accumulators (device [N] f32, NULL = not bound) */
     float *aux_visible = nullptr, *aux_radius = nullptr, *aux_grad = nullptr, *aux_absgrad = nullptr;
     gsx_b200_gaussians g{};
@@ -242,7 +250,8 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     cudaDeviceSynchronize();
     DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->tile_masks, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
-                      &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->tile_aux, &ctx->words, &ctx->hist };
+                      &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->tile_aux, &ctx->words, &ctx->hist,
+                      &ctx->fingerprint, &ctx->refresh_rgb };
     for(DevBuf *b : all) release(*b);
     if(ctx->ev_created)
         for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
@@ -262,6 +271,22 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
 }
 
 namespace {
+
+/* fingerprint of the retained Gaussian inputs (ctx->g) into ctx->fingerprint word `slot` */
+int launch_fingerprint(gsx_b200_context *ctx, int slot, cudaStream_t stream)
+{
+    if(int rc = ensure(ctx->fingerprint, 2 * sizeof(unsigned long long))) return rc;
+    const gsx_b200_gaussians &g = ctx->g;
+    const uint64_t n = (uint64_t)g.count;
+    const float *fields[8] = { g.mean3d, g.rotation, g.logscale, g.opacity, g.sh0,
+                               ctx->sh_degree >= 1 ? g.sh1 : nullptr, ctx->sh_degree >= 2 ? g.sh2 : nullptr,
+                               ctx->sh_degree >= 3 ? g.sh3 : nullptr };
+    const uint64_t counts[8] = { 3 * n, 4 * n, 3 * n, n, 3 * n, 9 * n, 15 * n, 21 * n };
+    GSX_CUDA_TRY(gsx_launch_fingerprint(fields, counts, 8, (unsigned long long *)ctx->fingerprint.ptr + slot, stream),
+                 "fingerprint launch");
+    ctx->launches += 5 + (uint64_t)ctx->sh_degree;
+    return 0;
+}
 
 int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int sh_degree, const gsx_b200_camera *camera,
                         int row_begin, int row_end, const float background[3], int forward_type, void *out_rgb,
@@ -467,8 +492,51 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         ctx->has_train = true;
         ctx->g = *g;
         ctx->sh_degree = sh_degree;
+        if(ctx->train_state == GSX_B200_TRAIN_STATE_BORROWED) {
+            /* keep what a refresh re-renders with, and fingerprint the borrowed inputs */
+            ctx->saved_camera = *camera;
+            ctx->saved_rows[0] = row_begin;
+            ctx->saved_rows[1] = row_end;
+            memcpy(ctx->saved_bg, bg, sizeof(bg));
+            if(int rc = launch_fingerprint(ctx, 0, stream)) {
+                ctx->has_train = false;
+                return rc;
+            }
+        }
     }
     return 0;
+}
+
+/* Borrowed train state: the backward of the CURRENT inputs, as gsx-cuda/render.c:662-756 refreshes a
+ * borrowed TRAIN state.  The inputs are fingerprinted again; if they differ from the forward's, the TRAIN
+ * forward is re-run on them (into a private image, without touching the density-control statistics)
+ * before the backward uses the retained state.  Unchanged inputs cost one read of the fields and one
+ * host wait. */
+int refresh_borrowed(gsx_b200_context *ctx, cudaStream_t stream)
+{
+    if(ctx->g.count == 0) return 0;
+    if(int rc = launch_fingerprint(ctx, 1, stream)) return rc;
+    unsigned long long *h = reinterpret_cast<unsigned long long *>(ctx->host_words + 8);
+    GSX_CUDA_TRY(cudaMemcpyAsync(h, ctx->fingerprint.ptr, 2 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, stream),
+                 "D2H");
+    GSX_CUDA_TRY(cudaStreamSynchronize(stream), "fingerprint read-back");
+    if(h[0] == h[1]) return 0;
+    const gsx_b200_gaussians g = ctx->g;
+    const gsx_b200_camera cam = ctx->saved_camera;
+    const int r0 = ctx->saved_rows[0], r1 = ctx->saved_rows[1];
+    float bg[3];
+    memcpy(bg, ctx->saved_bg, sizeof(bg));
+    const size_t P = (size_t)cam.width * (size_t)(r1 - r0);
+    if(int rc = ensure(ctx->refresh_rgb, 3 * sizeof(float) * P)) return rc;
+    float *keep_visible = ctx->aux_visible, *keep_radius = ctx->aux_radius;
+    ctx->aux_visible = nullptr;
+    ctx->aux_radius = nullptr;
+    const int rc = render_forward_impl(ctx, &g, ctx->sh_degree, &cam, r0, r1, bg, GSX_B200_FORWARD_TRAIN,
+                                       ctx->refresh_rgb.ptr, false, stream);
+    ctx->aux_visible = keep_visible;
+    ctx->aux_radius = keep_radius;
+    if(rc == 0) ++ctx->refreshes;
+    return rc;
 }
 
 } // namespace
@@ -508,6 +576,8 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
     GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
     cudaStream_t stream = (cudaStream_t)stream_;
     if(n == 0) return 0;
+    if(ctx->train_state == GSX_B200_TRAIN_STATE_BORROWED)
+        if(int rc = refresh_borrowed(ctx, stream)) return rc;
     const unsigned long long *keys_a = (const unsigned long long *)ctx->keys.ptr;
     (void)keys_a;
     const uint32_t *vals_a = (const uint32_t *)ctx->vals.ptr;
@@ -542,6 +612,23 @@ int gsx_b200_render_bind_aux(gsx_b200_context *ctx, float *visible_counter, floa
     ctx->aux_radius = max_screen_radius;
     ctx->aux_grad = grad_acc;
     ctx->aux_absgrad = absgrad_acc;
+    return 0;
+}
+
+int gsx_b200_context_set_train_state(gsx_b200_context *ctx, int mode)
+{
+    if(ctx == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx must be non-null");
+    if(mode != GSX_B200_TRAIN_STATE_RETAINED && mode != GSX_B200_TRAIN_STATE_BORROWED)
+        return fail(GSX_B200_OUT_OF_RANGE, "mode must be GSX_B200_TRAIN_STATE_RETAINED or _BORROWED");
+    if(mode != ctx->train_state) ctx->has_train = false; /* a retained forward belongs to the mode it ran in */
+    ctx->train_state = mode;
+    return 0;
+}
+
+int gsx_b200_context_train_refreshes(gsx_b200_context *ctx, uint64_t *out_count)
+{
+    if(ctx == nullptr || out_count == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "ctx and out_count must be non-null");
+    *out_count = ctx->refreshes;
     return 0;
 }
 

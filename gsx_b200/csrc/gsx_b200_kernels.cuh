@@ -188,6 +188,9 @@ cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rot
                                            float *grad_norm_acc, float *absgrad_norm_acc,
                                            cudaStream_t stream);
 
+cudaError_t gsx_launch_fingerprint(const float *const *fields, const uint64_t *counts, int n_fields, unsigned long long *out,
+                                   cudaStream_t stream);
+
 #define GSX_ADAM_MAX_GROUPS 16
 struct AdamGroupDev {
     float *param;

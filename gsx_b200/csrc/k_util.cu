@@ -37,6 +37,26 @@ __global__ void __launch_bounds__(kThreads) count_nonfinite_kernel(const float *
     if((threadIdx.x & 31) == 0 && local) atomicAdd(count, local);
 }
 
+/* splitmix64 finaliser: a bijective 64-bit mix */
+__device__ __forceinline__ unsigned long long mix64(unsigned long long z)
+{
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+/* out += sum over i of mix64(word_i ^ (salt + i * golden)): changing any word (or moving it) changes
+ * its term, so the sum changes unless two 64-bit mixes collide */
+__global__ void __launch_bounds__(kThreads) fingerprint_kernel(const uint32_t *__restrict__ x, uint64_t n,
+                                                                unsigned long long salt, unsigned long long *out)
+{
+    unsigned long long acc = 0;
+    for(uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (uint64_t)gridDim.x * kThreads)
+        acc += mix64((unsigned long long)__ldg(x + i) ^ (salt + i * 0x9e3779b97f4a7c15ull));
+    for(int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if((threadIdx.x & 31) == 0) atomicAdd(out, acc);
+}
+
 unsigned grid_for(uint64_t n)
 {
     const uint64_t b = (n + kThreads - 1) / kThreads;
@@ -85,4 +105,20 @@ extern "C" int gsx_b200_count_nonfinite_f32(const float *x, uint64_t n, uint32_t
     const cudaError_t err = cudaGetLastError();
     if(err != cudaSuccess) return gsx_internal_fail(GSX_B200_UNKNOWN, cudaGetErrorString(err));
     return GSX_B200_SUCCESS;
+}
+
+/* 64-bit fingerprint of the Gaussian fields (mean3d, rotation, logscale, opacity, sh0, and sh1..sh3
+ * up to sh_degree) into *out (device): one streaming pass, used to detect inputs changed between a
+ * borrowed TRAIN forward and its backward. */
+cudaError_t gsx_launch_fingerprint(const float *const *fields, const uint64_t *counts, int n_fields, unsigned long long *out,
+                                   cudaStream_t stream)
+{
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(unsigned long long), stream);
+    for(int f = 0; f < n_fields && e == cudaSuccess; ++f) {
+        if(fields[f] == nullptr || counts[f] == 0) continue;
+        fingerprint_kernel<<<grid_for(counts[f]), kThreads, 0, stream>>>(reinterpret_cast<const uint32_t *>(fields[f]),
+                                                                         counts[f], 0x51ed270b27a1f5c3ull * (f + 1), out);
+        e = cudaGetLastError();
+    }
+    return e;
 }

@@ -646,6 +646,12 @@ static gsx_error b200_renderer_render(gsx_renderer_t renderer, gsx_render_contex
         /* density-control statistics of a TRAIN forward (gsx-render.h:123-124) */
         rc = gsx_b200_render_bind_aux(c->ctx, b200_tensor_f32(r->gs_visible_counter), b200_tensor_f32(r->gs_max_screen_radius),
                                       NULL, NULL);
+        /* borrowed TRAIN state: the backward re-renders if the caller changed the Gaussians in between
+         * (gsx-cuda/render.c:662-756); cloned state: the copies above are what the backward reads */
+        if(rc == 0)
+            rc = gsx_b200_context_set_train_state(c->ctx, ft == GSX_B200_FORWARD_TRAIN && r->borrow_train_state
+                                                              ? GSX_B200_TRAIN_STATE_BORROWED
+                                                              : GSX_B200_TRAIN_STATE_RETAINED);
         if(rc == 0) rc = gsx_b200_render_forward(c->ctx, &g, (int)r->sh_degree, &cam, bg, ft, out, be->stream);
     }
     if(rc != 0) return b200_lib_error(rc, "gsx_b200_render_forward failed");

@@ -175,6 +175,24 @@ GSX_B200_API int gsx_b200_context_check(gsx_b200_context *ctx, void *stream);
 GSX_B200_API int gsx_b200_render_bind_aux(gsx_b200_context *ctx, float *visible_counter, float *max_screen_radius,
                              float *grad_acc, float *absgrad_acc);
 
+/*
+ * How a TRAIN forward's state is kept for its backward (gsx_render_forward_request.borrow_train_state,
+ * gsx-render.h; gsx-cuda/render.c:481-756).
+ * RETAINED (default): the context keeps the forward's intermediates and the Gaussian pointers; the
+ *   caller must not change the Gaussians between the TRAIN forward and its backward (or must pass
+ *   private copies, as GSX's cloned train state does).  No extra work per step.
+ * BORROWED: the reference's borrowed state.  The forward also records a 64-bit fingerprint of the
+ *   Gaussian fields; the backward fingerprints them again (one read of the fields and one wait for the
+ *   stream) and, if they changed, re-runs the TRAIN forward on the current fields before the backward,
+ *   so the gradients are those of the current inputs, as the reference's refresh gives them.  The
+ *   re-run writes a private image (not the caller's out_rgb) and leaves the density-control statistics
+ *   alone.  Switching the mode drops a retained forward.
+ */
+enum { GSX_B200_TRAIN_STATE_RETAINED = 0, GSX_B200_TRAIN_STATE_BORROWED = 1 };
+GSX_B200_API int gsx_b200_context_set_train_state(gsx_b200_context *ctx, int mode);
+/* Number of borrowed-state refreshes (re-run TRAIN forwards) ctx has done. */
+GSX_B200_API int gsx_b200_context_train_refreshes(gsx_b200_context *ctx, uint64_t *out_count);
+
 /* Number of kernels ctx has launched since it was created (a host-side count, for benchmarks). */
 GSX_B200_API int gsx_b200_context_launch_count(gsx_b200_context *ctx, uint64_t *out_count);
 

@@ -18,6 +18,9 @@
  * (kernels_forward.cuh:433-436), which is nondeterministic.
  */
 #include "../gsx_b200/csrc/gsx_detmath.h"
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #include <stdint.h>
 #include <stdlib.h>
@@ -174,6 +177,7 @@ static uint64_t orc_preprocess_impl(int64_t n, const float *mean3d, const float 
     const float W = (float)cam->width, H = (float)cam->height;
     const int bases = (sh_degree + 1) * (sh_degree + 1);
     uint64_t total = 0;
+#pragma omp parallel for schedule(static, 4096) reduction(+ : total)
     for(int64_t i = 0; i < n; ++i) {
         n_touched[i] = 0;
         const float m[3] = { mean3d[i * 3 + 0], mean3d[i * 3 + 1], mean3d[i * 3 + 2] };
@@ -366,9 +370,11 @@ void orc_blend_forward(int width, int height, const uint32_t *ranges, const uint
 {
     const int gw = (width + ORC_TILE - 1) / ORC_TILE, gh = (height + ORC_TILE - 1) / ORC_TILE;
     const size_t P = (size_t)width * (size_t)height;
-    for(int ty = 0; ty < gh; ++ty) {
-        for(int tx = 0; tx < gw; ++tx) {
-            const int tile = ty * gw + tx;
+    /* tiles are independent (every output is per pixel or per tile): parallel over tiles */
+#pragma omp parallel for schedule(dynamic, 4)
+    for(int tile = 0; tile < gw * gh; ++tile) {
+        {
+            const int ty = tile / gw, tx = tile % gw;
             const uint32_t r0 = ranges[tile * 2 + 0], r1 = ranges[tile * 2 + 1];
             uint32_t tmax = 0;
             for(int ly = 0; ly < ORC_TILE; ++ly) {
@@ -420,17 +426,17 @@ void orc_blend_forward(int width, int height, const uint32_t *ranges, const uint
 static int orc_backward_consistent = 0;
 void orc_set_backward_consistent(int v) { orc_backward_consistent = v; }
 
-static void orc_blend_backward_impl(int width, int height, const uint32_t *ranges, const uint32_t *vals,
+static void orc_blend_backward_tile(int tile, int width, int height, const uint32_t *ranges, const uint32_t *vals,
                                     const float *mean2d, const float *conic_op, const float *color, const float *image,
                                     const uint32_t *n_contrib, const uint32_t *tile_max, const float *grad_rgb,
                                     float *d_mean2d, float *d_conic, float *d_opacity_raw, float *d_color,
                                     float *d_mean2d_abs)
 {
-    const int gw = (width + ORC_TILE - 1) / ORC_TILE, gh = (height + ORC_TILE - 1) / ORC_TILE;
+    const int gw = (width + ORC_TILE - 1) / ORC_TILE;
     const size_t P = (size_t)width * (size_t)height;
-    for(int ty = 0; ty < gh; ++ty) {
-        for(int tx = 0; tx < gw; ++tx) {
-            const int tile = ty * gw + tx;
+    {
+        {
+            const int ty = tile / gw, tx = tile % gw;
             const uint32_t r0 = ranges[tile * 2 + 0], r1 = ranges[tile * 2 + 1];
             const uint32_t n_inst = r1 - r0;
             for(int ly = 0; ly < ORC_TILE; ++ly) {
@@ -524,6 +530,59 @@ static void orc_blend_backward_impl(int width, int height, const uint32_t *range
     }
 }
 
+/* Tiles in parallel; each thread accumulates into its own gradient arrays, summed in thread order
+ * at the end (the summation order differs from a serial walk by rounding only). */
+static void orc_blend_backward_impl(int width, int height, const uint32_t *ranges, const uint32_t *vals,
+                                    const float *mean2d, const float *conic_op, const float *color, const float *image,
+                                    const uint32_t *n_contrib, const uint32_t *tile_max, const float *grad_rgb,
+                                    float *d_mean2d, float *d_conic, float *d_opacity_raw, float *d_color,
+                                    float *d_mean2d_abs)
+{
+    const int n_tiles = ((width + ORC_TILE - 1) / ORC_TILE) * ((height + ORC_TILE - 1) / ORC_TILE);
+    /* primitive count bound: the largest index referenced + 1 */
+    int64_t n = 0;
+    const uint64_t total = n_tiles > 0 ? ranges[(size_t)(n_tiles - 1) * 2 + 1] : 0;
+    for(int t = 0; t < n_tiles; ++t)
+        for(uint32_t j = ranges[t * 2]; j < ranges[t * 2 + 1]; ++j)
+            if((int64_t)vals[j] + 1 > n) n = (int64_t)vals[j] + 1;
+    (void)total;
+    int nt = 1;
+#ifdef _OPENMP
+    nt = omp_get_max_threads();
+#endif
+    const size_t per = (size_t)n * (d_mean2d_abs ? 11 : 9);
+    float *priv = nt > 1 && n > 0 ? (float *)calloc((size_t)nt * per, sizeof(float)) : NULL;
+    if(priv == NULL) {
+        for(int t = 0; t < n_tiles; ++t)
+            orc_blend_backward_tile(t, width, height, ranges, vals, mean2d, conic_op, color, image, n_contrib, tile_max,
+                                    grad_rgb, d_mean2d, d_conic, d_opacity_raw, d_color, d_mean2d_abs);
+        return;
+    }
+#pragma omp parallel num_threads(nt)
+    {
+        int me = 0;
+#ifdef _OPENMP
+        me = omp_get_thread_num();
+#endif
+        float *b = priv + (size_t)me * per;
+        float *pm = b, *pc = b + 2 * n, *po = b + 5 * n, *pcol = b + 6 * n, *pabs = d_mean2d_abs ? b + 9 * n : NULL;
+#pragma omp for schedule(dynamic, 2)
+        for(int t = 0; t < n_tiles; ++t)
+            orc_blend_backward_tile(t, width, height, ranges, vals, mean2d, conic_op, color, image, n_contrib, tile_max,
+                                    grad_rgb, pm, pc, po, pcol, pabs);
+    }
+    for(int k = 0; k < nt; ++k) {
+        const float *b = priv + (size_t)k * per;
+        for(int64_t i = 0; i < 2 * n; ++i) d_mean2d[i] += b[i];
+        for(int64_t i = 0; i < 3 * n; ++i) d_conic[i] += b[2 * n + i];
+        for(int64_t i = 0; i < n; ++i) d_opacity_raw[i] += b[5 * n + i];
+        for(int64_t i = 0; i < 3 * n; ++i) d_color[i] += b[6 * n + i];
+        if(d_mean2d_abs)
+            for(int64_t i = 0; i < 2 * n; ++i) d_mean2d_abs[i] += b[9 * n + i];
+    }
+    free(priv);
+}
+
 void orc_blend_backward(int width, int height, const uint32_t *ranges, const uint32_t *vals, const float *mean2d,
                         const float *conic_op, const float *color, const float *image, const uint32_t *n_contrib,
                         const uint32_t *tile_max, const float *grad_rgb, float *d_mean2d, float *d_conic,
@@ -557,6 +616,7 @@ void orc_preprocess_backward(int64_t n, const float *mean3d, const float *rotati
     const float *w = cam->w2c;
     const float W = (float)cam->width, H = (float)cam->height;
     const int bases = (sh_degree + 1) * (sh_degree + 1);
+#pragma omp parallel for schedule(static, 4096)
     for(int64_t i = 0; i < n; ++i) {
         memset(g_mean3d + i * 3, 0, 12);
         memset(g_rotation + i * 4, 0, 16);
@@ -764,6 +824,8 @@ int orc_ssim(int64_t outer, int channels, int height, int width, const float *p,
         for(int c = 0; c < channels; ++c) {
             const size_t base = ((size_t)o * (size_t)channels + (size_t)c) * plane;
             const float *P = p + base, *Tt = t + base;
+            /* rows in parallel; every output and partial is per pixel */
+#pragma omp parallel for schedule(static, 8)
             for(int y = 0; y < height; ++y) {
                 for(int x = 0; x < width; ++x) {
                     double mu1 = 0, mu2 = 0, s11 = 0, s22 = 0, s12 = 0;
@@ -799,6 +861,7 @@ int orc_ssim(int64_t outer, int channels, int height, int width, const float *p,
                 }
             }
             if(grad) {
+#pragma omp parallel for schedule(static, 8)
                 for(int y = 0; y < height; ++y) {
                     for(int x = 0; x < width; ++x) {
                         double c0 = 0, c1 = 0, c2 = 0;
@@ -831,6 +894,7 @@ int orc_ssim(int64_t outer, int channels, int height, int width, const float *p,
 void orc_adam(int64_t n, float *param, const float *grad, float *m1, float *m2, float beta1, float beta2, float lr,
               float weight_decay, float eps, float max_grad, double inv_c1, double inv_c2)
 {
+#pragma omp parallel for schedule(static, 65536)
     for(int64_t i = 0; i < n; ++i) {
         float g = grad[i];
         if(max_grad > 0.0f) {

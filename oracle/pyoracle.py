@@ -335,6 +335,22 @@ class RefSession:
         res = {self.FIELDS[f]: grads[f] for f in range(nf)}
         return out.reshape(3, self.cam.height, self.cam.width), res
 
+    def set_borrow(self, on=True):
+        """TRAIN requests borrow the Gaussian tensors (borrow_train_state) instead of cloning them."""
+        _ref_check(self.L, self.L.refdrv_session_set_borrow(self.h, 1 if on else 0))
+
+    def mutate_backward(self, grad_rgb, mutated: dict):
+        """TRAIN forward, overwrite the fields in `mutated` (numpy arrays), then the backward of grad_rgb;
+        returns the parameter gradients (the ordering of the reference's train-state tests)."""
+        cols = (3, 3, 4, 1, 3, 9, 15, 21)
+        nf = 5 + self.sh_degree
+        keep = [_f32(mutated[self.FIELDS[f]]).reshape(-1) if self.FIELDS[f] in mutated else None for f in range(nf)]
+        mp = (F32P * nf)(*[_p(x) if x is not None else None for x in keep])
+        grads = [np.zeros(self.n * cols[f], np.float32) for f in range(nf)]
+        arr = (F32P * nf)(*[_p(x) for x in grads])
+        _ref_check(self.L, self.L.refdrv_session_mutate_backward(self.h, _p(_f32(grad_rgb).reshape(-1)), mp, arr))
+        return {self.FIELDS[f]: grads[f] for f in range(nf)}
+
     def step(self, l1_weight=0.8, ssim_weight=0.2):
         sec = ctypes.c_double()
         _ref_check(self.L, self.L.refdrv_session_step(self.h, ctypes.c_float(l1_weight), ctypes.c_float(ssim_weight),

@@ -89,6 +89,7 @@ typedef struct refdrv_session {
     gsx_tensor_t out_rgb, target, loss_map, grad_rgb;
     gsx_tensor_t aux[4]; /* visible_counter, max_screen_radius, grad_acc, absgrad_acc ([N] f32) */
     int aux_on;
+    int borrow; /* borrow_train_state of TRAIN requests */
     gsx_camera_intrinsics intr;
     gsx_camera_pose pose;
     float near_plane, far_plane, bg[3];
@@ -217,7 +218,7 @@ static void refdrv_fill_forward(refdrv_session *s, gsx_render_forward_request *r
     rq->precision = GSX_RENDER_PRECISION_FLOAT32;
     rq->sh_degree = s->sh_degree;
     rq->forward_type = type;
-    rq->borrow_train_state = false;
+    rq->borrow_train_state = type == GSX_RENDER_FORWARD_TYPE_TRAIN && s->borrow;
     rq->gs_mean3d = s->params[0];
     rq->gs_logscale = s->params[1];
     rq->gs_rotation = s->params[2];
@@ -237,6 +238,13 @@ static void refdrv_fill_forward(refdrv_session *s, gsx_render_forward_request *r
 int refdrv_session_enable_aux(refdrv_session *s, int on)
 {
     s->aux_on = on;
+    return 0;
+}
+
+/* TRAIN requests borrow (on != 0) or clone (on == 0, the default) the Gaussian inputs. */
+int refdrv_session_set_borrow(refdrv_session *s, int on)
+{
+    s->borrow = on;
     return 0;
 }
 
@@ -275,6 +283,42 @@ int refdrv_session_render_backward(refdrv_session *s, const float *grad_rgb, flo
     }
     REF_CHECK(gsx_renderer_backward(s->renderer, s->rctx, &bq));
     REF_CHECK(gsx_tensor_download(s->out_rgb, out_rgb, (gsx_size_t)3 * s->width * s->height * 4));
+    for(int f = 0; f < s->n_fields; ++f) {
+        gsx_size_t bytes = 0;
+        REF_CHECK(gsx_tensor_get_size_bytes(s->grads[f], &bytes));
+        REF_CHECK(gsx_tensor_download(s->grads[f], grad_out[f], bytes));
+    }
+    return 0;
+}
+
+/* TRAIN forward, then the caller's tensors are overwritten with mutated[f] (host, NULL = unchanged),
+ * then the backward of grad_rgb: the ordering of the reference tests BackwardUsesRetainedTrainState and
+ * BackwardBorrowedTrainStateTracksInputMutations (tests/cuda_render_runtime.cpp:601-689).  Downloads
+ * the parameter gradients in field order. */
+int refdrv_session_mutate_backward(refdrv_session *s, const float *grad_rgb, const float **mutated, float **grad_out)
+{
+    gsx_render_forward_request rq;
+    gsx_render_backward_request bq;
+    refdrv_fill_forward(s, &rq, GSX_RENDER_FORWARD_TYPE_TRAIN);
+    REF_CHECK(gsx_renderer_render(s->renderer, s->rctx, &rq));
+    for(int f = 0; f < s->n_fields; ++f) {
+        if(mutated[f] == NULL) continue;
+        gsx_size_t bytes = 0;
+        REF_CHECK(gsx_tensor_get_size_bytes(s->params[f], &bytes));
+        REF_CHECK(gsx_tensor_upload(s->params[f], mutated[f], bytes));
+    }
+    REF_CHECK(gsx_tensor_upload(s->grad_rgb, grad_rgb, (gsx_size_t)3 * s->width * s->height * 4));
+    memset(&bq, 0, sizeof(bq));
+    bq.grad_rgb = s->grad_rgb;
+    bq.grad_gs_mean3d = s->grads[0];
+    bq.grad_gs_logscale = s->grads[1];
+    bq.grad_gs_rotation = s->grads[2];
+    bq.grad_gs_opacity = s->grads[3];
+    bq.grad_gs_sh0 = s->grads[4];
+    bq.grad_gs_sh1 = s->sh_degree >= 1 ? s->grads[5] : NULL;
+    bq.grad_gs_sh2 = s->sh_degree >= 2 ? s->grads[6] : NULL;
+    bq.grad_gs_sh3 = s->sh_degree >= 3 ? s->grads[7] : NULL;
+    REF_CHECK(gsx_renderer_backward(s->renderer, s->rctx, &bq));
     for(int f = 0; f < s->n_fields; ++f) {
         gsx_size_t bytes = 0;
         REF_CHECK(gsx_tensor_get_size_bytes(s->grads[f], &bytes));

@@ -1,0 +1,209 @@
+"""Parity at the benchmarked configurations: the exact shapes bench.py times, against the CPU oracle.
+
+Every case uses the seeded generators of gsx_b200/scenes.py at full size:
+- config 2: 1M Gaussians, 1920x1080, two of the 64 orbit cameras (INFERENCE);
+- config 3: 3M Gaussians (2M volume + 1M slab), 1245x825, one view, TRAIN forward, the fused L1+SSIM
+  gradient against the teacher render, and the backward of that gradient;
+- config 4: one tile-row band (band 3 of 8) of the 10M-Gaussian 3840x2160 frame, f32 and bf16;
+- config 5 shapes: fused SSIM+L1 at 1080p and 4K with batch 1 and 8, Adam over 20M Gaussians x 14
+  floats, and a 200M-pair radix sort (device-side property checks; no CPU sort of that size).
+
+Bars: tile keys, sort order, tile ranges and per-Gaussian offsets bit-exact;
+RGB within max-abs 1e-4 (and bit-identical under the arithmetic contract); gradients rel-L2 <= 1e-3
+per field; Adam bit-exact; SSIM+L1 loss map max-abs 2e-5 and gradient rel-L2 1e-4 against the fp64
+SSIM oracle (the same bars as the small-shape loss tests).
+"""
+import numpy as np
+import pytest
+import torch
+
+import gsx_b200 as gb
+from gsx_b200 import scenes
+from oracle import pyoracle as po
+from tests.gpu_helpers import fetch_view, rel_l2, render, to_dev
+
+pytestmark = pytest.mark.gpu
+
+RGB_TOL = 1e-4
+GRAD_TOL = 1e-3
+
+
+def _ocam(cam):
+    return po.Camera(cam.width, cam.height, cam.fx, cam.fy, cam.cx, cam.cy, cam.rot_xyzw, cam.transl, cam.near_plane,
+                     cam.far_plane)
+
+
+def _assert_forward_exact(v, ref, n):
+    exp_offsets = np.concatenate([[0], np.cumsum(ref["n_touched"].astype(np.uint64))]).astype(np.uint32)
+    np.testing.assert_array_equal(v["offsets"], exp_offsets)
+    np.testing.assert_array_equal(v["keys"], ref["keys"])
+    np.testing.assert_array_equal(v["vals"], ref["vals"])
+    np.testing.assert_array_equal(v["ranges"], ref["ranges"])
+    np.testing.assert_array_equal(v["tile_max"], ref["tile_max"])
+
+
+@pytest.fixture(scope="module")
+def ctx(cuda_device):
+    c = gb.RenderContext(0)
+    yield c
+    c.close()
+
+
+# ------------------------------------------------------------------------------------------ config 2
+@pytest.mark.parametrize("cam_index", [0, 37])
+def test_config2_forward_bit_exact(ctx, cam_index):
+    g = scenes.config2_scene(0)
+    cam = scenes.config2_cameras()[cam_index]
+    ref = po.render_forward(g, _ocam(cam))
+    assert ref["n_instances"] > 500_000
+    gd = to_dev(g)
+    out = render(ctx, gd, cam, train=False)
+    ctx.check()
+    _assert_forward_exact(fetch_view(ctx, g["mean3d"].shape[0]), ref, g["mean3d"].shape[0])
+    rgb = out.cpu().numpy()
+    assert np.abs(rgb - ref["rgb"]).max() <= RGB_TOL
+    assert np.array_equal(rgb, ref["rgb"]), "arithmetic contract: expected bit-identical RGB"
+
+
+# ------------------------------------------------------------------------------------------ config 3
+def test_config3_training_step_matches_oracle(ctx):
+    g = scenes.config3_scene(0)
+    cam = scenes.config3_cameras()[0]
+    n = g["mean3d"].shape[0]
+    oc = _ocam(cam)
+    # the target: the seeded teacher's render from the same view (bench.py's targets)
+    teacher = to_dev(scenes.teacher(g))
+    target = render(ctx, teacher, cam, train=False)
+    ctx.check()
+    del teacher
+    ref = po.render_forward(g, oc)
+    gd = to_dev(g)
+    out = render(ctx, gd, cam, train=True)
+    ctx.check()
+    _assert_forward_exact(fetch_view(ctx, n), ref, n)
+    rgb = out.cpu().numpy()
+    assert np.array_equal(rgb, ref["rgb"]), "arithmetic contract: expected bit-identical RGB"
+    # fused L1 (0.8) + SSIM (0.2), MEAN normalisation, at the full 3x825x1245 image
+    lm = torch.zeros_like(out)
+    grad_rgb = torch.zeros_like(out)
+    gb.l1_ssim(out, target, lm, grad_rgb, 0.8, 0.2)
+    torch.cuda.synchronize()
+    ref_lm, ref_g = po.l1_ssim_train(rgb, target.cpu().numpy(), 0.8, 0.2)
+    assert np.abs(lm.cpu().numpy() - ref_lm).max() <= 2e-5
+    assert rel_l2(grad_rgb.cpu().numpy(), ref_g) <= 1e-4
+    # backward of the GPU's own image gradient, on both sides
+    grads = {k: torch.full_like(v, 123.0) for k, v in gd.items()}  # written, not accumulated
+    gb.Renderer(cam.width, cam.height).backward(ctx, grad_rgb, grads)
+    ctx.check()
+    ref_b = po.render_backward(g, oc, ref, grad_rgb.cpu().numpy())
+    for k in gd:
+        got = grads[k].cpu().numpy()
+        assert np.isfinite(got).all(), k
+        err = rel_l2(got, ref_b[k])
+        assert err <= GRAD_TOL, f"{k}: rel-L2 {err:.3e}"
+
+
+# ------------------------------------------------------------------------------------------ config 4
+def test_config4_band_matches_oracle_full_frame_rows(ctx):
+    g = scenes.config4_scene(0)
+    cam = scenes.config4_cameras()[0]
+    n = g["mean3d"].shape[0]
+    ref = po.render_forward(g, _ocam(cam))
+    r0, r1 = gb.band_rows(cam.height, 3, 8)
+    gd = to_dev(g)
+    del g
+    rend = gb.Renderer(cam.width, cam.height)
+    out = torch.empty((3, r1 - r0, cam.width), dtype=torch.float32, device="cuda:0")
+    rend.render_rows(ctx, gd, cam, r0, r1, out, forward_type=gb.FORWARD_INFERENCE)
+    ctx.check()
+    v = fetch_view(ctx, n)
+    # the band's keys are the full frame's keys of its tile rows, tile index shifted by the first row
+    gw = (cam.width + 15) // 16
+    t0, t1 = r0 // 16, (r1 + 15) // 16
+    tiles = (ref["keys"] >> np.uint64(32)).astype(np.int64)
+    sel = (tiles >= t0 * gw) & (tiles < t1 * gw)
+    assert sel.sum() > 100_000
+    np.testing.assert_array_equal(v["keys"], ref["keys"][sel] - (np.uint64(t0 * gw) << np.uint64(32)))
+    np.testing.assert_array_equal(v["vals"], ref["vals"][sel])
+    rgb = out.cpu().numpy()
+    exp = ref["rgb"][:, r0:r1, :]
+    assert np.abs(rgb - exp).max() <= RGB_TOL
+    assert np.array_equal(rgb, exp)
+    # bf16 storage: round-to-nearest-even of the f32 result, bit for bit
+    outb = torch.empty((3, r1 - r0, cam.width), dtype=torch.bfloat16, device="cuda:0")
+    rend.render_rows(ctx, gd, cam, r0, r1, outb, forward_type=gb.FORWARD_INFERENCE)
+    ctx.check()
+    assert torch.equal(outb, torch.from_numpy(exp).cuda().to(torch.bfloat16))
+
+
+# ------------------------------------------------------------------------------------------ config 5
+def _pair(seed, shape):
+    rng = np.random.default_rng(seed)
+    p = rng.uniform(0, 1, shape).astype(np.float32)
+    t = np.clip(p + rng.normal(0, 0.15, shape), 0, 1).astype(np.float32)
+    return p, t
+
+
+@pytest.mark.parametrize("batch,height,width", [(1, 1080, 1920), (8, 1080, 1920), (1, 2160, 3840), (8, 2160, 3840)],
+                         ids=["1080p_b1", "1080p_b8", "4k_b1", "4k_b8"])
+def test_config5_l1_ssim_matches_oracle(batch, height, width):
+    p, t = _pair(batch * 7 + height, (batch, 3, height, width))
+    P, T = torch.from_numpy(p).cuda(), torch.from_numpy(t).cuda()
+    lm = torch.zeros_like(P)
+    g = torch.zeros_like(P)
+    s = torch.zeros(1, device="cuda:0")
+    gb.l1_ssim(P, T, lm, g, 0.8, 0.2, loss_sum=s)
+    torch.cuda.synchronize()
+    lm_h, g_h = lm.cpu().numpy(), g.cpu().numpy()
+    # the oracle restates each image separately; at 4K x 8 the first and the last image are compared
+    # in full (a plane's result depends on that plane only) and the loss sum over the whole batch
+    imgs = range(batch) if batch * height * width <= 8 * 1080 * 1920 else (0, batch - 1)
+    n = p.size
+    for b in imgs:
+        # MEAN normalisation is over the whole batch: scale the oracle's per-image gradient to it
+        ref_lm, ref_g = po.l1_ssim_train(p[b:b + 1], t[b:b + 1], 0.8, 0.2, normalization="sum")
+        assert np.abs(lm_h[b] - ref_lm[0]).max() <= 2e-5, b
+        exp_g = ref_g[0] * np.float32(1.0 / n)
+        assert rel_l2(g_h[b], exp_g) <= 1e-4, b
+    assert abs(float(s) - float(lm_h.astype(np.float64).sum())) <= 1e-4 * max(1.0, abs(float(s)))
+
+
+def test_config5_adam_20m_gaussians_bit_exact():
+    n = 20_000_000 * 14
+    rng = np.random.default_rng(5)
+    p = rng.standard_normal(n, dtype=np.float32)
+    ref_p, m1, m2 = p.copy(), np.zeros(n, np.float32), np.zeros(n, np.float32)
+    P = torch.from_numpy(p).cuda()
+    G = torch.empty_like(P)
+    opt = gb.Adam([gb.ParamGroup("custom", P, G, 1e-3)])
+    for step in (1, 2):
+        gr = (rng.standard_normal(n, dtype=np.float32) * np.float32(1e-3)).astype(np.float32)
+        G.copy_(torch.from_numpy(gr))
+        po.adam(ref_p, gr, m1, m2, step, 1e-3)
+        opt.step(force_all=True)
+    torch.cuda.synchronize()
+    assert np.array_equal(P.cpu().numpy(), ref_p)
+
+
+def test_config5_sort_200m_pairs_properties(ctx):
+    """200M (tile << 32 | depth bits) keys: sorted, a permutation of the input, stable: all checked on the
+    device.  Keys: tile uniform over 8160 tiles, depth log-uniform in [0.1, 100] (config 5)."""
+    n = 200_000_000
+    gen = torch.Generator(device="cuda:0").manual_seed(55)
+    tile = torch.randint(0, 8160, (n,), device="cuda:0", generator=gen, dtype=torch.int64)
+    u = torch.rand(n, device="cuda:0", generator=gen)
+    depth = torch.exp(torch.log(torch.tensor(0.1)) + u * (torch.log(torch.tensor(100.0)) - torch.log(torch.tensor(0.1))))
+    del u
+    keys = (tile << 32) | depth.view(torch.int32).to(torch.int64)
+    del tile, depth
+    orig = keys.clone()
+    vals = torch.arange(n, dtype=torch.int32, device="cuda:0")
+    gb.sort_pairs(ctx, keys, vals, 0, 45)
+    ctx.check()
+    assert bool((keys[1:] >= keys[:-1]).all())
+    assert torch.equal(orig[vals.long()], keys)          # the values carry each key's original position
+    eq = keys[1:] == keys[:-1]
+    assert bool((vals[1:][eq] > vals[:-1][eq]).all())     # stable: ties keep input order
+    seen = torch.zeros(n, dtype=torch.bool, device="cuda:0")
+    seen[vals.long()] = True
+    assert bool(seen.all())                               # a permutation
