@@ -303,9 +303,19 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
         __syncthreads();
     }
     if(DO_LOSS && loss_sum != nullptr) {
+        /* warp sums -> one block sum -> one atomic per block: few adds into the (f32) total, so its
+         * rounding stays near one ulp per block even when the total reaches 1e7 (4K x 8 images) */
+        __shared__ float warp_sums[kThreads / 32];
 #pragma unroll
         for(int d = 16; d > 0; d >>= 1) local_sum += __shfl_xor_sync(0xffffffffu, local_sum, d);
-        if((threadIdx.x & 31) == 0 && local_sum != 0.0f) atomicAdd(loss_sum, local_sum);
+        if((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = local_sum;
+        __syncthreads();
+        if(threadIdx.x < 32) {
+            float v = threadIdx.x < kThreads / 32 ? warp_sums[threadIdx.x] : 0.0f;
+#pragma unroll
+            for(int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
+            if(threadIdx.x == 0 && v != 0.0f) atomicAdd(loss_sum, v);
+        }
     }
 }
 

@@ -9,7 +9,7 @@ and re-renders at backward (borrow_train_state = true), gsx-cuda/render.c:481-75
 Both are ported through GSX's public API on the gsx_b200 provider, with a stronger check for the borrowed
 case: the gradients equal a fresh TRAIN forward + backward of the mutated inputs (oracle, rel-L2 1e-3).
 The direct C-ABI mode (gsx_b200_context_set_train_state) is checked for the refresh count, for the
-unchanged-input path (no refresh, the retained result bit for bit) and for the caller's image.
+unchanged-input path (no refresh, the retained result) and for the caller's image.
 """
 import numpy as np
 import pytest
@@ -109,7 +109,8 @@ def test_c_abi_borrowed_mode_refreshes_only_on_change(cuda_device):
     base = zeros_like_fields(gd)
     rend.backward(ctx, gr, base)
     ctx.check()
-    # borrowed mode, no mutation: no refresh, the same gradients bit for bit
+    # borrowed mode, no mutation: no refresh, the same gradients (up to the order of the blend
+    # backward's atomic additions)
     ctx.set_train_state(True)
     render(ctx, gd, cam, 1)
     same = zeros_like_fields(gd)
@@ -117,7 +118,7 @@ def test_c_abi_borrowed_mode_refreshes_only_on_change(cuda_device):
     ctx.check()
     assert ctx.train_refreshes() == 0
     for k in gd:
-        assert torch.equal(same[k], base[k]), k
+        assert rel_l2(same[k].cpu().numpy(), base[k].cpu().numpy()) <= 1e-5, k
     # borrowed mode, mutation after the forward: one refresh, gradients of the mutated inputs
     out = render(ctx, gd, cam, 1)
     out_before = out.clone()
