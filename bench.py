@@ -157,20 +157,25 @@ def forward_inference(args, dev, rank, world, local):
     mine = [c for f, c in enumerate(cams) if f % world == rank]
     for c in mine[:3]:
         rend.render(ctx, g, c, out, forward_type=gb.FORWARD_INFERENCE)
-    ctx.set_profiling(True)
-    ctx.read_profile()
     stream = torch.cuda.current_stream()
-    evs = []
-    for c in mine:
-        flush.fill_(1.0)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        rend.render(ctx, g, c, out, forward_type=gb.FORWARD_INFERENCE)
-        e1.record(stream)
-        evs.append((e0, e1))
-    torch.cuda.synchronize()
-    ctx.set_profiling(False)
-    prof = ctx.read_profile()
+
+    def frames(profiled):
+        ctx.set_profiling(profiled)
+        ctx.read_profile()
+        evs = []
+        for c in mine:
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            rend.render(ctx, g, c, out, forward_type=gb.FORWARD_INFERENCE)
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        ctx.set_profiling(False)
+        return evs, ctx.read_profile()
+
+    evs, _ = frames(False)         # timed: no stage events inside the frames
+    _, prof = frames(True)         # stage breakdown, a second pass
     ctx.check()
     ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([ms], device=dev)
@@ -260,6 +265,45 @@ def input_conversion(dev):
             "achieved_gbs": 15.0 * H * W / (ms / 1000.0) / 1e9}
 
 
+def profile_case(args):
+    """A scaled-down workload for ncu captures (one GPU): `--gaussians` of the config-3 generator (2:1
+    volume:slab) trained for `--steps` steps on one 1245x825 view, or, with `--profile-forward`, that many
+    config-2 INFERENCE renders at 1920x1080.  Prints per-stage CUDA-event times; not a bench line.
+    Launch order per training step: preprocess (+ block scan), emit, tile scan (3), tile bin, per-tile
+    sort (one launch per non-empty size class), blend_forward, l1_ssim, blend_backward,
+    preprocess_backward, adam."""
+    import torch
+
+    import gsx_b200 as gb
+    from gsx_b200 import scenes
+    from gsx_b200.train import GaussianModel, Trainer
+    torch.cuda.set_device(0)
+    if args.profile_forward:
+        g = {k: torch.from_numpy(v).cuda() for k, v in scenes.config2_scene(0, args.gaussians).items()}
+        cams = scenes.config2_cameras(8)
+        ctx = gb.RenderContext(0)
+        out = torch.empty((3, cams[0].height, cams[0].width), device="cuda")
+        ctx.set_profiling(True)
+        for s in range(args.steps):
+            c = cams[s % len(cams)]
+            gb.Renderer(c.width, c.height).render(ctx, g, c, out, forward_type=gb.FORWARD_INFERENCE)
+        ctx.check()
+        print(json.dumps({"stats": ctx.stats(), "profile": ctx.read_profile()}))
+        return
+    frac = args.gaussians / 3_000_000
+    g = scenes.config3_scene(0, n_volume=int(round(2_000_000 * frac)), n_slab=int(round(1_000_000 * frac)))
+    cams = scenes.config3_cameras()
+    model = GaussianModel(g)
+    c = cams[0]
+    trainer = Trainer(model, c.width, c.height)
+    target = torch.rand((3, c.height, c.width), device="cuda")
+    trainer.ctx.set_profiling(True)
+    for s in range(args.steps):
+        trainer.step(cams[s % len(cams)], target)
+    trainer.ctx.check()
+    print(json.dumps({"stats": trainer.ctx.stats(), "profile": trainer.ctx.read_profile()}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -269,7 +313,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU gradient exchange: fused NVLink reduce+Adam+gather kernel, or NCCL all-reduce + Adam")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="scaled-down one-GPU workload for ncu captures (see profile_case); prints stage times only")
+    ap.add_argument("--profile-forward", action="store_true", help="with --profile-case: config-2 forward renders")
+    ap.add_argument("--gaussians", type=int, default=1_000_000, help="with --profile-case: scene size")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return
@@ -313,14 +364,10 @@ def main():
     stats = trainer.ctx.stats()
 
     # ---- device-timed region: inputs resident in HBM (params/grads/moments 3M x 56 B x 4 > L2) ----
+    # No per-stage events inside it (they cost ~1 us each on the stream); the stage breakdown comes from
+    # a second, profiled pass of the same K steps right after it.
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    le = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    ae = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    trainer.ctx.set_profiling(True)
-    trainer.ctx.read_profile()
-    if trainer.sharded is not None:
-        trainer.sharded.kernel_events = []
     launches0 = trainer.ctx.launch_count()
     if world > 1:
         dist.barrier()
@@ -329,14 +376,38 @@ def main():
         e0.record(stream)
         for s in range(args.steps):
             c = cams[view(args.warmup + s)]
-            trainer.step(c, targets[view(args.warmup + s)], events=(le[s], ae[s]))
+            trainer.step(c, targets[view(args.warmup + s)])
         e1.record(stream)
         torch.cuda.synchronize()
-    trainer.ctx.set_profiling(False)
     # render context launches (counted by the library) + the fused loss and Adam launches per step
     timed_launches = trainer.ctx.launch_count() - launches0 + 2 * args.steps
-    prof = trainer.ctx.read_profile()
     ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms_max = float(t.item())
+    trainer.ctx.check()
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- profiled pass: the same steps with CUDA events around every stage (stage times, roofline) ----
+    le = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ae = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    trainer.ctx.set_profiling(True)
+    trainer.ctx.read_profile()
+    if trainer.sharded is not None:
+        trainer.sharded.kernel_events = []
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for s in range(args.steps):
+        c = cams[view(args.warmup + s)]
+        trainer.step(c, targets[view(args.warmup + s)], events=(le[s], ae[s]))
+    p1.record(stream)
+    torch.cuda.synchronize()
+    trainer.ctx.set_profiling(False)
+    prof = trainer.ctx.read_profile()
+    profiled_ms = p0.elapsed_time(p1) / args.steps
     exchange = None
     if trainer.sharded is not None:
         kms = sum(a.elapsed_time(b) for a, b in trainer.sharded.kernel_events) / len(trainer.sharded.kernel_events)
@@ -351,13 +422,7 @@ def main():
                             "to them; the NVLink reference is the measured 770 GB/s per direction peer copy"}
     loss_ms = sum(a.elapsed_time(b) for a, b in le) / args.steps
     adam_ms = sum(a.elapsed_time(b) for a, b in ae) / args.steps
-    t = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.barrier()
-    ms_max = float(t.item())
     trainer.ctx.check()
-    value = world * args.steps / (ms_max / 1000.0)
 
     # ---- end to end through the public API: H2D target + D2H loss every step ----
     # (gsx_b200.train.HostFeed: each step's pinned target uploads on a copy stream while the previous
@@ -464,6 +529,7 @@ def main():
                          "frac": achieved / hbm, "traffic": traffic, "peak_source": peak_kind,
                          "avg_ms": dom_ms, "algorithmic_bytes": algo_bytes[dom]},
             "stages_ms": {k: round(v, 4) for k, v in stage_avg.items()},
+            "stages_pass_ms_per_step": round(profiled_ms, 4),
             "forward": fwd,
             "large_frame": big,
             "input_conversion": conv,

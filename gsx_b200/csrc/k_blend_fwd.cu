@@ -119,12 +119,36 @@ template <bool kTrain, bool kBF16>
 __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     int width, int height, int row0, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, void *__restrict__ out_rgb,
-    float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile)
+    float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile,
+    const uint32_t *__restrict__ valid, const uint32_t *__restrict__ tile_lists, const uint32_t *__restrict__ class_sizes)
 {
+    if(valid != nullptr && *valid == 0u) return; /* a frame the host redoes (overflow or a huge tile) */
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem &S = *reinterpret_cast<FwdSmem *>(smem_raw);
     __shared__ uint32_t s_max[kWarps];
-    const int tile = blockIdx.x;
+    /* CTAs take tiles largest size class first (the tile scan's lists: classes 0..4 end to end, then
+     * the empty tiles), so the long tiles start in the first wave and the short ones fill the tail */
+    int tile = blockIdx.x;
+    if(tile_lists != nullptr) {
+        uint32_t cnt[GSX_SORT_CLASSES], off = 0;
+#pragma unroll
+        for(int c = 0; c < GSX_SORT_CLASSES; ++c) {
+            cnt[c] = class_sizes[c];
+            off += cnt[c];
+        }
+        uint32_t rem = blockIdx.x, at = off; /* at: start of the empty-tile list */
+        bool found = false;
+#pragma unroll
+        for(int c = GSX_SORT_CLASSES - 1; c >= 0; --c) {
+            at -= cnt[c];
+            if(!found && rem < cnt[c]) {
+                tile = (int)tile_lists[at + rem];
+                found = true;
+            }
+            if(!found) rem -= cnt[c];
+        }
+        if(!found) tile = (int)tile_lists[off + rem];
+    }
     const int tx = tile % grid_w, ty = tile / grid_w;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int lx = (warp & 1) * 8 + (lane & 7), ly = (warp >> 1) * 4 + (lane >> 3);
@@ -268,7 +292,8 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
 cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
-                                     float4 *snap, uint32_t *bucket_tile, bool train, cudaStream_t stream)
+                                     float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *valid,
+                                     const uint32_t *tile_lists, const uint32_t *class_sizes, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
     static bool attr_done[4][256];
@@ -285,6 +310,7 @@ cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w
     }
     kern<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(width, height, row0, grid_w, ranges, bucket_offsets, vals,
                                                                    rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
-                                                                   tile_max, snap, bucket_tile);
+                                                                   tile_max, snap, bucket_tile, valid, tile_lists,
+                                                                   class_sizes);
     return cudaGetLastError();
 }
