@@ -3,9 +3,9 @@
  * of the render forward/backward pipeline on one stream.
  *
  * Forward: preprocess (+ one-CTA scan of block totals) -> emit keys (+ in-block scan into offsets)
- * -> tile scan -> binning -> per-tile depth sort -> blend+compose, all queued before the host waits
- * for the one read-back (queued after the tile scan).  Backward: blend backward -> preprocess
- * backward.
+ * -> tile scan -> binning (queued behind the one read-back of the instance total, largest tile and
+ * size-class counts) -> per-tile depth sort (grids from the read-back) -> blend+compose.
+ * Backward: blend backward -> preprocess backward.
  * Scratch grows on demand with cudaMalloc (outside any stream capture) and is never shrunk.
  */
 #include "../../include/gsx_b200.h"
@@ -145,7 +145,7 @@ struct gsx_b200_context {
      * [4..8] tiles per per-tile-sort size class */
     DevBuf words;
     uint32_t *host_words = nullptr; /* pinned: [0] instance total, [1] flags, [2] largest tile, [3..7] class sizes,
-                                     * [8] frame valid, [16..19] two input fingerprints (u64) */
+                                     * [16..19] two input fingerprints (u64) */
     bool global_sort = false;       /* the last forward needed the global radix sort (a tile > GSX_SEG_MAX) */
     /* side streams and fork/join events of the per-tile sort's size classes (created on first use) */
     cudaStream_t side[GSX_SORT_CLASSES - 1] = {};
@@ -345,15 +345,13 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
     uint32_t *tile_masks = (uint32_t *)ctx->tile_masks.ptr;
     uint32_t *block_sums = (uint32_t *)ctx->block_sums.ptr;
 
-    /* preprocess -> block-total scan -> emission into the current instance capacity -> tile scan
-     * (ranges, bucket prefix, class lists, and a validity word: no capacity overflow and no tile beyond
-     * the shared-memory sort) -> binning -> per-tile depth sort -> blend, ALL queued before the host
-     * reads anything: every kernel after the scan sizes itself from device words (class sizes, instance
-     * total) and does nothing if the validity word is 0.  The read-back of the instance total, largest
-     * tile and validity is queued right after the scan; the host waits for it only after queueing the
-     * blend, so the GPU never idles on the host.  A frame found invalid (rare: the capacity keeps 25%
-     * headroom; tiles above GSX_SEG_MAX instances) is redone on the host's decision: the emission
-     * into grown buffers, or the global radix sort of the tile|depth keys for huge tiles. */
+    /* preprocess -> block-total scan -> emission into the current instance capacity (each instance
+     * takes its rank in its tile) -> tile scan (ranges, bucket prefix, total, largest tile) -> ONE
+     * read-back (instance total, largest tile, size-class counts), behind which the binning is already
+     * queued (it reads the total on the device), so the GPU bins while the host waits; if the
+     * capacity was too small the emission is repeated into grown buffers (rare: capacity keeps 25%
+     * headroom).  Then the per-tile depth sort, or, when a tile holds more instances than shared memory
+     * sorts, the global radix sort of the tile|depth keys (the binning's output is then unused). */
     int tile_bits = 0;
     while((1 << tile_bits) < n_tiles) ++tile_bits;
     const int end_bit = 32 + tile_bits;
@@ -362,29 +360,11 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
     if(int rc = ensure(ctx->tile_aux, sizeof(uint32_t) * gsx_tile_scan_aux_words(n_tiles))) return rc;
     if(ctx->readback_ev == nullptr)
         GSX_CUDA_TRY(cudaEventCreateWithFlags(&ctx->readback_ev, cudaEventDisableTiming), "cudaEventCreate");
-    if(!ctx->side_created) {
-        for(int k = 0; k < GSX_SORT_CLASSES - 1; ++k)
-            GSX_CUDA_TRY(cudaStreamCreateWithFlags(&ctx->side[k], cudaStreamNonBlocking), "cudaStreamCreate");
-        for(int k = 0; k < GSX_SORT_CLASSES; ++k)
-            GSX_CUDA_TRY(cudaEventCreateWithFlags(&ctx->side_ev[k], cudaEventDisableTiming), "cudaEventCreate");
-        ctx->side_created = true;
-    }
     uint32_t *tile_count = (uint32_t *)ctx->tile_count.ptr;
     uint32_t *class_tiles = (uint32_t *)ctx->class_tiles.ptr;
-    const bool train = forward_type == GSX_B200_FORWARD_TRAIN;
-    const uint32_t *valid_word = words + 2 + 2 + GSX_SORT_CLASSES;
-    auto blend = [&](const uint32_t *vals, const uint32_t *valid) -> int {
-        StageTimer st4(ctx, 4, stream);
-        GSX_CUDA_TRY(gsx_launch_blend_forward(cam.width, cam.height, row_begin, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
-                                              (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
-                                              out_rgb, out_bf16, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
-                                              (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr, train, valid,
-                                              class_tiles, words + 4, stream),
-                     "blend launch");
-        ctx->launches += n_tiles > 0 ? 1 : 0;
-        return 0;
-    };
-    auto queue_frame = [&](uint64_t cap) -> int {
+    uint64_t total = 0;
+    uint32_t max_tile = 0;
+    auto emit_into_capacity = [&](uint64_t cap) -> int {
         /* capacity in pairs; ensure() only reallocates when the request exceeds what is held, and
          * inst_cap is the exact floor of what is held, so a steady workload never reallocates */
         if(cap == 0) cap = 1;
@@ -393,13 +373,6 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         ctx->inst_cap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
         const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
         if(vcap < ctx->inst_cap) ctx->inst_cap = vcap;
-        if(train) {
-            /* bucket snapshots and the bucket -> tile table, for the backward only: sized from the
-             * capacity (the bucket count is known on the device only) */
-            const uint64_t bcap = (ctx->inst_cap + 31) / 32 + (uint64_t)n_tiles;
-            if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bcap)) return rc;
-            if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bcap)) return rc;
-        }
         /* the emission's capacity-overflow bit lives in its own word (words[1]), cleared per pass: an
          * overflow is expected on the pass before a capacity retry.  words[0] keeps the sticky flags
          * (lookback timeouts) until gsx_b200_context_check reads them. */
@@ -414,64 +387,63 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
                          "emit launch");
             ctx->launches += n > 0 ? 1 : 0;
         }
-        const uint64_t kc = ctx->keys.bytes / (2 * sizeof(unsigned long long));
-        unsigned long long *ka = (unsigned long long *)ctx->keys.ptr;
-        {
-            StageTimer st3(ctx, 3, stream);
-            GSX_CUDA_TRY(gsx_launch_tile_scan(tile_count, n_tiles, (uint2 *)ctx->ranges.ptr,
-                                              (uint32_t *)ctx->bucket_offsets.ptr, class_tiles,
-                                              (uint32_t *)ctx->tile_aux.ptr, words + 1, words + 2, stream),
-                         "tile scan launch");
-            ctx->launches += n_tiles > 0 ? 3 : 0;
-            /* read-back: [0] the preprocess's instance total (the true one, also on overflow),
-             * [2] largest tile, [3..7] class sizes, [8] validity */
-            if(n > 0)
-                GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
-                             "D2H");
-            else
-                ctx->host_words[0] = 0;
-            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (2 + GSX_SORT_CLASSES) * sizeof(uint32_t),
-                                         cudaMemcpyDeviceToHost, stream),
+        StageTimer st3(ctx, 3, stream);
+        GSX_CUDA_TRY(gsx_launch_tile_scan(tile_count, n_tiles, (uint2 *)ctx->ranges.ptr,
+                                          (uint32_t *)ctx->bucket_offsets.ptr, class_tiles,
+                                          (uint32_t *)ctx->tile_aux.ptr, words + 2, stream),
+                     "tile scan launch");
+        ctx->launches += n_tiles > 0 ? 3 : 0;
+        if(n > 0)
+            GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words, block_sums + pblocks, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
                          "D2H");
-            GSX_CUDA_TRY(cudaEventRecord(ctx->readback_ev, stream), "cudaEventRecord");
-            /* binning for the per-tile sort: keys/values of the emission -> (depth, primitive) keys in the
-             * second half of the key buffer, count read on the device (words[2], the tile scan's total) */
-            GSX_CUDA_TRY(gsx_launch_tile_bin(ka, (const uint32_t *)ctx->vals.ptr, words + 2, ctx->inst_cap, n_tiles,
-                                             tile_count, ka + kc, stream),
+        else
+            ctx->host_words[0] = 0;
+        GSX_CUDA_TRY(cudaMemcpyAsync(ctx->host_words + 2, words + 3, (1 + GSX_SORT_CLASSES) * sizeof(uint32_t),
+                                     cudaMemcpyDeviceToHost, stream),
+                     "D2H");
+        GSX_CUDA_TRY(cudaEventRecord(ctx->readback_ev, stream), "cudaEventRecord");
+        /* binning for the per-tile sort: keys/values of the emission -> (depth, primitive) keys in the
+         * second half of the key buffer, count read on the device (words[2], the tile scan's total) */
+        {
+            const uint64_t kc = ctx->keys.bytes / (2 * sizeof(unsigned long long));
+            unsigned long long *ka = (unsigned long long *)ctx->keys.ptr;
+            GSX_CUDA_TRY(gsx_launch_tile_bin(ka, (const uint32_t *)ctx->vals.ptr, words + 2, ctx->inst_cap, n_tiles, tile_count, ka + kc,
+                                             stream),
                          "tile bin launch");
             ctx->launches += 1;
         }
-        {
-            StageTimer st(ctx, 2, stream);
-            int sorts = 0;
-            GSX_CUDA_TRY(gsx_launch_tile_sort(ctx->inst_cap, n_tiles, (const uint2 *)ctx->ranges.ptr, class_tiles, words + 2,
-                                              ka + kc, ka, (uint32_t *)ctx->vals.ptr, stream, ctx->side, ctx->side_ev, &sorts),
-                         "tile sort launch");
-            ctx->launches += (uint64_t)sorts;
-        }
-        return blend((const uint32_t *)ctx->vals.ptr, valid_word);
+        return 0;
     };
     if(n > 0) {
-        StageTimer st0(ctx, 0, stream);
-        GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2,
-                                           g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, tile_masks,
-                                           block_sums, train ? ctx->aux_visible : nullptr, train ? ctx->aux_radius : nullptr,
-                                           stream),
-                     "preprocess launch");
-        ctx->launches += 2;
-    } else {
-        GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
-    }
-    if(int rc = queue_frame(ctx->inst_cap)) return rc;
-    GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
-    uint64_t total = ctx->host_words[0];
-    if(total > ctx->inst_cap) {
-        /* the emission overflowed: everything after the scan did nothing; redo into grown buffers */
-        if(int rc = queue_frame(total + total / 4 + 1024)) return rc;
+        {
+            StageTimer st0(ctx, 0, stream);
+            GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2,
+                                               g->sh3, sh_degree, n, cam, (PrimRec *)ctx->rec.ptr, counts, tile_masks,
+                                               block_sums, forward_type == GSX_B200_FORWARD_TRAIN ? ctx->aux_visible : nullptr,
+                                               forward_type == GSX_B200_FORWARD_TRAIN ? ctx->aux_radius : nullptr, stream),
+                         "preprocess launch");
+            ctx->launches += 2;
+        }
+        if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
         GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
         total = ctx->host_words[0];
+        if(total > ctx->inst_cap) {
+            if(int rc = emit_into_capacity(total + total / 4 + 1024)) return rc;
+            GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
+        }
+        max_tile = ctx->host_words[2];
+    } else {
+        GSX_CUDA_TRY(cudaMemsetAsync(offsets, 0, sizeof(uint32_t), stream), "memset");
+        if(int rc = emit_into_capacity(ctx->inst_cap)) return rc;
+        GSX_CUDA_TRY(cudaEventSynchronize(ctx->readback_ev), "forward read-back");
     }
-    const uint32_t max_tile = ctx->host_words[2];
+    ctx->n_instances = total;
+    const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
+    if(forward_type == GSX_B200_FORWARD_TRAIN) {
+        /* bucket snapshots and the bucket -> tile table exist for the backward only */
+        if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
+        if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
+    }
     const uint64_t kcap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
     unsigned long long *keys_a = (unsigned long long *)ctx->keys.ptr;
     unsigned long long *keys_b = keys_a + kcap;
@@ -479,23 +451,42 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
     uint32_t *vals_b = vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t));
     int in_b = 0;
     ctx->global_sort = false;
-    if(total > 0 && max_tile > (uint32_t)GSX_SEG_MAX) {
-        /* a tile too large for shared memory: the per-tile sort and the blend did nothing; stable global
-         * radix sort of the emitted tile|depth keys (in primitive order, so equal depths stay in
-         * primitive order), then the blend again */
-        ctx->global_sort = true;
-        {
-            StageTimer st(ctx, 2, stream);
+    if(total > 0) {
+        StageTimer st(ctx, 2, stream);
+        if(max_tile <= (uint32_t)GSX_SEG_MAX) {
+            if(!ctx->side_created) {
+                for(int k = 0; k < GSX_SORT_CLASSES - 1; ++k)
+                    GSX_CUDA_TRY(cudaStreamCreateWithFlags(&ctx->side[k], cudaStreamNonBlocking), "cudaStreamCreate");
+                for(int k = 0; k < GSX_SORT_CLASSES; ++k)
+                    GSX_CUDA_TRY(cudaEventCreateWithFlags(&ctx->side_ev[k], cudaEventDisableTiming), "cudaEventCreate");
+                ctx->side_created = true;
+            }
+            GSX_CUDA_TRY(gsx_launch_tile_sort(total, n_tiles, (const uint2 *)ctx->ranges.ptr, class_tiles, ctx->host_words + 3,
+                                              keys_b, keys_a, vals_a, stream, ctx->side, ctx->side_ev),
+                         "tile sort launch");
+            for(int c = 0; c < GSX_SORT_CLASSES; ++c) ctx->launches += ctx->host_words[3 + c] ? 1 : 0;
+        } else {
+            /* a tile too large for shared memory: stable global radix sort of the tile|depth keys
+             * (emitted in primitive order, so equal depths stay in primitive order) */
+            ctx->global_sort = true;
             if(int rc = ensure(ctx->sort_scratch, gsx_sort_scratch_bytes(total + 1))) return rc;
             GSX_CUDA_TRY(gsx_launch_sort_pairs(keys_a, vals_a, keys_b, vals_b, total, 0, end_bit, ctx->sort_scratch.ptr,
                                                ctx->sort_scratch.bytes, words, &in_b, stream),
                          "sort launch");
             ctx->launches += 1 + (uint64_t)((end_bit + 7) / 8);
         }
-        if(int rc = blend(in_b ? vals_b : vals_a, nullptr)) return rc;
     }
-    ctx->n_instances = total;
-    const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
+    const uint32_t *vals = in_b ? vals_b : vals_a;
+    {
+    StageTimer st4(ctx, 4, stream);
+    GSX_CUDA_TRY(gsx_launch_blend_forward(cam.width, cam.height, row_begin, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
+                                          (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
+                                          out_rgb, out_bf16, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
+                                          (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr,
+                                          forward_type == GSX_B200_FORWARD_TRAIN, class_tiles, words + 4, stream),
+                 "blend launch");
+    ctx->launches += n_tiles > 0 ? 1 : 0;
+    }
     ctx->keys_in_b = in_b;
     ctx->bucket_cap = bucket_cap;
     ctx->n_tiles = n_tiles;

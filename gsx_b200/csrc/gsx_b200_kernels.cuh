@@ -160,30 +160,24 @@ cudaError_t gsx_launch_sort_pairs(unsigned long long *keys_a, uint32_t *vals_a, 
  * counter index with one coalesced access */
 #define GSX_SUBCOUNTER(t, s, n_tiles) ((size_t)(s) * (size_t)(n_tiles) + (size_t)(t))
 size_t gsx_tile_scan_aux_words(int n_tiles);
-/* words_out: [0] instance total, [1] largest tile, [2 + c] tiles of size class c, [2 + GSX_SORT_CLASSES]
- * frame valid (*overflow == 0, the emission's overflow word, and largest tile <= GSX_SEG_MAX),
- * 8 words */
 cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
-                                 uint32_t *class_tiles, uint32_t *block_aux, const uint32_t *overflow,
-                                 uint32_t *words_out, cudaStream_t stream);
+                                 uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream);
 /* side: GSX_SORT_CLASSES - 1 streams; ev: GSX_SORT_CLASSES events (fork and join) */
 cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *vals, const uint32_t *d_total,
                                 uint64_t max_n, int n_tiles, uint32_t *tile_end, unsigned long long *sort_keys, cudaStream_t stream);
-/* scan_words: the tile scan's words_out (class sizes and validity read on the device) */
-cudaError_t gsx_launch_tile_sort(uint64_t capacity, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
-                                 const uint32_t *scan_words, const unsigned long long *sort_keys,
+cudaError_t gsx_launch_tile_sort(uint64_t n, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
+                                 const uint32_t *class_counts, const unsigned long long *sort_keys,
                                  unsigned long long *keys_out, uint32_t *vals_out, cudaStream_t stream,
-                                 cudaStream_t const *side, cudaEvent_t const *ev, int *out_launches);
+                                 cudaStream_t const *side, cudaEvent_t const *ev);
 /* out_rgb: [3, height, width] f32, or bf16 (round to nearest even) when out_bf16; row0 = first pixel
  * row of the band in the full frame (a multiple of 16, 0 for a full frame) */
-/* valid (device word, may be NULL): the blend does nothing when it is 0 (a frame the host redoes).
- * tile_lists / class_sizes (may be NULL): the tile scan's class lists and class sizes; CTAs then take
- * tiles from the largest class down */
+/* tile_lists / class_sizes (may be NULL): the tile scan's class lists (classes 0..4 end to end, then
+ * the empty tiles) and the device class sizes; CTAs then take tiles from the largest class down */
 cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
-                                     float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *valid,
-                                     const uint32_t *tile_lists, const uint32_t *class_sizes, cudaStream_t stream);
+                                     float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *tile_lists,
+                                     const uint32_t *class_sizes, cudaStream_t stream);
 cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_w, const uint2 *ranges,
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
                                       int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,

@@ -120,9 +120,8 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
     int width, int height, int row0, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, void *__restrict__ out_rgb,
     float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile,
-    const uint32_t *__restrict__ valid, const uint32_t *__restrict__ tile_lists, const uint32_t *__restrict__ class_sizes)
+    const uint32_t *__restrict__ tile_lists, const uint32_t *__restrict__ class_sizes)
 {
-    if(valid != nullptr && *valid == 0u) return; /* a frame the host redoes (overflow or a huge tile) */
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem &S = *reinterpret_cast<FwdSmem *>(smem_raw);
     __shared__ uint32_t s_max[kWarps];
@@ -292,8 +291,8 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
 cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
-                                     float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *valid,
-                                     const uint32_t *tile_lists, const uint32_t *class_sizes, cudaStream_t stream)
+                                     float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *tile_lists,
+                                     const uint32_t *class_sizes, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
     static bool attr_done[4][256];
@@ -310,7 +309,6 @@ cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w
     }
     kern<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(width, height, row0, grid_w, ranges, bucket_offsets, vals,
                                                                    rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
-                                                                   tile_max, snap, bucket_tile, valid, tile_lists,
-                                                                   class_sizes);
+                                                                   tile_max, snap, bucket_tile, tile_lists, class_sizes);
     return cudaGetLastError();
 }

@@ -15,7 +15,7 @@
  * between them.  Here one CTA owns a 32x32 output tile and recomputes the partials it needs on a
  * 42x42 halo region from a 52x52 input tile in shared memory, so HBM sees only the inputs, the
  * loss map and the gradient (no scratch at all); each separable pass keeps its 11-tap window in
- * registers over a run of 6-8 outputs per thread.  The same kernel, with the loss or the gradient
+ * registers over a run of 4-8 outputs per thread.  The same kernel, with the loss or the gradient
  * stage compiled out, serves the standalone SSIM forward and backward calls.
  */
 #include <cuda_runtime.h>
@@ -56,9 +56,26 @@ __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c)
 }
 __device__ __forceinline__ f2 ld2(const float2 &v) { return *reinterpret_cast<const f2 *>(&v); }
 
-/* row strides are odd (in elements) so that lanes walking down a column hit distinct banks */
+__device__ __forceinline__ float rcp_approx(float x)
+{
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+/* row strides are odd (in elements) so that lanes walking down a column hit distinct banks.  Two
+ * unions, each member live in different stages: the input tile (stages 0-1) shares its space with the
+ * SSIM partials (written in stage 2, read in stage 3; stages 2 and 4 take p and t from global memory,
+ * where the tile's inputs are still in L2), and the horizontal moment blurs (stages 1-2) with the
+ * horizontal partial blurs (stages 3-4): 66.8 KB, three CTAs per SM. */
 struct LossSmem {
-    float2 in[kIn][kIn + 1]; /* (p, t) */
+    union {
+        float2 in[kIn][kIn + 1]; /* (p, t) */
+        struct {
+            float2 part01[kMid][kMid + 1]; /* dm/dmu, dm/dsigma1^2 (scaled), per halo pixel */
+            float part2[kMid][kMid + 1];   /* dm/dsigma12 (scaled) */
+        } p;
+    } u0;
     union {
         struct {
             float2 mu[kIn][kMid + 1]; /* horizontal blur of (p, t) */
@@ -69,9 +86,7 @@ struct LossSmem {
             float2 d01[kMid][kOut + 1]; /* horizontal blur of the partials d0, d1 */
             float d2[kMid][kOut + 1];   /* and d2 (h is dead by then) */
         } h2;
-    };
-    float2 part01[kMid][kMid + 1]; /* dm/dmu, dm/dsigma1^2 (scaled), per halo pixel */
-    float part2[kMid][kMid + 1];   /* dm/dsigma12 (scaled) */
+    } u1;
 };
 
 /*
@@ -82,7 +97,7 @@ struct LossSmem {
  * travel as f32x2 pairs: 3 instructions per tap instead of 5 in the moment passes.
  */
 template <bool DO_LOSS, bool DO_GRAD, bool WITH_L1>
-__global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__restrict__ pred, const float *__restrict__ target,
+__global__ void __launch_bounds__(kThreads, 3) l1_ssim_kernel(const float *__restrict__ pred, const float *__restrict__ target,
                                                               float *__restrict__ loss_map, float *__restrict__ grad,
                                                               float *__restrict__ loss_sum, int planes, int height, int width,
                                                               float l1_scale, float ssim_scale, float l1_grad_scale,
@@ -103,17 +118,28 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
     for(int plane = blockIdx.z; plane < planes; plane += gridDim.z) {
         const float *P = pred + (size_t)plane * plane_elems;
         const float *Tg = target + (size_t)plane * plane_elems;
-        /* stage 0: 52x52 input tile of (p, t) pairs with zero padding */
-        for(int j = threadIdx.x; j < kIn * kIn; j += kThreads) {
-            const int y = j / kIn, x = j % kIn;
-            const int gy = oy - 2 * kR + y, gx = ox - 2 * kR + x;
-            float pv = 0.0f, tv = 0.0f;
-            if(gy >= 0 && gy < height && gx >= 0 && gx < width) {
-                const size_t idx = (size_t)gy * width + gx;
-                pv = P[idx];
-                tv = Tg[idx];
+        /* stage 0: 52x52 input tile of (p, t) pairs with zero padding; every load of the thread is
+         * issued before the first store, so their latencies overlap */
+        {
+            constexpr int kPer = (kIn * kIn + kThreads - 1) / kThreads;
+            float pv[kPer], tv[kPer];
+#pragma unroll
+            for(int q = 0; q < kPer; ++q) {
+                const int j = threadIdx.x + q * kThreads;
+                const int y = j / kIn, x = j % kIn;
+                const int gy = oy - 2 * kR + y, gx = ox - 2 * kR + x;
+                pv[q] = tv[q] = 0.0f;
+                if(j < kIn * kIn && gy >= 0 && gy < height && gx >= 0 && gx < width) {
+                    const size_t idx = (size_t)gy * width + gx;
+                    pv[q] = __ldg(P + idx);
+                    tv[q] = __ldg(Tg + idx);
+                }
             }
-            S.in[y][x] = make_float2(pv, tv);
+#pragma unroll
+            for(int q = 0; q < kPer; ++q) {
+                const int j = threadIdx.x + q * kThreads;
+                if(j < kIn * kIn) S.u0.in[j / kIn][j % kIn] = make_float2(pv[q], tv[q]);
+            }
         }
         __syncthreads();
         /* stage 1: horizontal blur of the moments; item = (row, run of 6 columns) */
@@ -123,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
             float c[16];
 #pragma unroll
             for(int k = 0; k < 16; ++k) {
-                const float2 pt = S.in[y][x0 + k];
+                const float2 pt = S.u0.in[y][x0 + k];
                 v[k] = ld2(pt);
                 q[k] = mul2(v[k], v[k]);
                 c[k] = pt.x * pt.y;
@@ -140,10 +166,10 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                 }
                 float a, b;
                 upk(smu, a, b);
-                S.h.mu[y][x0 + o] = make_float2(a, b);
+                S.u1.h.mu[y][x0 + o] = make_float2(a, b);
                 upk(ssq, a, b);
-                S.h.sq[y][x0 + o] = make_float2(a, b);
-                S.h.x[y][x0 + o] = sx;
+                S.u1.h.sq[y][x0 + o] = make_float2(a, b);
+                S.u1.h.x[y][x0 + o] = sx;
             }
         }
         __syncthreads();
@@ -156,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
             {
                 f2 v[16];
 #pragma unroll
-                for(int k = 0; k < 16; ++k) v[k] = ld2(S.h.mu[y0 + k][x]);
+                for(int k = 0; k < 16; ++k) v[k] = ld2(S.u1.h.mu[y0 + k][x]);
 #pragma unroll
                 for(int o = 0; o < 6; ++o) {
                     f2 acc = 0ull;
@@ -165,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                     mmu[o] = acc;
                 }
 #pragma unroll
-                for(int k = 0; k < 16; ++k) v[k] = ld2(S.h.sq[y0 + k][x]);
+                for(int k = 0; k < 16; ++k) v[k] = ld2(S.u1.h.sq[y0 + k][x]);
 #pragma unroll
                 for(int o = 0; o < 6; ++o) {
                     f2 acc = 0ull;
@@ -175,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                 }
                 float c[16];
 #pragma unroll
-                for(int k = 0; k < 16; ++k) c[k] = S.h.x[y0 + k][x];
+                for(int k = 0; k < 16; ++k) c[k] = S.u1.h.x[y0 + k][x];
 #pragma unroll
                 for(int o = 0; o < 6; ++o) {
                     float acc = 0.0f;
@@ -199,14 +225,14 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                 const float A = mu1_sq + mu2_sq + 1e-4f, B = s1sq + s2sq + 9e-4f;
                 const float C = 2.0f * mu1 * mu2 + 1e-4f, D = 2.0f * s12 + 9e-4f;
                 const float den = A * B;
+                /* approximate reciprocals (SFU): the loss is compared with tolerance, and the
+                 * reciprocal's error (~1 ulp) is far below the fp32 cancellation in the variances */
+                const float iden = rcp_approx(den);
                 if(DO_LOSS && in_image && y >= kR && y < kR + kOut && x >= kR && x < kR + kOut) {
                     const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
-                    const float ssim = den == 0.0f ? 1.0f : (C * D) / den;
+                    const float ssim = den == 0.0f ? 1.0f : (C * D) * iden;
                     float lm = overwrite ? 0.0f : loss_map[idx];
-                    if(WITH_L1) {
-                        const float2 pt = S.in[y + kR][x + kR];
-                        lm += l1_scale * fabsf(pt.x - pt.y);
-                    }
+                    if(WITH_L1) lm += l1_scale * fabsf(pred[idx] - target[idx]);
                     lm = border ? 0.0f : lm + ssim_scale * (1.0f - ssim);
                     loss_map[idx] = lm;
                     local_sum += lm;
@@ -215,14 +241,14 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                     float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f;
                     if(in_image && !border && den != 0.0f) {
                         const float cd = C * D;
-                        const float iden = 1.0f / den;
-                        d0 = (mu2 * 2.0f * D) * iden - (mu2 * 2.0f * C) * iden - (mu1 * 2.0f * cd) * iden / A
-                            + (mu1 * 2.0f * cd) * iden / B;
-                        d1 = -cd * iden / B;
+                        const float iA = rcp_approx(A), iB = rcp_approx(B);
+                        d0 = (mu2 * 2.0f * D) * iden - (mu2 * 2.0f * C) * iden - (mu1 * 2.0f * cd) * iden * iA
+                            + (mu1 * 2.0f * cd) * iden * iB;
+                        d1 = -cd * iden * iB;
                         d2 = (2.0f * C) * iden;
                     }
-                    S.part01[y][x] = make_float2(d0 * -ssim_grad_scale, d1 * -ssim_grad_scale);
-                    S.part2[y][x] = d2 * -ssim_grad_scale;
+                    S.u0.p.part01[y][x] = make_float2(d0 * -ssim_grad_scale, d1 * -ssim_grad_scale);
+                    S.u0.p.part2[y][x] = d2 * -ssim_grad_scale;
                 }
             }
         }
@@ -235,8 +261,8 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                 float c[18];
 #pragma unroll
                 for(int k = 0; k < 18; ++k) {
-                    v[k] = ld2(S.part01[y][x0 + k]);
-                    c[k] = S.part2[y][x0 + k];
+                    v[k] = ld2(S.u0.p.part01[y][x0 + k]);
+                    c[k] = S.u0.p.part2[y][x0 + k];
                 }
 #pragma unroll
                 for(int o = 0; o < 8; ++o) {
@@ -249,26 +275,27 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                     }
                     float a, b;
                     upk(acc, a, b);
-                    S.h2.d01[y][x0 + o] = make_float2(a, b);
-                    S.h2.d2[y][x0 + o] = accx;
+                    S.u1.h2.d01[y][x0 + o] = make_float2(a, b);
+                    S.u1.h2.d2[y][x0 + o] = accx;
                 }
             }
             __syncthreads();
-            /* stage 4: vertical blur, chain rule, L1 gradient; item = (column, run of 8 rows) */
-            for(int j = threadIdx.x; j < kOut * 4; j += kThreads) {
-                const int x = j % kOut, y0 = (j / kOut) * 8;
-                f2 b01[8];
-                float b2[8];
+            /* stage 4: vertical blur, chain rule, L1 gradient; item = (column, run of 4 rows): one
+             * item per thread */
+            for(int j = threadIdx.x; j < kOut * 8; j += kThreads) {
+                const int x = j % kOut, y0 = (j / kOut) * 4;
+                f2 b01[4];
+                float b2[4];
                 {
-                    f2 v[18];
-                    float c[18];
+                    f2 v[14];
+                    float c[14];
 #pragma unroll
-                    for(int k = 0; k < 18; ++k) {
-                        v[k] = ld2(S.h2.d01[y0 + k][x]);
-                        c[k] = S.h2.d2[y0 + k][x];
+                    for(int k = 0; k < 14; ++k) {
+                        v[k] = ld2(S.u1.h2.d01[y0 + k][x]);
+                        c[k] = S.u1.h2.d2[y0 + k][x];
                     }
 #pragma unroll
-                    for(int o = 0; o < 8; ++o) {
+                    for(int o = 0; o < 4; ++o) {
                         f2 acc = 0ull;
                         float accx = 0.0f;
 #pragma unroll
@@ -281,13 +308,12 @@ __global__ void __launch_bounds__(kThreads, 2) l1_ssim_kernel(const float *__res
                     }
                 }
 #pragma unroll
-                for(int o = 0; o < 8; ++o) {
+                for(int o = 0; o < 4; ++o) {
                     const int y = y0 + o;
                     const int gy = oy + y, gx = ox + x;
                     if(gy >= height || gx >= width) continue;
-                    const float2 pt = S.in[y + 2 * kR][x + 2 * kR];
-                    const float p = pt.x, t = pt.y;
                     const size_t idx = (size_t)plane * plane_elems + (size_t)gy * width + gx;
+                    const float p = pred[idx], t = target[idx];
                     float g = overwrite ? 0.0f : grad[idx];
                     if(WITH_L1) {
                         const float d = p - t;

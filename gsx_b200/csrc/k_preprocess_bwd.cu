@@ -15,7 +15,7 @@ namespace {
 
 constexpr int kThreads = 256;
 
-__global__ void __launch_bounds__(kThreads) preprocess_backward_kernel(
+__global__ void __launch_bounds__(kThreads, 4) preprocess_backward_kernel(
     const float *__restrict__ mean3d, const float *__restrict__ rotation, const float *__restrict__ logscale,
     const float *__restrict__ sh1, const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n,
     CameraParams cam, const uint32_t *__restrict__ counts, float4 *__restrict__ grad_acc, float *__restrict__ g_mean3d,

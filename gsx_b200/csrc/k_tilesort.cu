@@ -22,10 +22,7 @@
  *      determined.  Five size classes (up to 512, 1024, 2048, 4096 and 16384 instances), each launched
  *      over its own compact tile list (so a CTA's work follows its tile's size) and on its own
  *      stream, so that the classes run side by side.
- * No launch here needs a host read-back: the binning and the per-tile sort read the instance total and
- * the class sizes from the device, and a validity word from the tile scan switches them (and the
- * blend) off when the emission overflowed or a tile exceeds GSX_SEG_MAX; the host then redoes the
- * frame with grown buffers or with the global radix sort.
+ * The host falls back to the global radix sort when the largest tile exceeds GSX_SEG_MAX instances.
  */
 #include "gsx_b200_kernels.cuh"
 
@@ -48,11 +45,10 @@ __device__ __forceinline__ int size_class(uint32_t n)
 /* Tile scan, three launches (one thread per tile, 256 tiles per CTA):
  *   tile_reduce_kernel: per CTA, the sums of (instances, buckets, tiles per size class) and the
  *     largest tile -> block_aux[block * kAux + v] (the empty tiles form one more list, after the
- *     classes: the blend visits the lists from the largest class down to the empty tiles);
+ *     classes, so that the blend can visit the lists from the largest class down to the empty tiles);
  *   block_scan_aux_kernel (one CTA): exclusive scan of those over the CTAs; the class lists are laid
  *     end to end, class by class; words_out[0] = instance total, [1] = largest tile,
- *     [2 + c] = tiles of size class c, [2 + kClasses] = 1 if the emission did not overflow its capacity
- *     and the largest tile fits the per-tile sort (the frame needs no host decision), else 0;
+ *     [2 + c] = tiles of size class c;
  *   tile_write_kernel: ranges [start, end) (empty tiles [0, 0)), the inclusive bucket prefix, the
  *     class lists (each class in increasing tile order), and every sub-counter turned into the
  *     absolute end position of its slice of the tile's range. */
@@ -104,7 +100,6 @@ __global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_
 
 /* one CTA of 1024 threads, at most 1024 tile blocks (262144 tiles) */
 __global__ void __launch_bounds__(1024) block_scan_aux_kernel(uint32_t *__restrict__ block_aux, int n_blocks,
-                                                              const uint32_t *__restrict__ overflow,
                                                               uint32_t *__restrict__ words_out)
 {
     __shared__ uint32_t s_w[32][kAux];
@@ -157,9 +152,6 @@ __global__ void __launch_bounds__(1024) block_scan_aux_kernel(uint32_t *__restri
         words_out[1] = s_tot[kAux - 1];
 #pragma unroll
         for(int c = 0; c < kClasses; ++c) words_out[2 + c] = s_tot[2 + c];
-        /* the frame can be finished without the host: the emission kept every instance (no overflow
-         * of its capacity) and every tile fits the shared-memory sort */
-        words_out[2 + kClasses] = (overflow == nullptr || *overflow == 0u) && s_tot[kAux - 1] <= (uint32_t)GSX_SEG_MAX ? 1u : 0u;
     }
 }
 
@@ -233,8 +225,7 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const unsigned long lo
 {
     const uint64_t i = (uint64_t)blockIdx.x * kBinThreads + threadIdx.x;
     const uint64_t n = *d_total;
-    /* the total is what the emission kept (never above its capacity, max_n) */
-    if(i >= n || n > max_n) return;
+    if(i >= n || i >= max_n) return;
     const unsigned long long k = keys[i];
     const uint32_t tile = (uint32_t)(k >> 32);
     const uint32_t slot = atomicSub(&tile_end[GSX_SUBCOUNTER(tile, i & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u) - 1u;
@@ -248,10 +239,9 @@ __global__ void __launch_bounds__(kBinThreads) bin_kernel(const unsigned long lo
  * sorts the 4 depth bytes only; runs of equal depth (in arbitrary binning order) are then put in
  * primitive order in place, or, if one is longer than 32, the tile is reloaded and sorted on all 8
  * bytes, primitive bytes first. */
-template <int kThreads_, int kItems, int kClass>
+template <int kThreads_, int kItems>
 __global__ void __launch_bounds__(kThreads_) segsort_kernel(const uint2 *__restrict__ ranges,
-                                                            const uint32_t *__restrict__ class_tiles,
-                                                            const uint32_t *__restrict__ scan_words,
+                                                            const uint32_t *__restrict__ tile_list,
                                                             const unsigned long long *__restrict__ sort_keys,
                                                             unsigned long long *__restrict__ keys_out,
                                                             uint32_t *__restrict__ vals_out)
@@ -262,21 +252,12 @@ __global__ void __launch_bounds__(kThreads_) segsort_kernel(const uint2 *__restr
     uint32_t *s_wh = reinterpret_cast<uint32_t *>(s_key + kN);  /* kW * 256: per-warp digit counters, then their exclusive prefix */
     uint32_t *s_dbase = s_wh + kW * 256;                        /* 256: exclusive prefix of the block's digit counts */
     uint32_t *s_misc = s_dbase + 256;                           /* 32: per-warp digit totals; [8] = pass is the identity */
-    /* the grid is an upper bound of the class size: the tile scan's words give the class's tile count
-     * (CTAs past it exit at once), where its list starts (after the lists of the smaller classes), and
-     * whether the frame is valid at all (else the host redoes it) */
-    if(scan_words[2 + kClasses] == 0u) return;
-    uint32_t list0 = 0;
-#pragma unroll
-    for(int c = 0; c < kClass; ++c) list0 += scan_words[2 + c];
-    if(blockIdx.x >= scan_words[2 + kClass]) return;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned lt = (1u << lane) - 1u;
-    {
-    const int tile = (int)class_tiles[list0 + blockIdx.x];
+    const int tile = (int)tile_list[blockIdx.x];
     const uint2 r = ranges[tile];
     const int n = (int)(r.y - r.x);
     if(n <= 0 || n > kN) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned lt = (1u << lane) - 1u;
     for(int attempt = 0; attempt < 2; ++attempt) {
         /* element e of the current order sits at s_key[e]; thread (warp, lane) owns
          * e = warp * 32 * kItems + it * 32 + lane */
@@ -374,7 +355,6 @@ __global__ void __launch_bounds__(kThreads_) segsort_kernel(const uint2 *__restr
         keys_out[r.x + e] = thi | (s >> 32);
         vals_out[r.x + e] = (uint32_t)s;
     }
-    }
 }
 
 constexpr size_t segsort_smem(int threads, int items) { return (size_t)8 * threads * items + (size_t)4 * ((threads / 32) * 256 + 256 + 32); }
@@ -385,14 +365,13 @@ constexpr size_t segsort_smem(int threads, int items) { return (size_t)8 * threa
 size_t gsx_tile_scan_aux_words(int n_tiles) { return (size_t)((n_tiles + kTileThreads - 1) / kTileThreads) * kAux; }
 
 cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *ranges, uint32_t *bucket_offsets,
-                                 uint32_t *class_tiles, uint32_t *block_aux, const uint32_t *overflow,
-                                 uint32_t *words_out, cudaStream_t stream)
+                                 uint32_t *class_tiles, uint32_t *block_aux, uint32_t *words_out, cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
     const int blocks = (n_tiles + kTileThreads - 1) / kTileThreads;
     if(blocks > 1024) return cudaErrorInvalidValue;
     tile_reduce_kernel<<<blocks, kTileThreads, 0, stream>>>(tile_count, n_tiles, block_aux);
-    block_scan_aux_kernel<<<1, 1024, 0, stream>>>(block_aux, blocks, overflow, words_out);
+    block_scan_aux_kernel<<<1, 1024, 0, stream>>>(block_aux, blocks, words_out);
     tile_write_kernel<<<blocks, kTileThreads, 0, stream>>>(tile_count, n_tiles, block_aux, ranges, bucket_offsets, class_tiles);
     return cudaGetLastError();
 }
@@ -402,69 +381,25 @@ int gsx_tile_sort_classes() { return kClasses; }
 namespace {
 
 template <int C>
-cudaError_t launch_class(const uint2 *ranges, const uint32_t *class_tiles, const uint32_t *scan_words, uint32_t grid,
-                         const unsigned long long *sort_keys, unsigned long long *keys_out, uint32_t *vals_out, int dev,
-                         cudaStream_t stream)
+cudaError_t launch_class(const uint2 *ranges, const uint32_t *list, uint32_t count, const unsigned long long *sort_keys,
+                         unsigned long long *keys_out, uint32_t *vals_out, int dev, cudaStream_t stream)
 {
     static bool attr_done[256];
     constexpr int T = kClassThreads[C], I = kClassItems[C];
     static_assert((uint32_t)(T * I) == kClassMax[C], "class capacity");
-    auto kern = segsort_kernel<T, I, C>;
+    auto kern = segsort_kernel<T, I>;
     const size_t smem = segsort_smem(T, I);
-    if(grid == 0) return cudaSuccess;
+    if(count == 0) return cudaSuccess;
     if(smem > 48 * 1024 && (dev < 0 || dev >= 256 || !attr_done[dev])) {
         const cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if(err != cudaSuccess) return err;
         if(dev >= 0 && dev < 256) attr_done[dev] = true;
     }
-    kern<<<grid, T, smem, stream>>>(ranges, class_tiles, scan_words, sort_keys, keys_out, vals_out);
+    kern<<<count, T, smem, stream>>>(ranges, list, sort_keys, keys_out, vals_out);
     return cudaGetLastError();
 }
 
 } // namespace
-
-
-cudaError_t gsx_launch_tile_sort(uint64_t capacity, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
-                                 const uint32_t *scan_words, const unsigned long long *sort_keys,
-                                 unsigned long long *keys_out, uint32_t *vals_out, cudaStream_t stream,
-                                 cudaStream_t const *side, cudaEvent_t const *ev, int *out_launches)
-{
-    *out_launches = 0;
-    static_assert(kClassMax[kClasses - 1] == GSX_SEG_MAX, "the largest class covers up to GSX_SEG_MAX");
-    static_assert(kClasses == GSX_SORT_CLASSES, "class count");
-    if(capacity == 0 || n_tiles <= 0) return cudaSuccess;
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if(err != cudaSuccess) return err;
-    /* fork: class c > 0 runs on side[c - 1] after the binning, class 0 on the caller's stream; join.
-     * Grids: the class sizes live on the device; a class holds at most n_tiles tiles, and at most
-     * capacity / (smallest size of the class) of them */
-    err = cudaEventRecord(ev[0], stream);
-    if(err != cudaSuccess) return err;
-    cudaError_t (*launchers[kClasses])(const uint2 *, const uint32_t *, const uint32_t *, uint32_t,
-                                       const unsigned long long *, unsigned long long *, uint32_t *, int, cudaStream_t) = {
-        launch_class<0>, launch_class<1>, launch_class<2>, launch_class<3>, launch_class<4> };
-    for(int c = 0; c < kClasses; ++c) {
-        const uint64_t smallest = c == 0 ? 1u : (uint64_t)kClassMax[c - 1] + 1u;
-        uint64_t bound = capacity / smallest < (uint64_t)n_tiles ? capacity / smallest : (uint64_t)n_tiles;
-        if(bound == 0) continue;
-        cudaStream_t st = stream;
-        if(c > 0) {
-            st = side[c - 1];
-            err = cudaStreamWaitEvent(st, ev[0], 0);
-            if(err != cudaSuccess) return err;
-        }
-        err = launchers[c](ranges, class_tiles, scan_words, (uint32_t)bound, sort_keys, keys_out, vals_out, dev, st);
-        if(err != cudaSuccess) return err;
-        ++*out_launches;
-        if(c > 0) {
-            err = cudaEventRecord(ev[c], st);
-            if(err == cudaSuccess) err = cudaStreamWaitEvent(stream, ev[c], 0);
-            if(err != cudaSuccess) return err;
-        }
-    }
-    return cudaSuccess;
-}
 
 cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *vals, const uint32_t *d_total,
                                 uint64_t max_n, int n_tiles, uint32_t *tile_end, unsigned long long *sort_keys,
@@ -474,4 +409,41 @@ cudaError_t gsx_launch_tile_bin(const unsigned long long *keys, const uint32_t *
     bin_kernel<<<(unsigned)((max_n + kBinThreads - 1) / kBinThreads), kBinThreads, 0, stream>>>(keys, vals, d_total, max_n,
                                                                                               n_tiles, tile_end, sort_keys);
     return cudaGetLastError();
+}
+
+cudaError_t gsx_launch_tile_sort(uint64_t n, int n_tiles, const uint2 *ranges, const uint32_t *class_tiles,
+                                 const uint32_t *class_counts, const unsigned long long *sort_keys,
+                                 unsigned long long *keys_out, uint32_t *vals_out, cudaStream_t stream,
+                                 cudaStream_t const *side, cudaEvent_t const *ev)
+{
+    static_assert(kClassMax[kClasses - 1] == GSX_SEG_MAX, "the largest class covers up to GSX_SEG_MAX");
+    static_assert(kClasses == GSX_SORT_CLASSES, "class count");
+    if(n == 0 || n_tiles <= 0) return cudaSuccess;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if(err != cudaSuccess) return err;
+    /* fork: class c > 0 runs on side[c - 1] after the binning, class 0 on the caller's stream; join */
+    err = cudaEventRecord(ev[0], stream);
+    if(err != cudaSuccess) return err;
+    cudaError_t (*launchers[kClasses])(const uint2 *, const uint32_t *, uint32_t, const unsigned long long *,
+                                       unsigned long long *, uint32_t *, int, cudaStream_t) = {
+        launch_class<0>, launch_class<1>, launch_class<2>, launch_class<3>, launch_class<4> };
+    const uint32_t *list = class_tiles;
+    for(int c = 0; c < kClasses; ++c) {
+        cudaStream_t st = stream;
+        if(c > 0 && class_counts[c] > 0) {
+            st = side[c - 1];
+            err = cudaStreamWaitEvent(st, ev[0], 0);
+            if(err != cudaSuccess) return err;
+        }
+        err = launchers[c](ranges, list, class_counts[c], sort_keys, keys_out, vals_out, dev, st);
+        if(err != cudaSuccess) return err;
+        if(c > 0 && class_counts[c] > 0) {
+            err = cudaEventRecord(ev[c], st);
+            if(err == cudaSuccess) err = cudaStreamWaitEvent(stream, ev[c], 0);
+            if(err != cudaSuccess) return err;
+        }
+        list += class_counts[c];
+    }
+    return cudaSuccess;
 }
