@@ -141,6 +141,9 @@ struct gsx_b200_context {
     uint32_t *host_hist = nullptr; /* pinned copy of hist */
     /* per tile / pixel / bucket */
     DevBuf ranges, bucket_offsets, tile_max, pix, bucket_tile, snap, tile_count, class_tiles, tile_aux;
+    /* TRAIN: per tile the pixel order by last contributor, per bucket the pixels its backward walks,
+     * and the backward's bucket order and its counting-sort state */
+    DevBuf tile_order, bucket_active, bucket_order, bucket_sort;
     /* small device words: [0] sticky flags, [1] the emission's overflow bit; from the tile scan: [2] instance total, [3] largest tile,
      * [4..8] tiles per per-tile-sort size class */
     DevBuf words;
@@ -254,7 +257,8 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
     DevBuf *all[] = { &ctx->rec, &ctx->offsets, &ctx->counts, &ctx->tile_masks, &ctx->block_sums, &ctx->grad_acc, &ctx->keys, &ctx->vals,
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
                       &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->tile_aux, &ctx->words, &ctx->hist,
-                      &ctx->fingerprint, &ctx->refresh_rgb };
+                      &ctx->fingerprint, &ctx->refresh_rgb, &ctx->tile_order, &ctx->bucket_active, &ctx->bucket_order,
+                      &ctx->bucket_sort };
     for(DevBuf *b : all) release(*b);
     if(ctx->ev_created)
         for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
@@ -440,9 +444,12 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
     ctx->n_instances = total;
     const uint64_t bucket_cap = (total + 31) / 32 + (uint64_t)n_tiles;
     if(forward_type == GSX_B200_FORWARD_TRAIN) {
-        /* bucket snapshots and the bucket -> tile table exist for the backward only */
+        /* bucket snapshots, the bucket -> tile table, the per-tile pixel order and the per-bucket pixel
+         * counts exist for the backward only */
         if(int rc = ensure(ctx->bucket_tile, sizeof(uint32_t) * (size_t)bucket_cap)) return rc;
         if(int rc = ensure(ctx->snap, sizeof(float4) * GSX_TILE_PIXELS * (size_t)bucket_cap)) return rc;
+        if(int rc = ensure(ctx->bucket_active, sizeof(uint16_t) * (size_t)bucket_cap)) return rc;
+        if(int rc = ensure(ctx->tile_order, (size_t)GSX_TILE_PIXELS * (size_t)n_tiles)) return rc;
     }
     const uint64_t kcap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
     unsigned long long *keys_a = (unsigned long long *)ctx->keys.ptr;
@@ -483,7 +490,8 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
                                           (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
                                           out_rgb, out_bf16, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
                                           (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr,
-                                          forward_type == GSX_B200_FORWARD_TRAIN, class_tiles, words + 4, stream),
+                                          forward_type == GSX_B200_FORWARD_TRAIN, class_tiles, words + 4,
+                                          (uint8_t *)ctx->tile_order.ptr, (uint16_t *)ctx->bucket_active.ptr, stream),
                  "blend launch");
     ctx->launches += n_tiles > 0 ? 1 : 0;
     }
@@ -587,14 +595,18 @@ int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const
     const uint32_t *vals = ctx->keys_in_b ? vals_a + ctx->vals.bytes / (2 * sizeof(uint32_t)) : vals_a;
     if(ctx->n_instances > 0) {
         StageTimer st(ctx, 5, stream);
-        GSX_CUDA_TRY(gsx_launch_blend_backward(ctx->cam.width, ctx->cam.height, ctx->cam.trow0 * GSX_TILE, ctx->cam.grid_w, (const uint2 *)ctx->ranges.ptr,
-                                               (const uint32_t *)ctx->bucket_offsets.ptr,
-                                               (const uint32_t *)ctx->bucket_tile.ptr, ctx->bucket_cap, ctx->n_tiles, vals,
+        if(int rc = ensure(ctx->bucket_order, sizeof(uint32_t) * (size_t)ctx->bucket_cap)) return rc;
+        if(int rc = ensure(ctx->bucket_sort, sizeof(uint32_t) * gsx_bucket_sort_state_words())) return rc;
+        GSX_CUDA_TRY(gsx_launch_blend_backward(ctx->cam.width, ctx->cam.height, ctx->cam.trow0 * GSX_TILE, ctx->cam.grid_w,
+                                               (const uint2 *)ctx->ranges.ptr, (const uint32_t *)ctx->bucket_offsets.ptr,
+                                               (const uint32_t *)ctx->bucket_tile.ptr, ctx->bucket_cap, ctx->n_tiles,
+                                               (const uint16_t *)ctx->bucket_active.ptr, (const uint8_t *)ctx->tile_order.ptr,
+                                               (uint32_t *)ctx->bucket_order.ptr, (uint32_t *)ctx->bucket_sort.ptr, vals,
                                                (const PrimRec *)ctx->rec.ptr, (const float4 *)ctx->pix.ptr,
-                                               (const uint32_t *)ctx->tile_max.ptr, (const float4 *)ctx->snap.ptr, grad_rgb,
-                                               (float4 *)ctx->grad_acc.ptr, n, ctx->aux_absgrad != nullptr, stream),
+                                               (const float4 *)ctx->snap.ptr, grad_rgb, (float4 *)ctx->grad_acc.ptr,
+                                               ctx->aux_absgrad != nullptr, stream),
                      "blend backward launch");
-        ctx->launches += 1;
+        ctx->launches += 3;
     }
     StageTimer st6(ctx, 6, stream);
     GSX_CUDA_TRY(gsx_launch_preprocess_backward(ctx->g.mean3d, ctx->g.rotation, ctx->g.logscale, ctx->g.sh1, ctx->g.sh2,

@@ -172,17 +172,25 @@ cudaError_t gsx_launch_tile_sort(uint64_t n, int n_tiles, const uint2 *ranges, c
 /* out_rgb: [3, height, width] f32, or bf16 (round to nearest even) when out_bf16; row0 = first pixel
  * row of the band in the full frame (a multiple of 16, 0 for a full frame) */
 /* tile_lists / class_sizes (may be NULL): the tile scan's class lists (classes 0..4 end to end, then
- * the empty tiles) and the device class sizes; CTAs then take tiles from the largest class down */
+ * the empty tiles) and the device class sizes; CTAs then take tiles from the largest class down.
+ * TRAIN: tile_order [n_tiles * 256] receives each tile's pixel ranks by decreasing last-contributor
+ * bucket, bucket_active [buckets] the number of pixels the backward walks in each bucket. */
 cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w, int n_tiles, const uint2 *ranges,
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
                                      float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *tile_lists,
-                                     const uint32_t *class_sizes, cudaStream_t stream);
+                                     const uint32_t *class_sizes, uint8_t *tile_order, uint16_t *bucket_active,
+                                     cudaStream_t stream);
+/* Blend backward of a TRAIN forward: orders the buckets by the number of pixels they walk
+ * (bucket_active, tile_order from the forward; bucket_order [buckets] and sort_state
+ * [gsx_bucket_sort_state_words()] are scratch), then the reverse blend into grad_acc */
+size_t gsx_bucket_sort_state_words();
 cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_w, const uint2 *ranges,
-                                      const uint32_t *bucket_offsets, const uint32_t *bucket_tile, uint64_t bucket_capacity,
-                                      int n_tiles, const uint32_t *vals, const PrimRec *rec, const float4 *pix,
-                                      const uint32_t *tile_max, const float4 *snap, const float *grad_rgb,
-                                      float4 *grad_acc, int64_t n, bool abs_grad, cudaStream_t stream);
+                                      const uint32_t *bucket_offsets, const uint32_t *bucket_tile,
+                                      uint64_t bucket_capacity, int n_tiles, const uint16_t *bucket_active,
+                                      const uint8_t *tile_order, uint32_t *bucket_order, uint32_t *sort_state,
+                                      const uint32_t *vals, const PrimRec *rec, const float4 *pix, const float4 *snap,
+                                      const float *grad_rgb, float4 *grad_acc, bool abs_grad, cudaStream_t stream);
 cudaError_t gsx_launch_preprocess_backward(const float *mean3d, const float *rotation, const float *logscale,
                                            const float *sh1, const float *sh2, const float *sh3, int sh_degree,
                                            int64_t n, const CameraParams &cam, const uint32_t *counts,

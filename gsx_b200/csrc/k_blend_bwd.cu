@@ -119,15 +119,67 @@ __device__ __forceinline__ void cp_async_wait()
 
 __device__ __forceinline__ f2 abs2(f2 a) { return a & 0x7fffffff7fffffffull; }
 
+/* Buckets grouped by the number of pixels they walk (bucket_active, from the TRAIN forward): a counting
+ * sort, descending, of the buckets with at least one pixel to walk, so that the four buckets of a warp
+ * walk about as many pixels each.  bucket_sort_state: [0, 257) histogram, [257, 514) cursors, [514]
+ * number of listed buckets; zeroed before the histogram. */
+constexpr int kCountBins = GSX_TILE_PIXELS + 1;
+
+__global__ void __launch_bounds__(256) bucket_hist_kernel(const uint32_t *__restrict__ bucket_offsets, int n_tiles,
+                                                          const uint16_t *__restrict__ bucket_active,
+                                                          uint32_t *__restrict__ state)
+{
+    __shared__ uint32_t h[kCountBins];
+    for(int k = threadIdx.x; k < kCountBins; k += 256) h[k] = 0u;
+    __syncthreads();
+    const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
+    for(uint32_t b = blockIdx.x * 256u + threadIdx.x; b < n_buckets; b += gridDim.x * 256u) atomicAdd(&h[bucket_active[b]], 1u);
+    __syncthreads();
+    for(int k = threadIdx.x; k < kCountBins; k += 256)
+        if(h[k]) atomicAdd(&state[k], h[k]);
+}
+
+__global__ void __launch_bounds__(256) bucket_scatter_kernel(const uint32_t *__restrict__ bucket_offsets, int n_tiles,
+                                                             const uint16_t *__restrict__ bucket_active,
+                                                             uint32_t *__restrict__ state, uint32_t *__restrict__ order)
+{
+    /* start[c] = buckets with a count above c (descending order), for c = 1..256; thread t owns c = t + 1 */
+    __shared__ uint32_t start[kCountBins];
+    __shared__ uint32_t s_warp[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t v = state[threadIdx.x + 1];
+    uint32_t incl = v;
+#pragma unroll
+    for(int d = 1; d < 32; d <<= 1) {
+        const uint32_t x = __shfl_down_sync(0xffffffffu, incl, d);
+        if(lane + d < 32) incl += x;
+    }
+    if(lane == 0) s_warp[warp] = incl;
+    __syncthreads();
+    uint32_t above = incl - v;
+    for(int w = warp + 1; w < 8; ++w) above += s_warp[w];
+    start[threadIdx.x + 1] = above;
+    if(blockIdx.x == 0 && threadIdx.x == 0) state[2 * kCountBins] = s_warp[0] + s_warp[1] + s_warp[2] + s_warp[3] +
+                                                                   s_warp[4] + s_warp[5] + s_warp[6] + s_warp[7];
+    __syncthreads();
+    const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
+    for(uint32_t b = blockIdx.x * 256u + threadIdx.x; b < n_buckets; b += gridDim.x * 256u) {
+        const uint32_t c = bucket_active[b];
+        if(c == 0u) continue;
+        order[start[c] + atomicAdd(&state[kCountBins + c], 1u)] = b;
+    }
+}
+
 /* kAbs: also accumulate sum over pixels of |d loss / d mean2d| per component (the absolute
  * screen-space gradient behind GSX's gs_absgrad_acc), into grad_acc[3i+2].yz */
 template <bool kAbs>
 __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
-    int width, int height, int row0, int grid_w, int n_tiles, const uint2 *__restrict__ ranges,
+    int width, int height, int row0, int grid_w, const uint2 *__restrict__ ranges,
     const uint32_t *__restrict__ bucket_offsets, const uint32_t *__restrict__ bucket_tile,
+    const uint32_t *__restrict__ bucket_order, const uint32_t *__restrict__ sort_state,
+    const uint16_t *__restrict__ bucket_active, const uint8_t *__restrict__ tile_order,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, const float4 *__restrict__ pix,
-    const uint32_t *__restrict__ tile_max, const float4 *__restrict__ snap, const float *__restrict__ grad_rgb,
-    float4 *__restrict__ grad_acc)
+    const float4 *__restrict__ snap, const float *__restrict__ grad_rgb, float4 *__restrict__ grad_acc)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     /* per warp, per segment: 2 x 32 PixIn + one float4 of padding, so the four segment heads read
@@ -135,21 +187,27 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     SegStage *s_in = reinterpret_cast<SegStage *>(smem_raw);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sub = lane & 7;
-    const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
-    const uint32_t bucket = ((uint32_t)blockIdx.x * kWarps + warp) * 4u + (uint32_t)(lane >> 3);
-    bool seg_active = bucket < n_buckets;
-    uint32_t tile = 0;
-    int n_inst = 0, tb = 0;
+    /* the warp's four buckets: consecutive entries of the bucket order (grouped by pixel count) */
+    const uint32_t n_listed = sort_state[2 * kCountBins];
+    const uint32_t slot = ((uint32_t)blockIdx.x * kWarps + warp) * 4u + (uint32_t)(lane >> 3);
+    const bool seg_active = slot < n_listed;
+    if(__ballot_sync(0xffffffffu, seg_active) == 0) return;
+    uint32_t tile = 0, bucket = 0;
+    int n_inst = 0, tb = 0, n_pix = 0;
     uint32_t inst0 = 0;
     if(seg_active) {
+        bucket = bucket_order[slot];
         tile = bucket_tile[bucket];
         const uint2 range = ranges[tile];
         inst0 = range.x;
         n_inst = (int)(range.y - range.x);
         tb = (int)(bucket - (tile == 0 ? 0u : bucket_offsets[tile - 1]));
-        seg_active = (uint32_t)tb * 32u < tile_max[tile];
+        n_pix = (int)bucket_active[bucket];
     }
-    if(__ballot_sync(0xffffffffu, seg_active) == 0) return;
+    /* the pixels a segment walks: the first n_pix of its tile's order (last contributor beyond the
+     * bucket's start); the warp runs until its longest segment is done */
+    const int steps = __reduce_max_sync(0xffffffffu, (unsigned)n_pix) + 7;
+    const uint8_t *order = tile_order + (size_t)tile * GSX_TILE_PIXELS;
 
     /* this lane's four instances, as two pairs */
     FragPair f[kPerLane / 2];
@@ -201,21 +259,24 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     const int seg = lane >> 3;
     PixIn(*stage)[32] = s_in[warp * 4 + seg].buf;
 
-    /* the 8 lanes of a segment prefetch 32 pixels' inputs (snapshot, composed colour + last
-     * contributor, upstream gradient) into shared memory, one batch ahead, with cp.async */
+    /* the 8 lanes of a segment prefetch the inputs of 32 list positions (snapshot, composed colour +
+     * last contributor, upstream gradient, and the pixel's rank in the tile) into shared memory, one
+     * batch ahead, with cp.async */
     auto prefetch = [&](int batch) {
         PixIn *dst = stage[batch & 1];
 #pragma unroll
         for(int q = 0; q < 4; ++q) {
-            const int pl = sub + 8 * q, p = batch * 32 + pl;
-            const int qx = tx0 + (p & (GSX_TILE - 1)), qy = ty0 + (p >> 4);
-            if(seg_active && qx < width && qy < height) {
+            const int pl = sub + 8 * q, j = batch * 32 + pl;
+            if(j < n_pix) {
+                const int p = order[j];
+                const int qx = tx0 + (p & (GSX_TILE - 1)), qy = ty0 + (p >> 4);
                 const size_t idx = (size_t)qy * (size_t)width + (size_t)qx;
                 cp_async16(&dst[pl].snap, bsnap + p);
                 cp_async16(&dst[pl].img, pix + idx);
                 cp_async4(&dst[pl].grad.x, grad_rgb + idx);
                 cp_async4(&dst[pl].grad.y, grad_rgb + P + idx);
                 cp_async4(&dst[pl].grad.z, grad_rgb + 2 * P + idx);
+                dst[pl].grad.w = __int_as_float(p);
             }
         }
         cp_async_commit();
@@ -226,11 +287,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
      * contributor, transmittance, and nadg = -(colour still to come) . (upstream gradient), kept as one
      * scalar because every fragment raises it by w * (colour . gradient) */
     float gr = 0.0f, gg = 0.0f, gb = 0.0f, nadg = 0.0f, T = 0.0f;
-    int last = 0;
-    for(int i = 0; i < GSX_TILE_PIXELS + 7; ++i) {
-        if((i & 31) == 0 && i < GSX_TILE_PIXELS) {
+    int last = 0, rank = 0;
+    for(int i = 0; i < steps; ++i) {
+        if((i & 31) == 0 && i < steps - 7) {
             __syncwarp();
-            if(i + 32 < GSX_TILE_PIXELS) {
+            if(i + 32 < steps - 7) {
                 prefetch((i >> 5) + 1);
                 cp_async_wait<1>();
             } else {
@@ -244,11 +305,11 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
         nadg = __shfl_up_sync(0xffffffffu, nadg, 1);
         T = __shfl_up_sync(0xffffffffu, T, 1);
         last = __shfl_up_sync(0xffffffffu, last, 1);
-        const int p = i - sub;
-        const int qx = tx0 + (p & (GSX_TILE - 1)), qy = ty0 + (p >> 4);
-        const bool valid = seg_active && p >= 0 && p < GSX_TILE_PIXELS && qx < width && qy < height;
+        rank = __shfl_up_sync(0xffffffffu, rank, 1);
+        const int pos = i - sub; /* this lane's list position */
+        const bool valid = pos >= 0 && pos < n_pix;
         if(sub == 0) {
-            /* segment head: this bucket's inputs for pixel p (= i) */
+            /* segment head: this bucket's inputs for list position i */
             last = 0;
             if(valid) {
                 const PixIn &in = stage[(i >> 5) & 1][i & 31];
@@ -256,14 +317,14 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
                 gr = in.grad.x;
                 gg = in.grad.y;
                 gb = in.grad.z;
+                rank = __float_as_int(in.grad.w);
                 last = (int)__float_as_uint(img.w);
                 nadg = (sn.x - img.x) * gr + (sn.y - img.y) * gg + (sn.z - img.z) * gb;
                 T = sn.w;
             }
         }
-        /* whole warp past every pixel's last contributor: nothing to add, state unchanged */
-        if(!__any_sync(0xffffffffu, valid && tpi[0] < last)) continue;
         if(!valid) continue;
+        const int qx = tx0 + (rank & (GSX_TILE - 1)), qy = ty0 + (rank >> 4);
         /* full-frame pixel coordinates (a band starts at row row0) */
         const f2 fx2 = pk((float)qx, (float)qx), fy2 = pk((float)(qy + row0), (float)(qy + row0));
         const f2 gr2 = pk(gr, gr), gg2 = pk(gg, gg), gb2 = pk(gb, gb);
@@ -355,21 +416,31 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
 
 } // namespace
 
+size_t gsx_bucket_sort_state_words() { return 2 * kCountBins + 1; }
+
 cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_w, const uint2 *ranges,
                                       const uint32_t *bucket_offsets, const uint32_t *bucket_tile,
-                                      uint64_t bucket_capacity, int n_tiles, const uint32_t *vals, const PrimRec *rec,
-                                      const float4 *pix, const uint32_t *tile_max, const float4 *snap,
-                                      const float *grad_rgb, float4 *grad_acc, int64_t n, bool abs_grad,
-                                      cudaStream_t stream)
+                                      uint64_t bucket_capacity, int n_tiles, const uint16_t *bucket_active,
+                                      const uint8_t *tile_order, uint32_t *bucket_order, uint32_t *sort_state,
+                                      const uint32_t *vals, const PrimRec *rec, const float4 *pix, const float4 *snap,
+                                      const float *grad_rgb, float4 *grad_acc, bool abs_grad, cudaStream_t stream)
 {
-    (void)n;
     if(bucket_capacity == 0 || n_tiles <= 0) return cudaSuccess;
+    /* the bucket order: histogram of the pixel counts, then the scatter (both read the bucket count
+     * on the device; grids sized by the capacity, grid-stride loops) */
+    cudaError_t err = cudaMemsetAsync(sort_state, 0, sizeof(uint32_t) * gsx_bucket_sort_state_words(), stream);
+    if(err != cudaSuccess) return err;
+    uint64_t sblocks = (bucket_capacity + 255) / 256;
+    if(sblocks > 148 * 8) sblocks = 148 * 8;
+    bucket_hist_kernel<<<(unsigned)sblocks, 256, 0, stream>>>(bucket_offsets, n_tiles, bucket_active, sort_state);
+    bucket_scatter_kernel<<<(unsigned)sblocks, 256, 0, stream>>>(bucket_offsets, n_tiles, bucket_active, sort_state,
+                                                                 bucket_order);
     const uint64_t per_block = (uint64_t)kWarps * 4;
     const uint64_t blocks = (bucket_capacity + per_block - 1) / per_block;
     const size_t smem = sizeof(SegStage) * kWarps * 4;
     static bool attr_done[2][256];
     int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
+    err = cudaGetDevice(&dev);
     if(err != cudaSuccess) return err;
     auto kernel = abs_grad ? blend_backward_kernel<true> : blend_backward_kernel<false>;
     if(dev < 0 || dev >= 256 || !attr_done[abs_grad][dev]) {
@@ -377,8 +448,8 @@ cudaError_t gsx_launch_blend_backward(int width, int height, int row0, int grid_
         if(err != cudaSuccess) return err;
         if(dev >= 0 && dev < 256) attr_done[abs_grad][dev] = true;
     }
-    kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, row0, grid_w, n_tiles, ranges,
-                                                                      bucket_offsets, bucket_tile, vals, rec, pix,
-                                                                      tile_max, snap, grad_rgb, grad_acc);
+    kernel<<<(unsigned)blocks, kThreads, smem, stream>>>(width, height, row0, grid_w, ranges, bucket_offsets, bucket_tile,
+                                                         bucket_order, sort_state, bucket_active, tile_order, vals, rec,
+                                                         pix, snap, grad_rgb, grad_acc);
     return cudaGetLastError();
 }

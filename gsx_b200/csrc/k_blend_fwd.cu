@@ -6,9 +6,10 @@
  * alpha = min(opacity * exp(-sigma), 0.999), fragments with sigma < 0 or alpha < 1/255 skipped,
  * the pixel stops after the fragment that takes transmittance below 1e-4, a (colour,
  * transmittance) snapshot per pixel before every 32-instance bucket for the backward pass
- * (written for every bucket of every batch the tile processes, as the reference does; TRAIN
- * forwards only, an INFERENCE forward has no backward), and
- * out = colour + (1 - alpha) * background.
+ * (TRAIN forwards only, an INFERENCE forward has no backward; skipped for a pixel already finished,
+ * whose backward never reaches the bucket), and out = colour + (1 - alpha) * background.  TRAIN
+ * forwards also order each tile's pixels by last contributor and count, per bucket, the pixels the
+ * backward has to walk.
  *
  * B200 organisation: each warp owns an 8x4 pixel block of the tile.  After a round of up to 512
  * instances is staged in shared memory (long rounds keep the warps, whose lists differ in length,
@@ -30,6 +31,7 @@ namespace {
 constexpr int kThreads = GSX_TILE_PIXELS;
 constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 512; /* instances staged per round: 2 per thread */
+constexpr int kKeyMax = 511; /* last-contributor bucket keys above this share one bin */
 
 struct FwdSmem {
     float4 a[kChunk]; /* mean2d.x, mean2d.y, conic.x / 2, conic.y */
@@ -116,11 +118,12 @@ __device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, f
 }
 
 template <bool kTrain, bool kBF16>
-__global__ void __launch_bounds__(kThreads) blend_forward_kernel(
+__global__ void __launch_bounds__(kThreads, 5) blend_forward_kernel(
     int width, int height, int row0, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, void *__restrict__ out_rgb,
     float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile,
-    const uint32_t *__restrict__ tile_lists, const uint32_t *__restrict__ class_sizes)
+    const uint32_t *__restrict__ tile_lists, const uint32_t *__restrict__ class_sizes, uint8_t *__restrict__ tile_order,
+    uint16_t *__restrict__ bucket_active)
 {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem &S = *reinterpret_cast<FwdSmem *>(smem_raw);
@@ -204,7 +207,9 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
         int li = 0;
         for(int kb = 0; kb * 32 < batch; ++kb) {
             if(kTrain) {
-                snap[(size_t)bucket * kThreads + prank] = make_float4(cr, cg, cb, T);
+                /* a finished pixel (or one outside the image) has its last contributor before this
+                 * bucket: the backward never reads its snapshot here */
+                if(!done) snap[(size_t)bucket * kThreads + prank] = make_float4(cr, cg, cb, T);
                 ++bucket;
             }
             const int bend = (kb + 1) * 32;
@@ -284,6 +289,48 @@ __global__ void __launch_bounds__(kThreads) blend_forward_kernel(
         for(int w = 0; w < kWarps; ++w) mm = max(mm, s_max[w]);
         tile_max[tile] = mm;
     }
+    if(kTrain) {
+        /* For the backward: the tile's pixels ordered by decreasing last-contributor bucket
+         * (key = ceil(last / 32), capped at kKeyMax), and per bucket b of the tile the number of pixels
+         * whose last contributor lies beyond the bucket's start (key > b): the pixels the backward
+         * walks for that bucket are the first count(b) of the order.  A counting sort in shared
+         * memory (the instance lists are dead by now); the order within one key is arbitrary. */
+        static_assert((kKeyMax + 1) == 2 * kThreads, "two key bins per thread");
+        uint32_t *s_cnt = reinterpret_cast<uint32_t *>(&S.list[0][0]); /* kKeyMax + 1 bins */
+        uint32_t *s_warp = s_cnt + (kKeyMax + 1);                    /* kWarps partial sums */
+        const uint32_t key = inside ? min((ncon + 31u) / 32u, (uint32_t)kKeyMax) : 0u;
+        for(int k = threadIdx.x; k <= kKeyMax; k += kThreads) s_cnt[k] = 0u;
+        __syncthreads();
+        atomicAdd(&s_cnt[key], 1u);
+        __syncthreads();
+        /* descending exclusive scan: s_cnt[k] <- number of pixels with a key above k; thread t owns
+         * bins 2t and 2t + 1 */
+        const int k0 = 2 * (int)threadIdx.x, k1 = k0 + 1;
+        const uint32_t h0 = s_cnt[k0], h1 = s_cnt[k1];
+        /* suffix sums over threads: reverse the thread order into an inclusive prefix scan */
+        uint32_t v = h0 + h1, incl = v;
+#pragma unroll
+        for(int d = 1; d < 32; d <<= 1) {
+            const uint32_t x = __shfl_down_sync(0xffffffffu, incl, d);
+            if(lane + d < 32) incl += x;
+        }
+        if(lane == 0) s_warp[warp] = incl;
+        __syncthreads();
+        uint32_t above = incl - v; /* bins beyond this thread's pair, within the warp */
+        for(int w = warp + 1; w < kWarps; ++w) above += s_warp[w];
+        __syncthreads();
+        s_cnt[k0] = above + h1;
+        s_cnt[k1] = above;
+        __syncthreads();
+        /* count(b) = pixels with key > min(b, kKeyMax - 1): conservative for the capped keys */
+        const uint32_t b0 = tile == 0 ? 0u : bucket_offsets[tile - 1], nb = bucket_offsets[tile] - b0;
+        for(uint32_t b = threadIdx.x; b < nb; b += kThreads)
+            bucket_active[b0 + b] = (uint16_t)s_cnt[b < (uint32_t)kKeyMax ? b : (uint32_t)kKeyMax - 1u];
+        __syncthreads();
+        /* position: pixels with a larger key first, then a slot within the key */
+        const uint32_t pos = atomicAdd(&s_cnt[key], 1u);
+        tile_order[(size_t)tile * kThreads + pos] = (uint8_t)prank;
+    }
 }
 
 } // namespace
@@ -292,7 +339,8 @@ cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w
                                      const uint32_t *bucket_offsets, const uint32_t *vals, const PrimRec *rec,
                                      const float bg[3], void *out_rgb, bool out_bf16, float4 *pix, uint32_t *tile_max,
                                      float4 *snap, uint32_t *bucket_tile, bool train, const uint32_t *tile_lists,
-                                     const uint32_t *class_sizes, cudaStream_t stream)
+                                     const uint32_t *class_sizes, uint8_t *tile_order, uint16_t *bucket_active,
+                                     cudaStream_t stream)
 {
     if(n_tiles <= 0) return cudaSuccess;
     static bool attr_done[4][256];
@@ -309,6 +357,7 @@ cudaError_t gsx_launch_blend_forward(int width, int height, int row0, int grid_w
     }
     kern<<<(unsigned)n_tiles, kThreads, sizeof(FwdSmem), stream>>>(width, height, row0, grid_w, ranges, bucket_offsets, vals,
                                                                    rec, make_float3(bg[0], bg[1], bg[2]), out_rgb, pix,
-                                                                   tile_max, snap, bucket_tile, tile_lists, class_sizes);
+                                                                   tile_max, snap, bucket_tile, tile_lists, class_sizes,
+                                                                   tile_order, bucket_active);
     return cudaGetLastError();
 }
