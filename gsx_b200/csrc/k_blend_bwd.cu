@@ -125,6 +125,15 @@ __device__ __forceinline__ f2 abs2(f2 a) { return a & 0x7fffffff7fffffffull; }
  * number of listed buckets; zeroed before the histogram. */
 constexpr int kCountBins = GSX_TILE_PIXELS + 1;
 
+/* each CTA owns one contiguous chunk of the bucket list (neighbouring tiles stay together inside a
+ * count) */
+__device__ __forceinline__ void bucket_chunk(uint32_t n_buckets, uint32_t &b0, uint32_t &b1)
+{
+    const uint32_t chunk = (n_buckets + gridDim.x - 1) / gridDim.x;
+    b0 = blockIdx.x * chunk;
+    b1 = min(n_buckets, b0 + chunk);
+}
+
 __global__ void __launch_bounds__(256) bucket_hist_kernel(const uint32_t *__restrict__ bucket_offsets, int n_tiles,
                                                           const uint16_t *__restrict__ bucket_active,
                                                           uint32_t *__restrict__ state)
@@ -132,8 +141,9 @@ __global__ void __launch_bounds__(256) bucket_hist_kernel(const uint32_t *__rest
     __shared__ uint32_t h[kCountBins];
     for(int k = threadIdx.x; k < kCountBins; k += 256) h[k] = 0u;
     __syncthreads();
-    const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
-    for(uint32_t b = blockIdx.x * 256u + threadIdx.x; b < n_buckets; b += gridDim.x * 256u) atomicAdd(&h[bucket_active[b]], 1u);
+    uint32_t b0, b1;
+    bucket_chunk(bucket_offsets[n_tiles - 1], b0, b1);
+    for(uint32_t b = b0 + threadIdx.x; b < b1; b += 256u) atomicAdd(&h[bucket_active[b]], 1u);
     __syncthreads();
     for(int k = threadIdx.x; k < kCountBins; k += 256)
         if(h[k]) atomicAdd(&state[k], h[k]);
@@ -145,6 +155,7 @@ __global__ void __launch_bounds__(256) bucket_scatter_kernel(const uint32_t *__r
 {
     /* start[c] = buckets with a count above c (descending order), for c = 1..256; thread t owns c = t + 1 */
     __shared__ uint32_t start[kCountBins];
+    __shared__ uint32_t h[kCountBins];
     __shared__ uint32_t s_warp[8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t v = state[threadIdx.x + 1];
@@ -155,18 +166,29 @@ __global__ void __launch_bounds__(256) bucket_scatter_kernel(const uint32_t *__r
         if(lane + d < 32) incl += x;
     }
     if(lane == 0) s_warp[warp] = incl;
+    for(int k = threadIdx.x; k < kCountBins; k += 256) h[k] = 0u;
     __syncthreads();
     uint32_t above = incl - v;
     for(int w = warp + 1; w < 8; ++w) above += s_warp[w];
-    start[threadIdx.x + 1] = above;
     if(blockIdx.x == 0 && threadIdx.x == 0) state[2 * kCountBins] = s_warp[0] + s_warp[1] + s_warp[2] + s_warp[3] +
                                                                    s_warp[4] + s_warp[5] + s_warp[6] + s_warp[7];
-    __syncthreads();
-    const uint32_t n_buckets = bucket_offsets[n_tiles - 1];
-    for(uint32_t b = blockIdx.x * 256u + threadIdx.x; b < n_buckets; b += gridDim.x * 256u) {
+    /* this CTA's buckets per count (shared-memory atomics), then ONE global reservation per count */
+    uint32_t b0, b1;
+    bucket_chunk(bucket_offsets[n_tiles - 1], b0, b1);
+    for(uint32_t b = b0 + threadIdx.x; b < b1; b += 256u) {
         const uint32_t c = bucket_active[b];
-        if(c == 0u) continue;
-        order[start[c] + atomicAdd(&state[kCountBins + c], 1u)] = b;
+        if(c) atomicAdd(&h[c], 1u);
+    }
+    __syncthreads();
+    {
+        const int c = threadIdx.x + 1;
+        start[c] = h[c] ? above + atomicAdd(&state[kCountBins + c], h[c]) : 0u;
+        h[c] = 0u;
+    }
+    __syncthreads();
+    for(uint32_t b = b0 + threadIdx.x; b < b1; b += 256u) {
+        const uint32_t c = bucket_active[b];
+        if(c) order[start[c] + atomicAdd(&h[c], 1u)] = b;
     }
 }
 
@@ -262,13 +284,19 @@ __global__ void __launch_bounds__(kThreads, 2) blend_backward_kernel(
     /* the 8 lanes of a segment prefetch the inputs of 32 list positions (snapshot, composed colour +
      * last contributor, upstream gradient, and the pixel's rank in the tile) into shared memory, one
      * batch ahead, with cp.async */
+    /* each lane takes 4 consecutive list positions of a batch, whose ranks it reads as one 32-bit word
+     * of the order one batch ahead of their prefetch (so the gather never waits on that read) */
+    const uint32_t *order4 = reinterpret_cast<const uint32_t *>(order);
+    uint32_t ranks = seg_active ? order4[sub] : 0u;
     auto prefetch = [&](int batch) {
         PixIn *dst = stage[batch & 1];
+        const uint32_t mine = ranks;
+        if(seg_active && (batch + 1) * 32 < n_pix) ranks = order4[(batch + 1) * 8 + sub];
 #pragma unroll
         for(int q = 0; q < 4; ++q) {
-            const int pl = sub + 8 * q, j = batch * 32 + pl;
+            const int pl = sub * 4 + q, j = batch * 32 + pl;
             if(j < n_pix) {
-                const int p = order[j];
+                const int p = (int)((mine >> (8 * q)) & 255u);
                 const int qx = tx0 + (p & (GSX_TILE - 1)), qy = ty0 + (p >> 4);
                 const size_t idx = (size_t)qy * (size_t)width + (size_t)qx;
                 cp_async16(&dst[pl].snap, bsnap + p);
