@@ -484,13 +484,19 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         }
     }
     const uint32_t *vals = in_b ? vals_b : vals_a;
+    /* Largest-tiles-first order for the blend when the grid is only a few waves (about 740 CTAs of
+     * 256 threads are resident at once on 148 SMs): there the last wave's long tiles decide the time.
+     * With many waves the raster order wins, as neighbouring tiles share instance records in L2. */
+    int sms = 148;
+    (void)cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+    const bool lpt = n_tiles <= sms * 5 * 8;
     {
     StageTimer st4(ctx, 4, stream);
     GSX_CUDA_TRY(gsx_launch_blend_forward(cam.width, cam.height, row_begin, cam.grid_w, n_tiles, (const uint2 *)ctx->ranges.ptr,
                                           (const uint32_t *)ctx->bucket_offsets.ptr, vals, (const PrimRec *)ctx->rec.ptr, bg,
                                           out_rgb, out_bf16, (float4 *)ctx->pix.ptr, (uint32_t *)ctx->tile_max.ptr,
                                           (float4 *)ctx->snap.ptr, (uint32_t *)ctx->bucket_tile.ptr,
-                                          forward_type == GSX_B200_FORWARD_TRAIN, class_tiles, words + 4,
+                                          forward_type == GSX_B200_FORWARD_TRAIN, lpt ? class_tiles : nullptr, words + 4,
                                           (uint8_t *)ctx->tile_order.ptr, (uint16_t *)ctx->bucket_active.ptr, stream),
                  "blend launch");
     ctx->launches += n_tiles > 0 ? 1 : 0;

@@ -118,7 +118,7 @@ __device__ __forceinline__ float rect_min_power(float mx, float my, float hcx, f
 }
 
 template <bool kTrain, bool kBF16>
-__global__ void __launch_bounds__(kThreads, 5) blend_forward_kernel(
+__global__ void __launch_bounds__(kThreads, kTrain ? 5 : 1) blend_forward_kernel(
     int width, int height, int row0, int grid_w, const uint2 *__restrict__ ranges, const uint32_t *__restrict__ bucket_offsets,
     const uint32_t *__restrict__ vals, const PrimRec *__restrict__ rec, float3 bg, void *__restrict__ out_rgb,
     float4 *__restrict__ pix, uint32_t *__restrict__ tile_max, float4 *__restrict__ snap, uint32_t *__restrict__ bucket_tile,
