@@ -539,8 +539,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
-                    help="multi-GPU gradient exchange: fused NVLink reduce+Adam+gather kernel, or NCCL all-reduce + Adam")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nvls", "peer", "nccl"],
+                    help="multi-GPU gradient exchange: fused reduce+Adam+gather kernel (NVSwitch multicast from 4 "
+                         "ranks up, else peer loads/stores; nvls / peer force one), or NCCL all-reduce + Adam")
     ap.add_argument("--profile-case", action="store_true",
                     help="scaled-down one-GPU workload for ncu captures (see profile_case); prints stage times only")
     ap.add_argument("--profile-forward", action="store_true", help="with --profile-case: config-2 forward renders")
@@ -648,11 +649,14 @@ def main():
         kt = torch.tensor([kms], device=dev)
         dist.all_reduce(kt, op=dist.ReduceOp.MAX)
         nb = trainer.sharded.nvlink_bytes()
-        exchange = {"kernel": "gsx_b200_dp_reduce_adam_gather", "avg_ms_max_over_ranks": float(kt.item()),
+        exchange = {"kernel": ("gsx_b200_dp_nvls_reduce_adam_broadcast" if trainer.sharded.nvls
+                               else "gsx_b200_dp_reduce_adam_gather"), "avg_ms_max_over_ranks": float(kt.item()),
                     "nvlink_bytes_per_rank": nb, "achieved_gbs_per_rank": nb / (float(kt.item()) / 1000.0) / 1e9,
                     "peer_copy_gbs_reference": 770.0,
-                    "note": "bytes = the shard's gradients read from the other ranks + the updated shard written "
-                            "to them; the NVLink reference is the measured 770 GB/s per direction peer copy"}
+                    "note": "bytes per direction per rank: peer form = the shard's gradients read from the other "
+                            "ranks + the updated shard written to them; NVSwitch form = all gradients to the switch + "
+                            "the shard out, the reduced shard + all updated shards in; the NVLink reference is the "
+                            "measured 770 GB/s per direction peer copy"}
     loss_ms = sum(a.elapsed_time(b) for a, b in le) / args.steps
     adam_ms = sum(a.elapsed_time(b) for a, b in ae) / args.steps
     trainer.ctx.check()
@@ -690,6 +694,9 @@ def main():
     e2e_value = world * args.steps / (float(t2.item()) / 1000.0)
     h2d = targets[0].numel() * 4
     trainer.ctx.check()
+    # multi-GPU correctness on the hardware: the fused exchange against the NCCL reference from the same
+    # state, and bit-identical replicas (after the timed regions)
+    exchange_parity = trainer.check_exchange(cams[view(0)], targets[view(0)]) if trainer.sharded is not None else None
     trainer.close()
 
     fwd = forward_inference(args, dev, rank, world, local)
@@ -747,8 +754,10 @@ def main():
                                    "one view per GPU per step, L1(0.8)+SSIM(0.2), per-role Adam",
                        "gaussians": n, "width": W, "height": H, "views_per_step": world,
                        "parallelism": (f"dp{world} (views), " + (
-                           "fused NVLink gradient average + sharded Adam + parameter all-gather (one kernel per rank)"
-                           if trainer.exchange == "fused" else "NCCL all-reduce AVG of 14 f32/Gaussian + Adam on every rank")
+                           ("fused gradient average + sharded Adam + parameter all-gather in one kernel per rank, "
+                            + ("NVSwitch multimem reduce-load + multicast store" if trainer.exchange == "fused-nvls"
+                               else "NVLink peer loads + stores"))
+                           if trainer.exchange.startswith("fused") else "NCCL all-reduce AVG of 14 f32/Gaussian + Adam on every rank")
                            if world > 1 else "dp1 (views)"),
                        "l2": "inputs larger than L2 (params+grads+moments = 672 MB)",
                        "visible": V, "instances": I, "buckets": B},
@@ -764,6 +773,7 @@ def main():
             "image_fit": fit1,
             "microbench": micro,
             "exchange": exchange,
+            "exchange_parity": exchange_parity,
             "cpu_baseline": cpu_baseline,
             "clocks": clk,
         }

@@ -1,5 +1,9 @@
 """Data-parallel training over NVLink with the fused gradient exchange + sharded Adam.
 
+Two forms of the exchange kernel: peer loads and stores over CUDA IPC mappings (below), and NVLink
+SHARP through the NVSwitch (MulticastBuffers: the switch sums the gradients and replicates the updated
+parameters; fewer bytes per rank from 4 ranks up).
+
 One process per GPU.  The flat parameter and gradient buffers of every rank are mapped into every
 other rank's process (CUDA IPC over the NVSwitch fabric); each rank owns one contiguous shard of the
 flat parameter space and runs gsx_b200_dp_reduce_adam_gather on it: peer loads of the shard's
@@ -157,6 +161,66 @@ def open_peer_buffers(numel: int, group, device, count: int = 2, api=None):
     return None, (str(err) if err is not None else "failed on another rank")
 
 
+class MulticastBuffers:
+    """One flat f32 buffer of `numel` elements per rank in symmetric memory, with an NVSwitch multicast
+    address bound to all ranks' buffers (`mc_ptr`): a multimem store there writes every rank's copy, a
+    multimem reduce-load returns the sum over the ranks.  Built by open_multicast_buffers."""
+
+    def __init__(self, world: int, rank: int, local, handle):
+        self.world, self.rank = world, rank
+        self.local, self.handle = local, handle
+        self.mc_ptr = int(handle.multicast_ptr)
+
+    def close_peers(self):
+        pass
+
+    def free(self):
+        self.local, self.handle = None, None
+
+
+def multicast_supported(device) -> bool:
+    """This process's GPU can bind memory to NVSwitch multicast objects."""
+    import torch
+    try:
+        from torch.distributed._symmetric_memory import DeviceType
+        return bool(torch._C._distributed_c10d._SymmetricMemory.has_multicast_support(
+            DeviceType.CUDA, torch.device(device).index or 0))
+    except Exception:  # noqa: BLE001 - no symmetric memory in this build: not supported
+        return False
+
+
+def open_multicast_buffers(numel: int, group, device, count: int = 2):
+    """`count` MulticastBuffers of `numel` f32 each, or (None, reason) on EVERY rank when any rank
+    cannot: multicast support, the allocations and the multicast addresses are agreed on collectively,
+    so all ranks take the same exchange."""
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    if not _agree(multicast_supported(device), group):
+        return None, "NVSwitch multicast is not supported on every rank"
+    tensors, err = [], None
+    try:
+        for _ in range(count):
+            tensors.append(symm_mem.empty(numel, dtype=torch.float32, device=device))
+    except Exception as e:  # noqa: BLE001 - agreed on below
+        err = e
+    if not _agree(err is None, group):
+        return None, str(err) if err is not None else "symmetric allocation failed on another rank"
+    bufs = []
+    for t in tensors:
+        h = symm_mem.rendezvous(t, group)
+        t.zero_()
+        bufs.append(MulticastBuffers(world, rank, t, h))
+    if not _agree(all(b.mc_ptr != 0 for b in bufs), group):
+        for b in bufs:
+            b.free()
+        return None, "no multicast address on every rank"
+    torch.cuda.synchronize(device)
+    dist.barrier(group=group)
+    return tuple(bufs), None
+
+
 class Segment(ctypes.Structure):
     _fields_ = [("begin", ctypes.c_uint64), ("end", ctypes.c_uint64), ("learning_rate", ctypes.c_float),
                 ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("epsilon", ctypes.c_float),
@@ -168,10 +232,13 @@ class ShardedAdam:
     """Adam over this rank's shard, fused with the gradient average and the parameter all-gather.
     `field_ranges` maps each role to its [begin, end) in the flat buffers; `lr` maps role -> rate."""
 
-    def __init__(self, params: PeerBuffers, grads: PeerBuffers, field_ranges: dict, lr: dict, group, device,
-                 beta1=0.9, beta2=0.999, epsilon=1e-8):
+    def __init__(self, params, grads, field_ranges: dict, lr: dict, group, device, beta1=0.9, beta2=0.999,
+                 epsilon=1e-8):
+        """params / grads: PeerBuffers (peer loads and stores, gsx_b200_dp_reduce_adam_gather) or
+        MulticastBuffers (NVSwitch reduce-load and multicast store, gsx_b200_dp_nvls_reduce_adam_broadcast)."""
         import torch
         self.params, self.grads, self.group = params, grads, group
+        self.nvls = isinstance(params, MulticastBuffers)
         self.world, self.rank = params.world, params.rank
         numel = params.local.numel()
         self.begin, self.end = shard_bounds(numel, self.world, self.rank)
@@ -184,9 +251,10 @@ class ShardedAdam:
         self.steps = 0
         self.token = torch.zeros(1, dtype=torch.float32, device=device)
         self.kernel_events = None  # optional list receiving (start, end) CUDA events around each launch
-        P = ctypes.c_void_p * self.world
-        self._params = P(*self.params.ptrs)
-        self._grads = P(*self.grads.ptrs)
+        if not self.nvls:
+            P = ctypes.c_void_p * self.world
+            self._params = P(*self.params.ptrs)
+            self._grads = P(*self.grads.ptrs)
 
     def _barrier(self):
         import torch.distributed as dist
@@ -211,16 +279,27 @@ class ShardedAdam:
             import torch
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-        check(lib().gsx_b200_dp_reduce_adam_gather(self.world, self.rank, self._params, self._grads,
-                                                   ctypes.c_void_p(self.m1.data_ptr()),
-                                                   ctypes.c_void_p(self.m2.data_ptr()), self.begin, self.end, segs,
-                                                   len(self.runs), _stream_handle(stream)))
+        if self.nvls:
+            check(lib().gsx_b200_dp_nvls_reduce_adam_broadcast(
+                self.world, ctypes.c_void_p(self.params.mc_ptr), ctypes.c_void_p(self.grads.mc_ptr),
+                ctypes.c_void_p(self.params.local.data_ptr()), ctypes.c_void_p(self.m1.data_ptr()),
+                ctypes.c_void_p(self.m2.data_ptr()), self.begin, self.end, segs, len(self.runs), _stream_handle(stream)))
+        else:
+            check(lib().gsx_b200_dp_reduce_adam_gather(self.world, self.rank, self._params, self._grads,
+                                                       ctypes.c_void_p(self.m1.data_ptr()),
+                                                       ctypes.c_void_p(self.m2.data_ptr()), self.begin, self.end, segs,
+                                                       len(self.runs), _stream_handle(stream)))
         if ev is not None:
             ev[1].record()
             self.kernel_events.append(ev)
         self._barrier()
 
     def nvlink_bytes(self) -> int:
-        """Bytes this rank moves over NVLink per step: its shard's gradients read from the other ranks
-        and its updated shard written to them."""
-        return 2 * (self.world - 1) * (self.end - self.begin) * 4
+        """Bytes this rank moves over NVLink per step and direction.  Peer form: its shard's gradients read
+        from the other ranks and its updated shard written to them, 2 (world - 1) shards.  Multicast form:
+        out, all its gradients to the switch plus its updated shard; in, the reduced shard plus every
+        rank's updated shard: 1 + 1/world of the flat buffer."""
+        shard = (self.end - self.begin) * 4
+        if self.nvls:
+            return shard * self.world + shard
+        return 2 * (self.world - 1) * shard

@@ -64,7 +64,9 @@ class Trainer:
     def __init__(self, model: GaussianModel, width: int, height: int, lr: dict | None = None, l1_weight=0.8,
                  ssim_weight=0.2, background=(0.0, 0.0, 0.0), group=None, device="cuda:0", exchange="fused"):
         """exchange (with a group): "fused" = gsx_b200.dp.ShardedAdam (gradient average + sharded Adam +
-        parameter all-gather in one NVLink kernel per rank); "nccl" = all-reduce AVG then Adam everywhere."""
+        parameter all-gather in one NVLink kernel per rank), through the NVSwitch (multimem reduce-load and
+        multicast store) from 4 ranks up where every GPU supports it, else over peer loads and stores;
+        "nvls" / "peer" force one form; "nccl" = all-reduce AVG then Adam everywhere."""
         self.model = model
         self.renderer = Renderer(width, height)
         self.ctx = RenderContext(torch.device(device).index or 0)
@@ -78,31 +80,47 @@ class Trainer:
         lr = dict(DEFAULT_LR, **(lr or {}))
         self.sharded = None
         self.exchange = "nccl" if group is not None else None
-        if group is not None and exchange == "fused":
-            self._setup_fused(model, group, device, lr)
+        if group is not None and exchange in ("fused", "nvls", "peer"):
+            self._setup_fused(model, group, device, lr, exchange)
         if self.sharded is None:
             self.optim = Adam([ParamGroup(f, model.params[f], model.grads[f], lr[f]) for f in model.fields])
 
-    def _setup_fused(self, model, group, device, lr):
-        """Peer-map the flat buffers and build the sharded optimizer.  open_peer_buffers agrees on the
-        outcome across ranks (every rank runs the same collectives even when one fails locally), so if
-        any rank failed (e.g. no peer access between two GPUs) all ranks keep the NCCL exchange."""
-        from .dp import ShardedAdam, open_peer_buffers
-        peer, err = open_peer_buffers(model.numel, group, device, count=2)
-        if peer is None:
-            import warnings
+    def _setup_fused(self, model, group, device, lr, exchange):
+        """Map the flat buffers into every rank (NVSwitch multicast or CUDA IPC) and build the sharded
+        optimizer.  The opening functions agree on the outcome across ranks (every rank runs the same
+        collectives even when one fails locally), so all ranks fall back together: multicast -> peer
+        mappings -> NCCL."""
+        import warnings
+
+        import torch.distributed as dist
+        from .dp import ShardedAdam, open_multicast_buffers, open_peer_buffers
+        bufs, err, form = None, None, None
+        if exchange == "nvls" or (exchange == "fused" and dist.get_world_size(group) >= 4):
+            bufs, err = open_multicast_buffers(model.numel, group, device, count=2)
+            form = "nvls"
+            if bufs is None:
+                warnings.warn(f"NVSwitch multicast exchange unavailable ({err}); trying peer mappings")
+        if bufs is None:
+            bufs, err = open_peer_buffers(model.numel, group, device, count=2)
+            form = "peer"
+        if bufs is None:
             warnings.warn(f"fused NVLink exchange unavailable ({err}); using NCCL")
             return
-        self._peer = peer
-        model.rebind(peer[0].local, peer[1].local)
-        self.sharded = ShardedAdam(peer[0], peer[1], model.field_ranges, lr, group, device)
+        self._peer = bufs
+        model.rebind(bufs[0].local, bufs[1].local)
+        self.sharded = ShardedAdam(bufs[0], bufs[1], model.field_ranges, lr, group, device)
         self.optim = None
-        self.exchange = "fused"
+        self.exchange = "fused-" + form
 
     def step(self, camera: Camera, target, events=None):
         """One training iteration on `camera` against `target` ([3,H,W] on the device).
         Returns the device scalar holding the summed loss map of this view.  `events`, if given, is
         ((loss_start, loss_end), (adam_start, adam_end)) CUDA events recorded around those launches."""
+        self.gradients(camera, target, events)
+        return self.update(events)
+
+    def gradients(self, camera: Camera, target, events=None):
+        """Render TRAIN, fused L1+SSIM, render backward: this rank's gradients in model.flat_grad."""
         m = self.model
         self.renderer.render(self.ctx, m.params, camera, self.out, background=self.background,
                              sh_degree=m.sh_degree, forward_type=FORWARD_TRAIN)
@@ -114,6 +132,10 @@ class Trainer:
         if events:
             events[0][1].record()
         self.renderer.backward(self.ctx, self.grad_rgb, m.grads)
+
+    def update(self, events=None):
+        """The gradient exchange (with a group) and Adam; returns the loss-sum device scalar."""
+        m = self.model
         if self.sharded is not None:
             if events:
                 events[1][0].record()
@@ -129,6 +151,68 @@ class Trainer:
         if events:
             events[1][1].record()
         return self.loss_sum
+
+    def check_exchange(self, camera: Camera, target) -> dict:
+        """Validate the sharded exchange on the hardware: from the current state, one step through the
+        fused exchange, and the same step through the reference exchange (NCCL all-reduce AVG of the
+        gradients, then the single-GPU Adam kernel over every parameter with the full moments gathered
+        from the shards).  Returns the largest absolute and relative difference of the updated parameters
+        (fused vs reference, max over ranks) and whether every rank holds bit-identical parameters.
+        Leaves the model in the fused step's state."""
+        import torch
+        import torch.distributed as dist
+
+        from . import Adam, ParamGroup
+        from .dp import ALIGN, shard_bounds
+        if self.sharded is None or self.group is None:
+            raise RuntimeError("check_exchange needs the fused exchange on a process group")
+        m, sh, grp = self.model, self.sharded, self.group
+        world = dist.get_world_size(grp)
+        self.gradients(camera, target)
+        p0, g0 = m.flat_param.clone(), m.flat_grad.clone()
+        # full moments from the shards (padded to the largest shard for one all-gather each)
+        width = max(e - b for b, e in (shard_bounds(m.numel, world, r) for r in range(world)))
+        width = max(width, ALIGN)
+        full = []
+        for mom in (sh.m1, sh.m2):
+            pad = torch.zeros(width, dtype=torch.float32, device=mom.device)
+            pad[: sh.end - sh.begin].copy_(mom[: sh.end - sh.begin])
+            every = torch.empty(world * width, dtype=torch.float32, device=mom.device)
+            dist.all_gather_into_tensor(every, pad, group=grp)
+            f = torch.zeros(m.numel, dtype=torch.float32, device=mom.device)
+            for r in range(world):
+                b, e = shard_bounds(m.numel, world, r)
+                f[b:e].copy_(every[r * width: r * width + (e - b)])
+            full.append(f)
+        steps = sh.steps
+        self.update()  # the fused exchange
+        torch.cuda.synchronize()
+        p_fused = m.flat_param.clone()
+        # the reference exchange from the same state
+        g_avg = g0.clone()
+        allreduce_mean(g_avg, grp)
+        p_ref = p0.clone()
+        groups = [ParamGroup(f, p_ref[a:b], g_avg[a:b], sh.lr[f]) for f, (a, b) in m.field_ranges.items()]
+        opt = Adam(groups)
+        for i, (f, (a, b)) in enumerate(m.field_ranges.items()):
+            opt.m1[i].copy_(full[0][a:b])
+            opt.m2[i].copy_(full[1][a:b])
+            opt.steps[i] = steps
+        opt.step(force_all=True)
+        torch.cuda.synchronize()
+        diff = (p_fused - p_ref).abs()
+        moved = (p_ref - p0).abs()
+        stats = torch.tensor([float(diff.max()), float((diff / moved.clamp_min(1e-30))[moved > 0].max()) if bool((moved > 0).any()) else 0.0],
+                             dtype=torch.float64, device=p0.device)
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX, group=grp)
+        # bit-identical replicas: a position-weighted hash of the parameter bits, compared over ranks
+        bits = p_fused.view(torch.int32).to(torch.int64)
+        h = int((bits * (torch.arange(bits.numel(), device=bits.device, dtype=torch.int64) % 1021 + 1)).sum())
+        hashes = [None] * world
+        dist.all_gather_object(hashes, h, group=grp)
+        return {"reference": "NCCL all-reduce AVG + single-GPU Adam over every parameter (moments gathered)",
+                "max_abs_diff": float(stats[0]), "max_rel_diff_of_update": float(stats[1]),
+                "replicas_identical": all(x == hashes[0] for x in hashes)}
 
     def close(self):
         """Release the peer mappings: every rank unmaps, a barrier, then every rank frees its own."""

@@ -347,6 +347,20 @@ GSX_B200_API int gsx_b200_dp_reduce_adam_gather(int world, int rank, float *cons
                                                 float *first_moment, float *second_moment, uint64_t shard_begin,
                                                 uint64_t shard_end, const gsx_b200_dp_segment *segments, int n_segments,
                                                 void *stream);
+/*
+ * The same step over NVLink SHARP (NVSwitch multicast, no counterpart in the reference).  mc_grads and
+ * mc_params are multicast addresses bound to every rank's flat gradient / parameter buffer; params is
+ * this rank's own parameter buffer.  The shard's gradients are summed inside the switch
+ * (multimem.ld_reduce), averaged, run through Adam with the shard-local moments, and the result is
+ * written to every rank's parameter buffer with one multicast store: per rank and direction only
+ * 1/world of the bytes cross NVLink.  The switch's summation order may differ from rank order (the
+ * average agrees with the peer-load form to rounding); replicas stay identical.  Same ordering contract
+ * as gsx_b200_dp_reduce_adam_gather: no waits inside, collectives around it on the host.
+ */
+GSX_B200_API int gsx_b200_dp_nvls_reduce_adam_broadcast(int world, float *mc_params, const float *mc_grads,
+                                                        const float *params, float *first_moment, float *second_moment,
+                                                        uint64_t shard_begin, uint64_t shard_end,
+                                                        const gsx_b200_dp_segment *segments, int n_segments, void *stream);
 /* Device buffers that other processes can map: cudaMalloc / cudaFree, the 64-byte CUDA IPC handle of a
  * buffer from gsx_b200_device_alloc, and mapping / unmapping another process's buffer by its handle. */
 GSX_B200_API int gsx_b200_device_alloc(uint64_t bytes, void **out);

@@ -1,7 +1,9 @@
-"""The fused data-parallel exchange on two real GPUs (one process per GPU, NCCL for the two ordering
-collectives, CUDA IPC peer mappings): after a few training steps the replicas are bit-identical and
-agree with the NCCL all-reduce + Adam path to float rounding.  Skipped on a box with fewer than two
-GPUs (the single-GPU emulation in test_gpu_dp.py covers the arithmetic)."""
+"""The fused data-parallel exchange on real GPUs (one process per GPU, NCCL for the two ordering
+collectives), in both forms: CUDA IPC peer mappings, and NVSwitch multicast (multimem reduce-load and
+multicast store).  After a few training steps the replicas are bit-identical and agree with the NCCL
+all-reduce + Adam path to float rounding; Trainer.check_exchange compares one step of each form with
+the NCCL reference from the same state.  Skipped on a box with fewer than two GPUs (the single-GPU
+emulation in test_gpu_dp.py covers the peer form's arithmetic)."""
 import datetime
 import os
 import socket
@@ -49,8 +51,10 @@ def _worker(rank, world, port, exchange, q):
             tr.step(cam, target)
         torch.cuda.synchronize()
         out = model.flat_param.cpu().numpy().copy()
+        chk = tr.check_exchange(cam, target) if tr.sharded is not None else None
+        form = tr.exchange
         tr.close()
-        q.put((rank, out))
+        q.put((rank, (out, chk, form)))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -70,13 +74,22 @@ def _run(exchange, world=2):
     return [res[r] for r in range(world)]
 
 
-def test_fused_exchange_two_gpus():
+@pytest.mark.parametrize("exchange", ["peer", "nvls"])
+def test_fused_exchange_two_gpus(exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    fused = _run("fused")
-    np.testing.assert_array_equal(fused[0], fused[1])
+    res = _run(exchange)
+    (p0, chk0, form), (p1, chk1, _) = res
+    if exchange == "nvls" and form != "fused-nvls":
+        pytest.skip(f"NVSwitch multicast not available here (exchange fell back to {form})")
+    assert form == "fused-" + exchange
+    np.testing.assert_array_equal(p0, p1)
+    # the same step through the NCCL reference: replicas identical, updates equal to rounding
+    for chk in (chk0, chk1):
+        assert chk["replicas_identical"]
+        assert chk["max_rel_diff_of_update"] <= 1e-3, chk
     nccl = _run("nccl")
-    np.testing.assert_array_equal(nccl[0], nccl[1])
+    np.testing.assert_array_equal(nccl[0][0], nccl[1][0])
     # separate runs: the backward's atomic order differs, Adam amplifies it (two NCCL runs differ as much)
-    np.testing.assert_allclose(fused[0], nccl[0], rtol=2e-3, atol=1e-4)
-    assert np.abs(fused[0]).sum() > 0
+    np.testing.assert_allclose(p0, nccl[0][0], rtol=2e-3, atol=1e-4)
+    assert np.abs(p0).sum() > 0
