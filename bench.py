@@ -199,10 +199,11 @@ def forward_inference(args, dev, rank, world, local):
 
 def large_frame(args, dev, rank, world, local):
     """Config 4: 10M Gaussians, 3840x2160 frames from 16 orbit cameras, split by tile rows over the
-    ranks: rank r renders band r (gb.band_rows) of EVERY frame, INFERENCE, bf16 output (f32
-    accumulation).  No exchange: each rank owns its rows of the output.  L2 flushed before every
-    band; per-band CUDA events around the render call.  Frames/s of the job = 16 / (max over ranks
-    of the summed band times)."""
+    ranks: for every frame each rank computes the same per-tile-row work estimate
+    (RenderContext.row_costs: one pass over the Gaussians, integer sums) and renders its band of the
+    equal-work cut (gb.balanced_band_rows), INFERENCE, bf16 output (f32 accumulation).  No exchange:
+    each rank owns its rows of the output.  L2 flushed before every frame; per-frame CUDA events around
+    the cost pass and the band render.  Frames/s of the job = 16 / (max over ranks of the summed times)."""
     import torch
     import torch.distributed as dist
 
@@ -212,26 +213,33 @@ def large_frame(args, dev, rank, world, local):
     g = {k: torch.from_numpy(v).to(dev) for k, v in scenes.config4_scene(0).items()}
     cams = scenes.config4_cameras()
     c0 = cams[0]
-    r0, r1 = gb.band_rows(c0.height, rank, world)
     ctx = gb.RenderContext(local)
     rend = gb.Renderer(c0.width, c0.height)
-    out = torch.empty((3, max(r1 - r0, 1), c0.width), dtype=torch.bfloat16, device=dev)
+    flat = torch.empty(3 * c0.height * c0.width, dtype=torch.bfloat16, device=dev)
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
-    evs, inst = [], 0
-    if r1 > r0:
-        for c in cams[:3]:
+
+    def frame(c):
+        r0, r1 = gb.balanced_band_rows(ctx.row_costs(g, c), c.height, rank, world) if world > 1 else (0, c.height)
+        if r1 > r0:
+            out = flat[: 3 * (r1 - r0) * c.width].view(3, r1 - r0, c.width)
             rend.render_rows(ctx, g, c, r0, r1, out, forward_type=gb.FORWARD_INFERENCE)
-        for c in cams:
-            flush.fill_(1.0)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            rend.render_rows(ctx, g, c, r0, r1, out, forward_type=gb.FORWARD_INFERENCE)
-            e1.record(stream)
-            evs.append((e0, e1))
-            inst += ctx.stats()["n_instances"]
-        torch.cuda.synchronize()
-        ctx.check()
+        return r0, r1
+
+    for c in cams[:3]:
+        frame(c)
+    evs, inst, rows = [], 0, []
+    for c in cams:
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        r0, r1 = frame(c)
+        e1.record(stream)
+        evs.append((e0, e1))
+        rows.append(r1 - r0)
+        inst += ctx.stats()["n_instances"] if r1 > r0 else 0
+    torch.cuda.synchronize()
+    ctx.check()
     ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -241,10 +249,10 @@ def large_frame(args, dev, rank, world, local):
     del g
     torch.cuda.empty_cache()
     return {"workload": "config 4: 10M Gaussians (config-3 generator, 2:1 volume:slab), 3840x2160, fx=fy=2200, "
-                        "16 orbit cameras, INFERENCE, bf16 RGB, split by tile rows over ranks",
+                        "16 orbit cameras, INFERENCE, bf16 RGB, split by tile rows over ranks into equal-work bands",
             "frames_per_s": len(cams) / (ms_max / 1000.0), "ms_per_frame": ms_max / len(cams),
-            "rows_rank0": [r0, r1], "instances_per_band_rank0": inst // max(len(evs), 1),
-            "l2": "flushed (256 MB write) before every band"}
+            "rows_rank0_mean": sum(rows) / len(rows), "instances_per_band_rank0": inst // max(len(evs), 1),
+            "l2": "flushed (256 MB write) before every frame"}
 
 
 def image_fit(dev):

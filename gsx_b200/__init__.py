@@ -124,6 +124,18 @@ class RenderContext:
         check(lib().gsx_b200_context_train_refreshes(self.handle, ctypes.byref(c)))
         return int(c.value)
 
+    def row_costs(self, gaussians: dict, camera: "Camera", stream=None):
+        """Per tile row of the full frame, the integer work estimate of gsx_b200_render_row_costs
+        (numpy uint32 array of ceil(height / 16) entries; waits for the stream)."""
+        import numpy as np
+        rows = (camera.height + 15) // 16
+        out = np.zeros(rows, np.uint32)
+        g = _c_gaussians(gaussians)
+        cam = camera.c_struct()
+        check(lib().gsx_b200_render_row_costs(self.handle, ctypes.byref(g), ctypes.byref(cam),
+                                              out.ctypes.data_as(ctypes.c_void_p), rows, _stream_handle(stream)))
+        return out
+
     def launch_count(self) -> int:
         """Kernels this context has launched since it was created (host-side count)."""
         c = ctypes.c_uint64()
@@ -186,6 +198,33 @@ def band_rows(height: int, rank: int, world_size: int):
     base, extra = divmod(tiles, world_size)
     t0 = rank * base + min(rank, extra)
     t1 = t0 + base + (1 if rank < extra else 0)
+    return min(16 * t0, height), min(16 * t1, height)
+
+
+def balanced_band_rows(row_costs, height: int, rank: int, world_size: int):
+    """Rows [begin, end) of rank `rank`'s band when the frame's tile rows are cut where the running sum
+    of `row_costs` (one work estimate per tile row, RenderContext.row_costs) crosses k/world_size of the
+    total, so the bands carry about equal work; whole tile rows, in order, covering [0, height).  Every
+    rank that passes the same costs gets the same cut (integer arithmetic)."""
+    if height <= 0 or world_size <= 0 or not 0 <= rank < world_size:
+        raise GsxError(INVALID_ARGUMENT, "balanced_band_rows: height, world_size positive and 0 <= rank < world_size")
+    tiles = (height + 15) // 16
+    costs = [int(c) for c in row_costs]
+    if len(costs) != tiles:
+        raise GsxError(INVALID_ARGUMENT, "one cost per tile row")
+    total = sum(costs)
+    if total == 0:
+        return band_rows(height, rank, world_size)
+    cuts, run, k = [0], 0, 1
+    for t, c in enumerate(costs):
+        run += c
+        while k < world_size and run * world_size >= k * total:
+            cuts.append(t + 1)
+            k += 1
+    while len(cuts) < world_size:
+        cuts.append(tiles)
+    cuts.append(tiles)
+    t0, t1 = cuts[rank], cuts[rank + 1]
     return min(16 * t0, height), min(16 * t1, height)
 
 

@@ -96,6 +96,7 @@ SIGNATURES = {
     "gsx_b200_context_check": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "gsx_b200_context_launch_count": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
     "gsx_b200_context_set_train_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "gsx_b200_render_row_costs": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]),
     "gsx_b200_context_train_refreshes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
     "gsx_b200_context_set_profiling": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "gsx_b200_context_read_profile": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_float),

@@ -144,6 +144,7 @@ struct gsx_b200_context {
     /* TRAIN: per tile the pixel order by last contributor, per bucket the pixels its backward walks,
      * and the backward's bucket order and its counting-sort state */
     DevBuf tile_order, bucket_active, bucket_order, bucket_sort;
+    DevBuf row_cost; /* per tile row work estimate (gsx_b200_render_row_costs) */
     /* small device words: [0] sticky flags, [1] the emission's overflow bit; from the tile scan: [2] instance total, [3] largest tile,
      * [4..8] tiles per per-tile-sort size class */
     DevBuf words;
@@ -258,7 +259,7 @@ int gsx_b200_context_destroy(gsx_b200_context *ctx)
                       &ctx->sort_scratch, &ctx->ranges, &ctx->bucket_offsets, &ctx->tile_max, &ctx->pix,
                       &ctx->bucket_tile, &ctx->snap, &ctx->tile_count, &ctx->class_tiles, &ctx->tile_aux, &ctx->words, &ctx->hist,
                       &ctx->fingerprint, &ctx->refresh_rgb, &ctx->tile_order, &ctx->bucket_active, &ctx->bucket_order,
-                      &ctx->bucket_sort };
+                      &ctx->bucket_sort, &ctx->row_cost };
     for(DevBuf *b : all) release(*b);
     if(ctx->ev_created)
         for(int s = 0; s < GSX_B200_STAGE_COUNT; ++s)
@@ -574,6 +575,30 @@ int gsx_b200_render_forward_rows(gsx_b200_context *ctx, const gsx_b200_gaussians
     if(camera == nullptr) return fail(GSX_B200_INVALID_ARGUMENT, "camera must be non-null");
     return render_forward_impl(ctx, g, sh_degree, camera, row_begin, row_end, background, forward_type, out_rgb,
                                out_bf16 != 0, stream);
+}
+
+int gsx_b200_render_row_costs(gsx_b200_context *ctx, const gsx_b200_gaussians *g, const gsx_b200_camera *camera,
+                              uint32_t *host_row_costs, int32_t n_rows, void *stream_)
+{
+    if(ctx == nullptr || g == nullptr || camera == nullptr || host_row_costs == nullptr)
+        return fail(GSX_B200_INVALID_ARGUMENT, "ctx, gaussians, camera and host_row_costs must be non-null");
+    if(camera->width <= 0 || camera->height <= 0) return fail(GSX_B200_INVALID_ARGUMENT, "camera size must be positive");
+    const CameraParams cam = make_camera(*camera, 0, camera->height);
+    if(n_rows != cam.grid_h) return fail(GSX_B200_INVALID_ARGUMENT, "n_rows must be the frame's tile rows, ceil(height / 16)");
+    if(cam.grid_h > 1024) return fail(GSX_B200_OUT_OF_RANGE, "at most 1024 tile rows");
+    if(g->count > 0 && (g->mean3d == nullptr || g->logscale == nullptr))
+        return fail(GSX_B200_INVALID_ARGUMENT, "mean3d and logscale must be non-null");
+    GSX_CUDA_TRY(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t stream = (cudaStream_t)stream_;
+    if(int rc = ensure(ctx->row_cost, sizeof(uint32_t) * 1024)) return rc;
+    GSX_CUDA_TRY(gsx_launch_band_cost(g->mean3d, g->logscale, g->count, cam, (uint32_t *)ctx->row_cost.ptr, stream),
+                 "row cost launch");
+    ctx->launches += g->count > 0 ? 1 : 0;
+    GSX_CUDA_TRY(cudaMemcpyAsync(host_row_costs, ctx->row_cost.ptr, sizeof(uint32_t) * (size_t)n_rows,
+                                 cudaMemcpyDeviceToHost, stream),
+                 "D2H");
+    GSX_CUDA_TRY(cudaStreamSynchronize(stream), "sync");
+    return 0;
 }
 
 int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const gsx_b200_gaussian_grads *gr,

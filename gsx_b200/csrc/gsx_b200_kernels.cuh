@@ -140,6 +140,9 @@ cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, co
                                   const float *sh3, int sh_degree, int64_t n, const CameraParams &cam, PrimRec *rec,
                                   uint32_t *counts, uint32_t *tile_masks, uint32_t *block_sums, float *visible_counter,
                                   float *max_screen_radius, cudaStream_t stream);
+/* per tile row of the (full-frame) camera, an integer estimate of the instances it holds */
+cudaError_t gsx_launch_band_cost(const float *mean3d, const float *logscale, int64_t n, const CameraParams &cam,
+                                 uint32_t *row_cost, cudaStream_t stream);
 cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *counts, const uint32_t *tile_masks,
                             const uint32_t *block_offsets,
                             uint32_t *offsets, int grid_w, int trow0, int n_tiles, unsigned long long *keys, uint32_t *vals,

@@ -19,6 +19,7 @@
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kCoopLanes = 6; /* up to this many small-rectangle lanes, the warp emits them together */
 
 __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec *__restrict__ rec,
                                                         const uint32_t *__restrict__ counts,
@@ -32,9 +33,16 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
 {
     __shared__ uint32_t s_warp[kThreads / 32];
     __shared__ uint32_t s_hist[8][256];
+    const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+    if(n_digits == 0 && block_offsets[blockIdx.x + 1] == block_offsets[blockIdx.x]) {
+        /* no instance in this block (every Gaussian culled: most blocks of a band): offsets only */
+        const uint32_t start = block_offsets[blockIdx.x];
+        if(i < n) offsets[i] = start;
+        if(i == n - 1) offsets[n] = start;
+        return;
+    }
     for(int j = threadIdx.x; j < n_digits * 256; j += kThreads) (&s_hist[0][0])[j] = 0u;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
     uint32_t cnt = i < n ? counts[i] : 0u;
     /* exclusive position = block offset + in-block exclusive scan of the counts */
     uint32_t incl = cnt;
@@ -77,22 +85,53 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
         }
     }
     uint32_t wpos = start;
-    if(tmax > 0 && tmax <= 32u) {
-        /* the preprocess already ran the exact overlap test for rectangles of up to 32 tiles */
-        unsigned m = tile_masks[i];
-        while(m) {
-            const unsigned k = (unsigned)__ffs(m) - 1u;
-            m &= m - 1u;
-            const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
-            const unsigned t = ty * grid_w + tx;
-            const unsigned long long key = ((unsigned long long)t << 32) | dbits;
-            keys[wpos] = key;
-            vals[wpos] = (uint32_t)i;
-            if(tile_count) atomicAdd(&tile_count[GSX_SUBCOUNTER(t, wpos & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u);
-            ++wpos;
-            for(int p = 0; p < n_digits; ++p) atomicAdd(&s_hist[p][(uint32_t)(key >> (8 * p)) & 0xffu], 1u);
+    const unsigned lt_mask = (1u << lane) - 1u;
+    /* rectangles of up to 32 tiles: the preprocess already ran the exact overlap test and left the
+     * overlap mask.  A warp with few such lanes (a band of a large frame: most Gaussians culled) emits
+     * one Gaussian at a time, lane k taking tile k of its rectangle, instead of walking tiles lane by
+     * lane with the rest of the warp idle */
+    {
+        const unsigned m_own = tmax > 0 && tmax <= 32u ? tile_masks[i] : 0u;
+        unsigned small = __ballot_sync(0xffffffffu, tmax > 0 && tmax <= 32u);
+        if(__popc(small) > kCoopLanes) {
+            /* many such lanes: each lane walks its own mask (fewer instructions than the broadcasts) */
+            unsigned m = m_own;
+            while(m) {
+                const unsigned k = (unsigned)__ffs(m) - 1u;
+                m &= m - 1u;
+                const unsigned tx = bx0 + k % bw, ty = by0 + k / bw;
+                const unsigned t = ty * grid_w + tx;
+                const unsigned long long key = ((unsigned long long)t << 32) | dbits;
+                keys[wpos] = key;
+                vals[wpos] = (uint32_t)i;
+                if(tile_count) atomicAdd(&tile_count[GSX_SUBCOUNTER(t, wpos & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u);
+                ++wpos;
+                for(int q = 0; q < n_digits; ++q) atomicAdd(&s_hist[q][(uint32_t)(key >> (8 * q)) & 0xffu], 1u);
+            }
+            small = 0u;
         }
-        tmax = 0; /* done: neither the sequential nor the cooperative pass below runs */
+        while(small) {
+            const int L = __ffs(small) - 1;
+            small &= small - 1u;
+            const unsigned m = __shfl_sync(0xffffffffu, m_own, L);
+            const unsigned lbx0 = __shfl_sync(0xffffffffu, bx0, L), lbw = __shfl_sync(0xffffffffu, bw, L);
+            const unsigned lby0 = __shfl_sync(0xffffffffu, by0, L);
+            const unsigned long long ldb = __shfl_sync(0xffffffffu, dbits, L);
+            const uint32_t lpos = __shfl_sync(0xffffffffu, wpos, L);
+            const uint32_t lidx = (uint32_t)__shfl_sync(0xffffffffu, (long long)i, L);
+            if((m >> lane) & 1u) {
+                const unsigned k = (unsigned)lane;
+                const unsigned tx = lbx0 + k % lbw, ty = lby0 + k / lbw;
+                const unsigned t = ty * grid_w + tx;
+                const uint32_t p = lpos + (uint32_t)__popc(m & lt_mask);
+                const unsigned long long key = ((unsigned long long)t << 32) | ldb;
+                keys[p] = key;
+                vals[p] = lidx;
+                if(tile_count) atomicAdd(&tile_count[GSX_SUBCOUNTER(t, p & (GSX_TILE_SUBCOUNTERS - 1), n_tiles)], 1u);
+                for(int q = 0; q < n_digits; ++q) atomicAdd(&s_hist[q][(uint32_t)(key >> (8 * q)) & 0xffu], 1u);
+            }
+        }
+        if(tmax <= 32u) tmax = 0; /* done: neither the sequential nor the cooperative pass below runs */
     }
     const unsigned nseq = tmax < GSX_SEQ_TILES ? tmax : GSX_SEQ_TILES;
     for(unsigned k = 0; k < nseq; ++k) {
@@ -108,7 +147,6 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
         }
     }
     unsigned coop = __ballot_sync(0xffffffffu, tmax > GSX_SEQ_TILES);
-    const unsigned lt_mask = (1u << lane) - 1u;
     while(coop) {
         const int L = __ffs(coop) - 1;
         coop &= coop - 1u;

@@ -85,6 +85,14 @@ __device__ __forceinline__ void sh_color(const float *__restrict__ sh0, const fl
  * dependent chain, so the CTA's duration is the number of rounds, not the number of live lanes. */
 constexpr int kGroup = 8;
 constexpr int kRows = kThreads * kGroup;
+static_assert((kRows * 3) % (4 * kThreads) == 0, "16-byte staging chunks split evenly over the threads");
+
+/* 16-byte global -> shared copy; bytes < 16 reads that many and zero-fills the rest */
+__device__ __forceinline__ void cp_async16_zfill(void *smem, const void *gmem, unsigned bytes)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(bytes) : "memory");
+}
 
 struct PrepSmem {
     float m[kRows * 3];
@@ -109,12 +117,27 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     const int lane = threadIdx.x & 31;
     const int64_t base = (int64_t)blockIdx.x * kRows;
     {
-        /* coalesced staging of the CTA's [kRows,3] mean and log-scale rows */
+        /* staging of the CTA's [kRows,3] mean and log-scale rows: 16-byte asynchronous copies, all in
+         * flight at once (a load-then-store loop waits out one memory latency per iteration); the
+         * copy past the end of the arrays is zero-filled.  Unaligned arrays take the plain loop. */
         const int64_t avail = (n - base) * 3;
-        for(int j = threadIdx.x; j < kRows * 3; j += kThreads) {
-            const bool ok = j < avail;
-            s_m[j] = ok ? mean3d[base * 3 + j] : 0.0f;
-            s_s[j] = ok ? logscale[base * 3 + j] : 0.0f;
+        const float *gm = mean3d + base * 3, *gs = logscale + base * 3;
+        if(((reinterpret_cast<uintptr_t>(mean3d) | reinterpret_cast<uintptr_t>(logscale)) & 15u) == 0) {
+#pragma unroll
+            for(int q = 0; q < kRows * 3 / 4 / kThreads; ++q) {
+                const int c = q * kThreads + (int)threadIdx.x; /* 16-byte chunk */
+                const int64_t left = avail - 4 * (int64_t)c;
+                const unsigned bytes = left >= 4 ? 16u : left > 0 ? (unsigned)left * 4u : 0u;
+                cp_async16_zfill(s_m + 4 * c, bytes ? gm + 4 * c : mean3d, bytes);
+                cp_async16_zfill(s_s + 4 * c, bytes ? gs + 4 * c : logscale, bytes);
+            }
+            asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+        } else {
+            for(int j = threadIdx.x; j < kRows * 3; j += kThreads) {
+                const bool ok = j < avail;
+                s_m[j] = ok ? mean3d[base * 3 + j] : 0.0f;
+                s_s[j] = ok ? logscale[base * 3 + j] : 0.0f;
+            }
         }
         if(threadIdx.x < kGroup) S.bsum[threadIdx.x] = 0u;
         if(threadIdx.x == 0) S.nsurv = 0;
@@ -359,6 +382,62 @@ __global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t *__restrict__
 }
 
 } // namespace
+
+namespace {
+
+/* Per tile row of the full frame, an estimate of the instances it will hold: every Gaussian that the
+ * preprocess's conservative screen cull keeps adds the number of tile columns of its cull rectangle to
+ * each tile row the rectangle covers (integer atomics, so every rank that computes it gets the same
+ * array).  The frame split of large-frame inference cuts the rows where the running sum crosses
+ * k/world of the total, so the bands carry about equal work. */
+constexpr int kCostRows = 1024;
+
+__global__ void __launch_bounds__(kThreads) band_cost_kernel(const float *__restrict__ mean3d,
+                                                             const float *__restrict__ logscale, int64_t n,
+                                                             CameraParams cam, uint32_t *__restrict__ row_cost)
+{
+    __shared__ uint32_t s_cost[kCostRows];
+    const int rows = cam.grid_h;
+    for(int r = threadIdx.x; r < rows; r += kThreads) s_cost[r] = 0u;
+    __syncthreads();
+    const float *w = cam.w2c;
+    for(int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
+        const float mx = mean3d[i * 3 + 0], my = mean3d[i * 3 + 1], mz = mean3d[i * 3 + 2];
+        const float d = w[8] * mx + w[9] * my + w[10] * mz + w[11];
+        if(d < cam.near_plane || d > cam.far_plane) continue;
+        const float inv = __frcp_rn(d);
+        const float cxp = (w[0] * mx + w[1] * my + w[2] * mz + w[3]) * inv * cam.fx + cam.cx;
+        const float cyp = (w[4] * mx + w[5] * my + w[6] * mz + w[7]) * inv * cam.fy + cam.cy;
+        const float ls = fmaxf(fmaxf(logscale[i * 3 + 0], logscale[i * 3 + 1]), logscale[i * 3 + 2]);
+        const float var = __expf(2.0f * ls) * 1.01f;
+        const float j1 = cam.fx * inv, j2 = cam.fy * inv;
+        const float rx = 3.34f * sqrtf(j1 * j1 * cam.cull_jx * var + 0.31f) + 2.0f;
+        const float ry = 3.34f * sqrtf(j2 * j2 * cam.cull_jy * var + 0.31f) + 2.0f;
+        const int x0 = max(0, (int)floorf((cxp - rx) * (1.0f / GSX_TILE)));
+        const int x1 = min(cam.grid_w - 1, (int)floorf((cxp + rx) * (1.0f / GSX_TILE)));
+        const int y0 = max(0, (int)floorf((cyp - ry) * (1.0f / GSX_TILE)));
+        const int y1 = min(rows - 1, (int)floorf((cyp + ry) * (1.0f / GSX_TILE)));
+        if(x1 < x0 || y1 < y0) continue;
+        for(int r = y0; r <= y1; ++r) atomicAdd(&s_cost[r], (uint32_t)(x1 - x0 + 1));
+    }
+    __syncthreads();
+    for(int r = threadIdx.x; r < rows; r += kThreads)
+        if(s_cost[r]) atomicAdd(&row_cost[r], s_cost[r]);
+}
+
+} // namespace
+
+cudaError_t gsx_launch_band_cost(const float *mean3d, const float *logscale, int64_t n, const CameraParams &cam,
+                                 uint32_t *row_cost, cudaStream_t stream)
+{
+    if(cam.grid_h > kCostRows) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(row_cost, 0, sizeof(uint32_t) * (size_t)cam.grid_h, stream);
+    if(e != cudaSuccess || n == 0) return e;
+    int64_t blocks = (n + kThreads - 1) / kThreads;
+    if(blocks > 148 * 8) blocks = 148 * 8;
+    band_cost_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(mean3d, logscale, n, cam, row_cost);
+    return cudaGetLastError();
+}
 
 cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, const float *logscale,
                                   const float *opacity, const float *sh0, const float *sh1, const float *sh2,

@@ -133,6 +133,18 @@ GSX_B200_API int gsx_b200_render_forward_rows(gsx_b200_context *ctx, const gsx_b
  * Gaussian (zero where culled); no prior zeroing needed.  Fails with GSX_B200_INVALID_STATE when
  * no TRAIN forward is retained (render.c:1434-1436).
  */
+/*
+ * Work estimate per tile row of the full frame, for splitting a large frame into bands of equal work
+ * (no reference counterpart; the frame split of large-frame inference): host_row_costs[r] (n_rows =
+ * ceil(height / 16) entries) receives, for every Gaussian the preprocess's conservative screen cull
+ * keeps, the number of tile columns of its cull rectangle, added to each tile row the rectangle covers.
+ * Integer sums: every rank computing it for the same inputs gets the same array, so every rank derives
+ * the same bands without exchanging anything.  Waits for the stream (the array is host memory).
+ */
+GSX_B200_API int gsx_b200_render_row_costs(gsx_b200_context *ctx, const gsx_b200_gaussians *gaussians,
+                                           const gsx_b200_camera *camera, uint32_t *host_row_costs, int32_t n_rows,
+                                           void *stream);
+
 GSX_B200_API int gsx_b200_render_backward(gsx_b200_context *ctx, const float *grad_rgb, const gsx_b200_gaussian_grads *grads,
                              void *stream);
 

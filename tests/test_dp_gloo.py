@@ -242,3 +242,25 @@ def test_peer_mapping_failure_on_one_rank_falls_back_on_every_rank(fail):
             assert all(None not in p for p in ptrs)
         else:
             assert not ok and err and live == 0 and opened == 0, (rank, err, live, opened)
+
+
+def test_balanced_bands_cover_the_frame_and_even_out_work():
+    """The equal-work cut of large-frame inference: whole tile rows, in order, covering [0, height),
+    the same on every rank, and no band above the ideal share by more than one tile row's cost."""
+    from gsx_b200 import balanced_band_rows
+    rng = np.random.default_rng(3)
+    height = 2160
+    tiles = (height + 15) // 16
+    costs = (rng.gamma(0.5, 1000.0, tiles) * (np.arange(tiles) > 40)).astype(np.uint32)  # empty sky, dense ground
+    for world in (1, 2, 3, 4, 8):
+        bands = [balanced_band_rows(costs, height, r, world) for r in range(world)]
+        pos = 0
+        for b0, b1 in bands:
+            assert b0 == pos and b1 >= b0 and b0 % 16 == 0
+            pos = b1
+        assert pos == height
+        share = [int(costs[b0 // 16:(b1 + 15) // 16].sum()) for b0, b1 in bands]
+        assert max(share) <= costs.sum() / world + costs.max()
+    # no work anywhere: the even split
+    from gsx_b200 import band_rows
+    assert balanced_band_rows(np.zeros(tiles, np.uint32), height, 2, 8) == band_rows(height, 2, 8)

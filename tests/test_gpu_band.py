@@ -122,3 +122,26 @@ def test_band_argument_checks(ctx):
         out = torch.empty((3, max(r1 - r0, 1), cam.width), device="cuda:0")
         with pytest.raises(gb.GsxError):
             r.render_rows(ctx, gd, cam, r0, r1, out)
+
+
+def test_row_costs_are_deterministic_and_cut_into_bands(ctx):
+    """gsx_b200_render_row_costs: integer per-tile-row work estimates, identical on repeated calls (every
+    rank of a frame split derives the same bands from them), zero for rows no Gaussian reaches; the
+    equal-work bands they give render bit-identically to the full frame's rows."""
+    g, cam = scenes.small_scene(13, 6000, 96, 200, 0, scale_mu=-2.5)
+    gd = to_dev(g)
+    a = ctx.row_costs(gd, cam)
+    b = ctx.row_costs(gd, cam)
+    assert a.shape == ((cam.height + 15) // 16,) and a.sum() > 0
+    np.testing.assert_array_equal(a, b)
+    full = render(ctx, gd, cam, 0, (0.0, 0.0, 0.0), train=False).cpu().numpy()
+    pos = 0
+    for r in range(3):
+        r0, r1 = gb.balanced_band_rows(a, cam.height, r, 3)
+        assert r0 == pos
+        pos = r1
+        if r1 > r0:
+            out = _band(ctx, gd, cam, r0, r1)
+            ctx.check()
+            np.testing.assert_array_equal(out.cpu().numpy(), full[:, r0:r1, :])
+    assert pos == cam.height
