@@ -369,6 +369,17 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
     uint32_t *class_tiles = (uint32_t *)ctx->class_tiles.ptr;
     uint64_t total = 0;
     uint32_t max_tile = 0;
+    auto clear_counters = [&]() -> int {
+        /* the emission's capacity-overflow bit lives in its own word (words[1]), cleared per pass: an
+         * overflow is expected on the pass before a capacity retry.  words[0] keeps the sticky flags
+         * (lookback timeouts) until gsx_b200_context_check reads them. */
+        GSX_CUDA_TRY(cudaMemsetAsync(words + 1, 0, sizeof(uint32_t), stream), "memset");
+        GSX_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * GSX_TILE_SUBCOUNTERS * (size_t)n_tiles, stream),
+                     "memset");
+        return 0;
+    };
+    bool counters_clear = false; /* cleared before the preprocess, so the kernels from the preprocess to
+                                  * the tile scan follow each other directly (programmatic dependent launch) */
     auto emit_into_capacity = [&](uint64_t cap) -> int {
         /* capacity in pairs; ensure() only reallocates when the request exceeds what is held, and
          * inst_cap is the exact floor of what is held, so a steady workload never reallocates */
@@ -378,12 +389,9 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         ctx->inst_cap = ctx->keys.bytes / (2 * sizeof(unsigned long long));
         const uint64_t vcap = ctx->vals.bytes / (2 * sizeof(uint32_t));
         if(vcap < ctx->inst_cap) ctx->inst_cap = vcap;
-        /* the emission's capacity-overflow bit lives in its own word (words[1]), cleared per pass: an
-         * overflow is expected on the pass before a capacity retry.  words[0] keeps the sticky flags
-         * (lookback timeouts) until gsx_b200_context_check reads them. */
-        GSX_CUDA_TRY(cudaMemsetAsync(words + 1, 0, sizeof(uint32_t), stream), "memset");
-        GSX_CUDA_TRY(cudaMemsetAsync(tile_count, 0, sizeof(uint32_t) * GSX_TILE_SUBCOUNTERS * (size_t)n_tiles, stream),
-                     "memset");
+        if(!counters_clear)
+            if(int rc = clear_counters()) return rc;
+        counters_clear = false;
         {
             StageTimer st(ctx, 1, stream);
             GSX_CUDA_TRY(gsx_launch_emit(n, (const PrimRec *)ctx->rec.ptr, counts, tile_masks, block_sums, offsets,
@@ -420,6 +428,8 @@ int render_forward_impl(gsx_b200_context *ctx, const gsx_b200_gaussians *g, int 
         return 0;
     };
     if(n > 0) {
+        if(int rc = clear_counters()) return rc;
+        counters_clear = true;
         {
             StageTimer st0(ctx, 0, stream);
             GSX_CUDA_TRY(gsx_launch_preprocess(g->mean3d, g->rotation, g->logscale, g->opacity, g->sh0, g->sh1, g->sh2,

@@ -22,6 +22,33 @@
 
 #include "gsx_detmath.h"
 
+#include <utility>
+
+/* Programmatic dependent launch (sm_90+): a kernel launched with gsx_launch_pdl may start while the
+ * kernel before it in the stream is finishing (its CTAs become resident as the previous kernel's last
+ * CTAs leave, and its launch overhead is hidden); it must call gsx_pdl_wait() before it touches anything
+ * the previous kernel reads or writes.  A kernel calls gsx_pdl_trigger() to let the next one launch
+ * early.  Both are no-ops for kernels launched without the attribute. */
+__device__ __forceinline__ void gsx_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void gsx_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t gsx_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 #define GSX_TILE 16
 #define GSX_TILE_PIXELS 256
 #define GSX_SEQ_TILES 8

@@ -31,6 +31,8 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(int64_t n, const PrimRec
                                                         uint32_t *__restrict__ hist, int n_digits,
                                                         uint32_t *__restrict__ tile_count)
 {
+    gsx_pdl_wait();
+    gsx_pdl_trigger();
     __shared__ uint32_t s_warp[kThreads / 32];
     __shared__ uint32_t s_hist[8][256];
     const int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x;
@@ -194,7 +196,7 @@ cudaError_t gsx_launch_emit(int64_t n, const PrimRec *rec, const uint32_t *count
 {
     if(n <= 0) return cudaSuccess;
     const int64_t blocks = (n + kThreads - 1) / kThreads;
-    emit_kernel<<<(unsigned)blocks, kThreads, 0, stream>>>(n, rec, counts, tile_masks, block_offsets, offsets, (unsigned)grid_w, (unsigned)trow0, (unsigned)n_tiles, keys,
-                                                            vals, capacity, flags, hist, n_digits, tile_count);
-    return cudaGetLastError();
+    return gsx_launch_pdl(emit_kernel, dim3((unsigned)blocks), dim3(kThreads), 0, stream, n, rec, counts, tile_masks,
+                          block_offsets, offsets, (unsigned)grid_w, (unsigned)trow0, (unsigned)n_tiles, keys, vals, capacity,
+                          flags, hist, n_digits, tile_count);
 }

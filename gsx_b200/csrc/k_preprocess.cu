@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     PrimRec *__restrict__ rec, uint32_t *__restrict__ counts, uint32_t *__restrict__ tile_masks,
     uint32_t *__restrict__ block_sums, int64_t n_blocks, float *__restrict__ vis_counter, float *__restrict__ max_radius)
 {
+    gsx_pdl_trigger(); /* the block-total scan may launch once every CTA has started */
     extern __shared__ __align__(16) unsigned char smem_raw[];
     PrepSmem &S = *reinterpret_cast<PrepSmem *>(smem_raw);
     float *const s_m = S.m;
@@ -353,6 +354,8 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
 /* exclusive scan of the per-CTA totals (one CTA); block_sums[nb] receives the grand total */
 __global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t *__restrict__ block_sums, int nb)
 {
+    gsx_pdl_wait();
+    gsx_pdl_trigger();
     __shared__ uint32_t s_w[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per = (nb + 1023) / 1024;
@@ -460,6 +463,7 @@ cudaError_t gsx_launch_preprocess(const float *mean3d, const float *rotation, co
     preprocess_kernel<<<(unsigned)ctas, kThreads, sizeof(PrepSmem), stream>>>(
         mean3d, rotation, logscale, opacity, sh0, sh1, sh2, sh3, (sh_degree + 1) * (sh_degree + 1), n, cam, rec, counts,
         tile_masks, block_sums, blocks, visible_counter, max_screen_radius);
-    block_scan_kernel<<<1, 1024, 0, stream>>>(block_sums, (int)blocks);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    if(e != cudaSuccess) return e;
+    return gsx_launch_pdl(block_scan_kernel, dim3(1), dim3(1024), 0, stream, block_sums, (int)blocks);
 }

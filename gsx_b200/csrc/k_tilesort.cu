@@ -70,6 +70,8 @@ __device__ __forceinline__ uint32_t tile_total(const uint32_t *__restrict__ sub,
 __global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_t *__restrict__ sub, int n_tiles,
                                                                    uint32_t *__restrict__ block_aux)
 {
+    gsx_pdl_wait();
+    gsx_pdl_trigger();
     __shared__ uint32_t s[kTileThreads / 32][kAux];
     const int t = blockIdx.x * kTileThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -102,6 +104,8 @@ __global__ void __launch_bounds__(kTileThreads) tile_reduce_kernel(const uint32_
 __global__ void __launch_bounds__(1024) block_scan_aux_kernel(uint32_t *__restrict__ block_aux, int n_blocks,
                                                               uint32_t *__restrict__ words_out)
 {
+    gsx_pdl_wait();
+    gsx_pdl_trigger();
     __shared__ uint32_t s_w[32][kAux];
     __shared__ uint32_t s_tot[kAux];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -160,6 +164,8 @@ __global__ void __launch_bounds__(kTileThreads) tile_write_kernel(uint32_t *__re
                                                                   uint2 *__restrict__ ranges, uint32_t *__restrict__ bucket_offsets,
                                                                   uint32_t *__restrict__ class_tiles)
 {
+    gsx_pdl_wait();
+    gsx_pdl_trigger();
     __shared__ uint32_t s[kTileThreads / 32][kAux - 1];
     const int t = blockIdx.x * kTileThreads + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -370,10 +376,14 @@ cudaError_t gsx_launch_tile_scan(uint32_t *tile_count, int n_tiles, uint2 *range
     if(n_tiles <= 0) return cudaSuccess;
     const int blocks = (n_tiles + kTileThreads - 1) / kTileThreads;
     if(blocks > 1024) return cudaErrorInvalidValue;
-    tile_reduce_kernel<<<blocks, kTileThreads, 0, stream>>>(tile_count, n_tiles, block_aux);
-    block_scan_aux_kernel<<<1, 1024, 0, stream>>>(block_aux, blocks, words_out);
-    tile_write_kernel<<<blocks, kTileThreads, 0, stream>>>(tile_count, n_tiles, block_aux, ranges, bucket_offsets, class_tiles);
-    return cudaGetLastError();
+    cudaError_t e = gsx_launch_pdl(tile_reduce_kernel, dim3(blocks), dim3(kTileThreads), 0, stream, tile_count, n_tiles,
+                                   block_aux);
+    if(e == cudaSuccess)
+        e = gsx_launch_pdl(block_scan_aux_kernel, dim3(1), dim3(1024), 0, stream, block_aux, blocks, words_out);
+    if(e == cudaSuccess)
+        e = gsx_launch_pdl(tile_write_kernel, dim3(blocks), dim3(kTileThreads), 0, stream, tile_count, n_tiles,
+                           (const uint32_t *)block_aux, ranges, bucket_offsets, class_tiles);
+    return e;
 }
 
 int gsx_tile_sort_classes() { return kClasses; }
