@@ -132,3 +132,34 @@ def test_public_api_training_step_matches_oracle_step():
         du, do = got - p0, p - p0
         assert rel_l2(du, do) <= 1e-3, k
         assert (np.abs(du - do) > lr).mean() <= 1e-3, k
+
+
+def test_public_api_training_step_at_config3():
+    """The drop-in at the benchmarked size: GSX's own training step (gsx-runtime.c:1413-1536 order: zero
+    grads, render TRAIN, L1 and SSIM forward and backward, render backward, Adam on every role) through the
+    public API on the provider, config 3 (3M Gaussians, 1245x825, teacher target).  Checks the loss map
+    against the fused direct path's on the same render, and prints the step's wall time (the driver syncs
+    the backend's stream at the end of each step) for the integration notes."""
+    _need()
+    import time
+    g = scenes.config3_scene(0)
+    cam = scenes.config3_cameras()[0]
+    oc = _ocam(cam)
+    ctx = gb.RenderContext(0)
+    target = render(ctx, to_dev(scenes.teacher(g)), cam, train=False)
+    ctx.check()
+    sess = po.RefSession("b200", g, oc, target.cpu().numpy())
+    sess.step()
+    P = 3 * cam.width * cam.height
+    lm_api = sess.download(9, P)
+    # the same step's loss map on the direct path (fused L1 + SSIM on the same render)
+    out = render(ctx, to_dev(g), cam, train=True)
+    lm = torch.zeros_like(out)
+    grad = torch.zeros_like(out)
+    gb.l1_ssim(out, target, lm, grad, 0.8, 0.2)
+    torch.cuda.synchronize()
+    assert np.abs(lm.cpu().numpy().ravel() - lm_api).max() <= 1e-4
+    secs = [sess.step() for _ in range(10)]
+    print(f"\nGSX public-API training step at config 3 on the provider: median {1e3 * sorted(secs)[5]:.3f} ms "
+          f"(min {1e3 * min(secs):.3f} ms) over 10 steps")
+    ctx.close()
