@@ -641,12 +641,28 @@ def main():
         trainer.sharded.kernel_events = []
     torch.cuda.synchronize()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ge = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     p0.record(stream)
     for s in range(args.steps):
         c = cams[view(args.warmup + s)]
-        trainer.step(c, targets[view(args.warmup + s)], events=(le[s], ae[s]))
+        ge[s][0].record(stream)
+        trainer.gradients(c, targets[view(args.warmup + s)], events=(le[s], ae[s]))
+        ge[s][1].record(stream)
+        trainer.update(events=(le[s], ae[s]))
     p1.record(stream)
     torch.cuda.synchronize()
+    # per-view balance: the render + loss + backward time of every rank's view in every step; a step of
+    # the data-parallel job waits for its slowest view
+    gms = torch.tensor([a.elapsed_time(b) for a, b in ge], device=dev, dtype=torch.float64)
+    if world > 1:
+        every = torch.empty(world * args.steps, device=dev, dtype=torch.float64)
+        dist.all_gather_into_tensor(every, gms)
+        gms = every.view(world, args.steps)
+    else:
+        gms = gms.view(1, args.steps)
+    view_balance = {"gradients_ms_mean": float(gms.mean()), "gradients_ms_slowest_rank_mean": float(gms.max(0).values.mean()),
+                    "note": "render TRAIN + L1/SSIM + backward of one view, profiled pass; the mean over ranks and "
+                            "steps, and the per-step slowest rank averaged over steps (what a step waits for)"}
     trainer.ctx.set_profiling(False)
     prof = trainer.ctx.read_profile()
     profiled_ms = p0.elapsed_time(p1) / args.steps
@@ -782,6 +798,7 @@ def main():
             "microbench": micro,
             "exchange": exchange,
             "exchange_parity": exchange_parity,
+            "view_balance": view_balance,
             "cpu_baseline": cpu_baseline,
             "clocks": clk,
         }
