@@ -351,37 +351,75 @@ __global__ void __launch_bounds__(kThreads) preprocess_kernel(
     (void)lane;
 }
 
-/* exclusive scan of the per-CTA totals (one CTA); block_sums[nb] receives the grand total */
+/* exclusive scan of the per-block totals (one CTA); block_sums[nb] receives the grand total.
+ * The totals are walked in chunks of 4096: every thread reads and writes 4 consecutive words (one
+ * coalesced 16-byte access per warp lane), and the next chunk's load is in flight while the current
+ * chunk is scanned.  (Giving each thread its own contiguous run of nb/1024 totals made every load of a
+ * warp touch 32 cache lines, one dependent round trip per element: 0.1 ms at 39k blocks.) */
+__device__ __forceinline__ uint4 load_chunk(const uint32_t *__restrict__ p, int idx, int nb)
+{
+    if(idx + 3 < nb) return *reinterpret_cast<const uint4 *>(p + idx);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if(idx < nb) v.x = p[idx];
+    if(idx + 1 < nb) v.y = p[idx + 1];
+    if(idx + 2 < nb) v.z = p[idx + 2];
+    return v;
+}
+
 __global__ void __launch_bounds__(1024) block_scan_kernel(uint32_t *__restrict__ block_sums, int nb)
 {
     gsx_pdl_wait();
     gsx_pdl_trigger();
-    __shared__ uint32_t s_w[32];
+    __shared__ uint32_t s_w[2][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int per = (nb + 1023) / 1024;
-    const int b0 = threadIdx.x * per;
-    uint32_t local = 0;
-    for(int b = b0; b < b0 + per && b < nb; ++b) local += block_sums[b];
-    uint32_t incl = local;
+    constexpr int kChunk = 4 * 1024;
+    const bool vec = (reinterpret_cast<uintptr_t>(block_sums) & 15u) == 0;
+    uint32_t carry = 0;
+    int idx = 4 * (int)threadIdx.x;
+    uint4 v = idx < nb ? (vec ? load_chunk(block_sums, idx, nb)
+                              : make_uint4(block_sums[idx], idx + 1 < nb ? block_sums[idx + 1] : 0u,
+                                           idx + 2 < nb ? block_sums[idx + 2] : 0u, idx + 3 < nb ? block_sums[idx + 3] : 0u))
+                       : make_uint4(0u, 0u, 0u, 0u);
+    for(int base = 0, it = 0; base < nb; base += kChunk, ++it) {
+        const uint4 cur = v;
+        const int nidx = idx + kChunk;
+        if(nidx < nb)
+            v = vec ? load_chunk(block_sums, nidx, nb)
+                    : make_uint4(block_sums[nidx], nidx + 1 < nb ? block_sums[nidx + 1] : 0u,
+                                 nidx + 2 < nb ? block_sums[nidx + 2] : 0u, nidx + 3 < nb ? block_sums[nidx + 3] : 0u);
+        else
+            v = make_uint4(0u, 0u, 0u, 0u); /* past the end: adds nothing to the next chunk's total */
+        const uint32_t local = cur.x + cur.y + cur.z + cur.w;
+        uint32_t incl = local;
 #pragma unroll
-    for(int d = 1; d < 32; d <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, d);
-        if(lane >= d) incl += t;
+        for(int d = 1; d < 32; d <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, d);
+            if(lane >= d) incl += t;
+        }
+        uint32_t *const w = s_w[it & 1]; /* alternating buffers: one barrier per chunk */
+        if(lane == 31) w[warp] = incl;
+        __syncthreads();
+        uint32_t woff = 0, tot = 0;
+#pragma unroll 8
+        for(int k = 0; k < 32; ++k) {
+            const uint32_t x = w[k];
+            woff += k < warp ? x : 0u;
+            tot += x;
+        }
+        const uint32_t e0 = carry + woff + incl - local;
+        const uint4 out = make_uint4(e0, e0 + cur.x, e0 + cur.x + cur.y, e0 + cur.x + cur.y + cur.z);
+        if(vec && idx + 3 < nb) {
+            *reinterpret_cast<uint4 *>(block_sums + idx) = out;
+        } else {
+            if(idx < nb) block_sums[idx] = out.x;
+            if(idx + 1 < nb) block_sums[idx + 1] = out.y;
+            if(idx + 2 < nb) block_sums[idx + 2] = out.z;
+            if(idx + 3 < nb) block_sums[idx + 3] = out.w;
+        }
+        carry += tot;
+        idx = nidx;
     }
-    if(lane == 31) s_w[warp] = incl;
-    __syncthreads();
-    uint32_t woff = 0, tot = 0;
-    for(int k = 0; k < 32; ++k) {
-        woff += k < warp ? s_w[k] : 0u;
-        tot += s_w[k];
-    }
-    uint32_t run = woff + incl - local;
-    for(int b = b0; b < b0 + per && b < nb; ++b) {
-        const uint32_t v = block_sums[b];
-        block_sums[b] = run;
-        run += v;
-    }
-    if(threadIdx.x == 0) block_sums[nb] = tot;
+    if(threadIdx.x == 0) block_sums[nb] = carry;
 }
 
 } // namespace

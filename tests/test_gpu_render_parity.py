@@ -206,3 +206,25 @@ def test_dense_tiles_order_and_gradients(ctx, n, size, z_levels):
     for k in gd:
         err = rel_l2(grads[k].cpu().numpy(), ref_b[k])
         assert err <= GRAD_TOL, f"{k}: rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("n", [1_100_003, 2_500_000])
+def test_instance_total_over_many_scan_chunks(ctx, n):
+    """More 256-Gaussian blocks than the block-total scan takes in one pass (4096 per chunk, a ragged
+    last chunk): the instance total read back to the host (the scan's last word) equals the last
+    per-Gaussian offset (the emission's in-block scans over the same totals) and the number of keys,
+    and the keys come out sorted."""
+    g, cam = scenes.small_scene(5, n, 640, 480, 0, scale_mu=-3.5)
+    gd = to_dev(g)
+    render(ctx, gd, cam, train=False)
+    ctx.check()
+    v = fetch_view(ctx, n)
+    off = v["offsets"].astype(np.int64)
+    assert off[0] == 0 and np.all(np.diff(off) >= 0)
+    assert int(ctx.stats()["n_instances"]) == int(off[-1]) == v["keys"].shape[0]
+    assert off[-1] > 0
+    assert np.all(v["keys"][1:] >= v["keys"][:-1])
+    # a second forward of the same scene gives the same total (the scan's last word is rewritten)
+    render(ctx, gd, cam, train=False)
+    ctx.check()
+    assert int(ctx.stats()["n_instances"]) == int(off[-1])
