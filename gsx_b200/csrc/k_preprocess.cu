@@ -82,8 +82,10 @@ __device__ __forceinline__ void sh_color(const float *__restrict__ sh0, const fl
  * screen cull over all of them and packs the survivors, then runs the full path in rounds of
  * kThreads survivors: off-screen Gaussians (42-52% in the benchmark views, 80-90% for a quarter-frame
  * band) cost the cull only, and the full path runs on dense warps.  Each warp's full path is a long
- * dependent chain, so the CTA's duration is the number of rounds, not the number of live lanes. */
-constexpr int kGroup = 8;
+ * dependent chain, so the CTA's duration is the number of rounds, not the number of live lanes.
+ * 1024 Gaussians per CTA (26 KB of staging) and 48 registers let 5 CTAs share an SM; 2048 per CTA
+ * (53 KB) held 4: config-3 preprocess 0.144 -> 0.137 ms. */
+constexpr int kGroup = 4;
 constexpr int kRows = kThreads * kGroup;
 static_assert((kRows * 3) % (4 * kThreads) == 0, "16-byte staging chunks split evenly over the threads");
 
@@ -103,7 +105,7 @@ struct PrepSmem {
     int nsurv;
 };
 
-__global__ void __launch_bounds__(kThreads) preprocess_kernel(
+__global__ void __launch_bounds__(kThreads, 5) preprocess_kernel(
     const float *__restrict__ mean3d, const float *__restrict__ rotation, const float *__restrict__ logscale,
     const float *__restrict__ opacity_raw, const float *__restrict__ sh0, const float *__restrict__ sh1,
     const float *__restrict__ sh2, const float *__restrict__ sh3, int bases, int64_t n, CameraParams cam,
