@@ -267,7 +267,13 @@ __global__ void __launch_bounds__(kThreads_) segsort_kernel(const uint2 *__restr
     for(int attempt = 0; attempt < 2; ++attempt) {
         /* element e of the current order sits at s_key[e]; thread (warp, lane) owns
          * e = warp * 32 * kItems + it * 32 + lane */
-        for(int e = threadIdx.x; e < n; e += kThreads_) s_key[e] = sort_keys[r.x + e];
+        /* asynchronous 8-byte copies, all of the thread's keys in flight together (a load-then-store
+         * loop waits out one memory round trip per item: 16 in a row for the largest class) */
+        for(int e = threadIdx.x; e < n; e += kThreads_) {
+            const unsigned dst = (unsigned)__cvta_generic_to_shared(s_key + e);
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(sort_keys + r.x + e) : "memory");
+        }
+        asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
         if(threadIdx.x == 0) s_misc[8] = 0u;
         __syncthreads();
         for(int shift = attempt == 0 ? 32 : 0; shift < 64; shift += 8) {
