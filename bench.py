@@ -41,7 +41,8 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region (200 ms period)."""
+    """Clocks and throttle reasons during the timed region: nvidia-smi at a 200 ms period, and NVML
+    (read-only queries) every 10 ms, so a timed region of a few tens of ms still gets several samples."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -51,8 +52,36 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.nvml = []  # (sm MHz, event-reason bitmask)
+        self.nvml_max = None
+        self._stop = threading.Event()
+        self._nvml_thread = None
+
+    def _poll_nvml(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+        except Exception:  # noqa: BLE001 - no NVML: the nvidia-smi samples stand alone
+            return
+        try:
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.nvml_max = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            while not self._stop.is_set():
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.nvml.append((float(sm), int(rs)))
+                self._stop.wait(0.01)
+        except Exception:  # noqa: BLE001 - a failed query ends the NVML sampling only
+            pass
+        finally:
+            try:
+                pynvml.nvmlShutdown()
+            except Exception:  # noqa: BLE001
+                pass
 
     def __enter__(self):
+        self._nvml_thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        self._nvml_thread.start()
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
@@ -68,6 +97,9 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        self._stop.set()
+        if self._nvml_thread is not None:
+            self._nvml_thread.join(timeout=2)
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -91,8 +123,24 @@ class ClockSampler:
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
+        n_smi = len(sm)
+        if mx is None:
+            mx = self.nvml_max
+        try:
+            import pynvml
+            bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+        except Exception:  # noqa: BLE001
+            bits = {}
+        for mhz, rs in self.nvml:
+            sm.append(mhz)
+            for nm, b in bits.items():
+                if rs & b:
+                    reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "samples_nvidia_smi": n_smi, "samples_nvml": len(self.nvml)}
 
 
 def _dist_init():
